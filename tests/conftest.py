@@ -1,0 +1,27 @@
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+GOLDEN = ROOT / "tests" / "golden"
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (sm_100a B200)")
+
+
+@pytest.fixture(scope="session")
+def golden():
+    with np.load(GOLDEN / "golden_small.npz") as z:
+        return {k: z[k] for k in z.files}
+
+
+@pytest.fixture(scope="session")
+def config1():
+    with np.load(GOLDEN / "config1.npz") as z:
+        return {k: z[k] for k in z.files}

@@ -1,0 +1,128 @@
+"""Pin the CPU oracle to the reference's own outputs (no GPU needed).
+
+Golden vectors come from running pico-kernels' functions
+(``tests/golden/make_golden.py``). Every check here is bit-exact.
+"""
+
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant_ref as o
+
+
+def _f32(arr: np.ndarray, dtype: str) -> np.ndarray:
+    if dtype == "bfloat16":
+        return o.bf16_bits_to_f32(arr)
+    return arr.astype(np.float32)
+
+
+def _group_keys(golden):
+    return sorted({k.split("/")[1] for k in golden if k.startswith("group/")})
+
+
+def test_kat_quantize_col(golden):
+    """tests/test_quantize.py:35-42 known answer, reproduced exactly."""
+    w = golden["kat_quantize_col/w"]
+    assert np.array_equal(o.quantize_col_fake(w, 4, 16), golden["kat_quantize_col/out"])
+    assert np.array_equal(o.quantize_col_fake(w, 4), golden["kat_quantize_col_nogroup/out"])
+    assert np.array_equal(o.quantize_col_fake(w, 3, 16), golden["kat_quantize_col_3bit/out"])
+
+
+def test_group_codes_scales_packed(golden):
+    names = _group_keys(golden)
+    assert len(names) >= 14
+    for name in names:
+        key = f"group/{name}"
+        dt = str(golden[f"{key}/dtype"])
+        g = int(golden[f"{key}/group"])
+        w = _f32(golden[f"{key}/w"], dt)
+        codes, scales = o.group_quant_codes(w, g)
+        assert np.array_equal(scales.view(np.uint32), golden[f"{key}/scales_f32"].view(np.uint32)), name
+        assert np.array_equal(codes, golden[f"{key}/codes"]), name
+        rep = np.repeat(scales, g, axis=0)[: w.shape[0]]
+        # by value: the reference's fake-quant keeps -0.0, int8 codes cannot
+        assert np.array_equal(codes.astype(np.float32) * rep, golden[f"{key}/fake"]), name
+        assert np.array_equal(o.store_scales(scales, "f16").astype(np.float16),
+                              golden[f"{key}/scales_f16"]), name
+        assert np.array_equal(o.f32_to_bf16_bits(scales), golden[f"{key}/scales_bf16"]), name
+        if f"{key}/packed" in golden:
+            assert np.array_equal(o.pack_int4_n(codes), golden[f"{key}/packed"]), name
+
+
+def test_group_fake_quant_matches_column_walk(golden):
+    """quantize_col on each column == codes * fp32 scale (quantize.py:63-68)."""
+    key = "group/rand_float32_K200_N32_g128"
+    w = golden[f"{key}/w"]
+    fake = np.stack([o.quantize_col_fake(w[:, n], 4, 128) for n in range(w.shape[1])], 1)
+    assert np.array_equal(fake, golden[f"{key}/fake"])
+
+
+def test_per_tensor_quantize_int4(golden):
+    keys = sorted({k.split("/")[1] for k in golden if k.startswith("pt/")})
+    assert len(keys) == 4
+    for name in keys:
+        key = f"pt/{name}"
+        dt = "bf16" if name.startswith("bfloat16") else "f16"
+        w = _f32(golden[f"{key}/w"], "bfloat16" if dt == "bf16" else "float16")
+        q, s = o.quantize_int4_per_tensor(w, dt)
+        assert s == float(golden[f"{key}/scale"]), name
+        assert np.array_equal(q, golden[f"{key}/codes"]), name
+        assert np.array_equal(o.pack_int4_n(q), golden[f"{key}/packed"]), name
+
+
+def test_pack_roundtrip(golden):
+    for case in ("roundtrip", "allnibbles"):
+        q = golden[f"pack/{case}/codes"]
+        p = o.pack_int4_n(q)
+        assert np.array_equal(p, golden[f"pack/{case}/packed"])
+        assert np.array_equal(o.unpack_int4_n(p), q)
+
+
+def test_fp8_quantize_and_gemm(golden):
+    for dt, odt in (("float16", "f16"), ("bfloat16", "bf16")):
+        key = f"fp8/{dt}"
+        a = _f32(golden[f"{key}/a"], dt)
+        b = _f32(golden[f"{key}/b"], dt)
+        a8, sa = o.fp8_quantize(a, odt)
+        b8, sb = o.fp8_quantize(b, odt)
+        assert sa == float(golden[f"{key}/sa"]) and sb == float(golden[f"{key}/sb"])
+        assert np.array_equal(a8, golden[f"{key}/a8"])
+        assert np.array_equal(b8, golden[f"{key}/b8"])
+        y = o.fp8_gemm_reference(a8, sa, b8, sb)
+        assert np.array_equal(y.view(np.uint32), golden[f"{key}/y"].view(np.uint32))
+
+
+def config1_inputs():
+    g0 = torch.Generator().manual_seed(0)
+    w = (torch.randn(1024, 1024, generator=g0) * 0.02).to(torch.float16)
+    g1 = torch.Generator().manual_seed(1)
+    a = torch.randn(16, 1024, generator=g1).to(torch.float16)
+    return w.numpy(), a.numpy()
+
+
+def test_config1_cpu_reference_run(config1):
+    """the whole CPU reference run (packed bytes, scales, Y)."""
+    w, a = config1_inputs()
+    assert hashlib.sha256(w.tobytes()).hexdigest() == str(config1["w_sha256"])
+    assert hashlib.sha256(a.tobytes()).hexdigest() == str(config1["a_sha256"])
+    codes, scales = o.group_quant_codes(w.astype(np.float32), 128)
+    s16 = scales.astype(np.float16)
+    assert np.array_equal(o.pack_int4_n(codes), config1["packed"])
+    assert np.array_equal(s16, config1["scales_f16"])
+    y = o.w4a16_reference(a.astype(np.float32), codes, s16.astype(np.float32), 128)
+    # fp32 matmul summation order differs between numpy BLAS and torch CPU
+    ref = config1["y"]
+    rel = np.linalg.norm(y - ref) / np.linalg.norm(ref)
+    assert rel < 1e-6 and np.abs(y - ref).max() < 1e-4
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_e4m3_encoder_matches_torch(seed):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(1 << 16, generator=g) * (10.0 ** (seed - 1))
+    x = x[x.abs() < 464]
+    ref = x.to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(o.f32_to_e4m3_bits(x.numpy()), ref)
