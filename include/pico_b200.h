@@ -1,0 +1,164 @@
+/*
+ * pico_b200.h -- C ABI of the B200 (sm_100a) quantized-matmul path.
+ *
+ * Drop-in boundary for pico-kernels' quantized-matmul functions. Every entry
+ * point takes plain device pointers, sizes and a cudaStream_t passed as
+ * `void*` (NULL = legacy default stream); no framework types cross the
+ * boundary. Every entry point is asynchronous on `stream` except where noted,
+ * returns a pk_status (0 = success), and on failure leaves a message for
+ * pk_last_error_string(). Shapes and layouts follow the reference:
+ *   - matrices are row-major with an explicit leading dimension in elements;
+ *   - packed int4 weights are uint8 [K, N/2], byte [k, j] holding column 2j
+ *     in its low nibble and column 2j+1 in its high nibble (gemm_int4.py:65-72);
+ *   - group scales are [ceil(K/group), N], groups running along K.
+ *
+ * Reference citations are paths within the pico-kernels project.
+ */
+#ifndef PICO_B200_H_
+#define PICO_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PK_API __attribute__((visibility("default")))
+#else
+#define PK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. The reference raises AssertionError on bad shapes
+ * (gemm_int4.py:78-81, gemm_splitk.py:71); the Python layer maps these codes
+ * to ValueError / TypeError / RuntimeError. */
+typedef enum {
+  PK_OK = 0,
+  PK_ERR_SHAPE = 1,        /* a size or leading dimension is invalid        */
+  PK_ERR_DTYPE = 2,        /* unsupported dtype combination                 */
+  PK_ERR_ALIGN = 3,        /* pointer or stride misaligned for 16-byte TMA  */
+  PK_ERR_CUDA = 4,         /* a CUDA runtime/driver call failed             */
+  PK_ERR_TIMEOUT = 5,      /* a device-side bounded wait expired            */
+  PK_ERR_WORKSPACE = 6,    /* workspace missing or too small                */
+  PK_ERR_UNSUPPORTED = 7   /* valid request this build does not implement   */
+} pk_status;
+
+/* Element types. */
+typedef enum {
+  PK_F16 = 0,
+  PK_BF16 = 1,
+  PK_F32 = 2,
+  PK_E4M3 = 3,
+  PK_U8 = 4,
+  PK_I8 = 5
+} pk_dtype;
+
+/* Library version (major*10000 + minor*100 + patch). */
+PK_API int pk_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+PK_API const char* pk_last_error_string(void);
+
+/* Device status word written by bounded device-side waits. Synchronises the
+ * current device. *code = first recorded pk_status (0 if none), *where = the
+ * site that recorded it; reset != 0 clears it. */
+PK_API int pk_device_status(int* code, int* where, int reset);
+
+/* ---------------------------------------------------------------------- */
+/* int4 quantization and packing                                           */
+/* ---------------------------------------------------------------------- */
+
+/* Per-group symmetric int4 quantize + pack of W[K, N] (dtype F16/BF16/F32),
+ * groups of `group_size` rows along K (the last group may be ragged).
+ *   scale = max|w[group, n]|.clamp_min(1e-12) / 7   (fp32, IEEE division)
+ *   q     = clamp(round_half_even(w / scale), -7, 7)
+ * Writes packed[K, N/2] (ld N/2) and scales[ceil(K/group), N] rounded to
+ * `scale_dtype` (F16/BF16/F32).
+ * Replaces quantize.quantize_col applied column-wise (quantize.py:42-68)
+ * followed by gemm_int4.pack_int4_n (gemm_int4.py:65-72). */
+PK_API int pk_quant_int4_group(const void* w, int w_dtype, int64_t K, int64_t N, int64_t ldw,
+                        int group_size, uint8_t* packed, void* scales, int scale_dtype,
+                        void* stream);
+
+/* max|x| over n elements (dtype F16/BF16/F32) into *absmax_dev (device fp32).
+ * The absmax half of gemm_int4.quantize_int4 (gemm_int4.py:60) and
+ * gemm_fp8.quantize (gemm_fp8.py:94). */
+PK_API int pk_absmax(const void* x, int dtype, int64_t n, float* absmax_dev, void* stream);
+
+/* Per-tensor int4 codes: q = clamp(round(dtype(w / scale)), -8, 7) as int8,
+ * the quotient computed in fp32 and rounded to w's dtype (F16/BF16/F32) before
+ * rounding to an integer. Replaces the elementwise half of
+ * gemm_int4.quantize_int4 (gemm_int4.py:61). */
+PK_API int pk_quant_int4_tensor(const void* w, int dtype, int64_t n, float scale, int8_t* codes,
+                         void* stream);
+
+/* Pack int8 codes q[K, N] into uint8 [K, N/2] (gemm_int4.py:65-72). */
+PK_API int pk_pack_int4_n(const int8_t* q, int64_t K, int64_t N, uint8_t* packed, void* stream);
+
+/* Unpack uint8 [K, N/2] into sign-extended int8 [K, N]; the inverse used by
+ * the reference's round-trip test (tests/test_gemm_int4.py:33-42). */
+PK_API int pk_unpack_int4_n(const uint8_t* packed, int64_t K, int64_t N, int8_t* q, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* W4A16 GEMM                                                              */
+/* ---------------------------------------------------------------------- */
+
+/* Bytes of workspace pk_w4a16_gemm needs for this shape with split_k (0 =
+ * the library's own choice). Zero when the chosen path needs none. */
+PK_API size_t pk_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int split_k);
+
+/* out[M, N] = A[M, K] @ dequant(Wp) where dequant(Wp)[k, n] =
+ *   q[k, n] * scales[k / group_size, n]   if scales != NULL, or
+ *   q[k, n] * scalar_scale                 if scales == NULL.
+ * A: F16 or BF16 (ld lda). Wp: uint8 [K, N/2] (ld N/2). scales dtype must
+ * equal A's dtype. out: F32 or BF16 (ld ldo). split_k: 0 = automatic,
+ * 1 = no split, > 1 = split the K reduction over that many CTAs (decode
+ * shapes), reduced deterministically in split order through `workspace`
+ * (pk_w4a16_workspace_size bytes, zero-filled once before its first use; the
+ * kernel leaves it ready for the next call). Calls sharing one workspace must
+ * not overlap on the GPU.
+ * Replaces gemm_int4.int4_gemm (gemm_int4.py:75-92); the reference's
+ * per-tensor float scale is scalar_scale, applied in the epilogue instead of
+ * a second pass over C (gemm_int4.py:92). */
+PK_API int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t* wp, const void* scales,
+                  float scalar_scale, int group_size, int64_t M, int64_t N, int64_t K, void* out,
+                  int out_dtype, int64_t ldo, int split_k, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* fp8 (e4m3) GEMM                                                         */
+/* ---------------------------------------------------------------------- */
+
+/* x8[i] = e4m3(dtype(x[i] * scale)), RNE (F16/BF16/F32 input). The cast half
+ * of gemm_fp8.quantize (gemm_fp8.py:95). */
+PK_API int pk_fp8_quantize(const void* x, int dtype, int64_t n, float scale, uint8_t* x8, void* stream);
+
+/* out[M, N] = (A8[M, K] @ B8[K, N]) * out_scale with e4m3 inputs, fp32
+ * accumulation and a single epilogue multiply; out F32 or BF16.
+ * A8 row-major (ld K), B8 row-major (ld N).
+ * Replaces gemm_fp8.fp8_gemm_precast (gemm_fp8.py:98-117), where
+ * out_scale = 1 / (a_scale * b_scale) (gemm_fp8.py:106). */
+PK_API int pk_fp8_gemm(const uint8_t* a8, const uint8_t* b8, int64_t M, int64_t N, int64_t K,
+                float out_scale, void* out, int out_dtype, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Dense split-K GEMM                                                      */
+/* ---------------------------------------------------------------------- */
+
+/* Bytes of workspace pk_gemm_splitk needs. */
+PK_API size_t pk_gemm_splitk_workspace_size(int64_t M, int64_t N, int64_t K, int split_k);
+
+/* out[M, N] fp32 = A[M, K] @ B[K, N] (both F16 or both BF16, row-major) with
+ * the K reduction split over split_k slices, partial sums reduced in slice
+ * order (deterministic) through `workspace`.
+ * Replaces gemm_splitk.triton_gemm_splitk (gemm_splitk.py:67-80), which
+ * reduces with fp32 atomics into a zeroed C (gemm_splitk.py:64,72). */
+PK_API int pk_gemm_splitk(const void* a, const void* b, int dtype, int64_t M, int64_t N, int64_t K,
+                   int split_k, float* out, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PICO_B200_H_ */

@@ -1,0 +1,306 @@
+// extern "C" entry points of libpico_b200.so (declared in include/pico_b200.h):
+// argument validation, path selection, tensor-map encoding, the device status
+// word and the per-thread error message.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "pk_internal.h"
+
+namespace pk {
+namespace {
+
+thread_local char g_msg[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(PK_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+void ok() { g_msg[0] = '\0'; }
+
+// First error code recorded by a device-side bounded wait, and where.
+__device__ int g_device_status[2];
+
+constexpr int kMaxDevices = 64;
+int* g_status_ptr[kMaxDevices] = {};
+int g_sms[kMaxDevices] = {};
+std::mutex g_mu;
+
+int current_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kMaxDevices) return -1;
+  return d;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+bool is16(int dt) { return dt == PK_F16 || dt == PK_BF16; }
+
+}  // namespace
+
+int* device_status_ptr() {
+  const int d = current_device();
+  if (d < 0) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_status_ptr[d] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
+    g_status_ptr[d] = static_cast<int*>(p);
+  }
+  return g_status_ptr[d];
+}
+
+int num_sms() {
+  const int d = current_device();
+  if (d < 0) return 148;
+  if (g_sms[d] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, d) != cudaSuccess || v <= 0)
+      v = 148;
+    g_sms[d] = v;
+  }
+  return g_sms[d];
+}
+
+bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                    uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                    uint32_t box_outer, CUtensorMapSwizzle swizzle, const char** why) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) {
+    *why = "cuTensorMapEncodeTiled unavailable";
+    return false;
+  }
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_stride_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *why = "cuTensorMapEncodeTiled rejected the operand (alignment or box)";
+    return false;
+  }
+  return true;
+}
+
+}  // namespace pk
+
+using namespace pk;
+
+extern "C" {
+
+int pk_version(void) { return 100; }
+
+const char* pk_last_error_string(void) { return g_msg; }
+
+int pk_device_status(int* code, int* where, int reset) {
+  int* p = device_status_ptr();
+  if (p == nullptr) return fail(PK_ERR_CUDA, "device status word unavailable");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  int h[2] = {0, 0};
+  e = cudaMemcpy(h, p, sizeof(h), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read device status");
+  if (code) *code = h[0];
+  if (where) *where = h[1];
+  if (reset) {
+    e = cudaMemset(p, 0, sizeof(h));
+    if (e != cudaSuccess) return cuda_fail(e, "reset device status");
+  }
+  ok();
+  return PK_OK;
+}
+
+int pk_quant_int4_group(const void* w, int w_dtype, int64_t K, int64_t N, int64_t ldw,
+                        int group_size, uint8_t* packed, void* scales, int scale_dtype,
+                        void* stream) {
+  if (!w || !packed || !scales) return fail(PK_ERR_SHAPE, "null pointer");
+  if (K <= 0 || N <= 0 || (N % 2) != 0)
+    return fail(PK_ERR_SHAPE, "need K > 0 and an even N > 0 (got K=%lld N=%lld)",
+                (long long)K, (long long)N);
+  if (ldw < N) return fail(PK_ERR_SHAPE, "ldw %lld < N %lld", (long long)ldw, (long long)N);
+  if (group_size <= 0) return fail(PK_ERR_SHAPE, "group_size must be positive");
+  if ((K + group_size - 1) / group_size > 65535)
+    return fail(PK_ERR_SHAPE, "too many groups along K");
+  if (w_dtype != PK_F16 && w_dtype != PK_BF16 && w_dtype != PK_F32)
+    return fail(PK_ERR_DTYPE, "weight dtype must be f16, bf16 or f32");
+  if (scale_dtype != PK_F16 && scale_dtype != PK_BF16 && scale_dtype != PK_F32)
+    return fail(PK_ERR_DTYPE, "scale dtype must be f16, bf16 or f32");
+  if ((reinterpret_cast<uintptr_t>(packed) & 3) != 0)
+    return fail(PK_ERR_ALIGN, "packed output must be 4-byte aligned");
+  cudaError_t e = launch_quant_int4_group(w, w_dtype, K, N, ldw, group_size, packed, scales,
+                                          scale_dtype, as_stream(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "quant_int4_group launch");
+  ok();
+  return PK_OK;
+}
+
+int pk_absmax(const void* x, int dtype, int64_t n, float* absmax_dev, void* stream) {
+  if (!x || !absmax_dev || n <= 0) return fail(PK_ERR_SHAPE, "need a non-empty input");
+  if (dtype != PK_F16 && dtype != PK_BF16 && dtype != PK_F32)
+    return fail(PK_ERR_DTYPE, "absmax dtype must be f16, bf16 or f32");
+  cudaError_t e = launch_absmax(x, dtype, n, absmax_dev, as_stream(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "absmax launch");
+  ok();
+  return PK_OK;
+}
+
+int pk_quant_int4_tensor(const void* w, int dtype, int64_t n, float scale, int8_t* codes,
+                         void* stream) {
+  if (!w || !codes || n <= 0) return fail(PK_ERR_SHAPE, "need a non-empty input");
+  if (!is16(dtype) && dtype != PK_F32)
+    return fail(PK_ERR_DTYPE, "quantize_int4 input must be f16, bf16 or f32");
+  cudaError_t e = launch_quant_int4_tensor(w, dtype, n, scale, codes, as_stream(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "quant_int4_tensor launch");
+  ok();
+  return PK_OK;
+}
+
+int pk_pack_int4_n(const int8_t* q, int64_t K, int64_t N, uint8_t* packed, void* stream) {
+  if (!q || !packed) return fail(PK_ERR_SHAPE, "null pointer");
+  if (K <= 0 || N <= 0 || (N % 2) != 0) return fail(PK_ERR_SHAPE, "N must be even");
+  cudaError_t e = launch_pack_int4(q, K, N, packed, as_stream(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "pack launch");
+  ok();
+  return PK_OK;
+}
+
+int pk_unpack_int4_n(const uint8_t* packed, int64_t K, int64_t N, int8_t* q, void* stream) {
+  if (!q || !packed) return fail(PK_ERR_SHAPE, "null pointer");
+  if (K <= 0 || N <= 0 || (N % 2) != 0) return fail(PK_ERR_SHAPE, "N must be even");
+  cudaError_t e = launch_unpack_int4(packed, K, N, q, as_stream(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "unpack launch");
+  ok();
+  return PK_OK;
+}
+
+size_t pk_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int split_k) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if (!decode_supported(M, N, K, 128, nullptr, 8, reinterpret_cast<const void*>(16)))
+    return 0;
+  const int split = split_k > 0 ? split_k : decode_pick_split(M, N, K);
+  return decode_workspace_bytes(M, N, K, split);
+}
+
+int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t* wp, const void* scales,
+                  float scalar_scale, int group_size, int64_t M, int64_t N, int64_t K, void* out,
+                  int out_dtype, int64_t ldo, int split_k, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  if (!a || !wp || !out) return fail(PK_ERR_SHAPE, "null pointer");
+  if (M <= 0 || N <= 0 || K <= 0 || (N % 2) != 0)
+    return fail(PK_ERR_SHAPE, "need M, K > 0 and an even N > 0 (got M=%lld N=%lld K=%lld)",
+                (long long)M, (long long)N, (long long)K);
+  if (lda < K || ldo < N) return fail(PK_ERR_SHAPE, "leading dimension too small");
+  if (!is16(a_dtype)) return fail(PK_ERR_DTYPE, "A must be f16 or bf16");
+  if (out_dtype != PK_F32 && out_dtype != PK_BF16)
+    return fail(PK_ERR_DTYPE, "output must be f32 or bf16");
+  if (scales != nullptr && group_size <= 0) return fail(PK_ERR_SHAPE, "group_size must be > 0");
+  if (split_k < 0) return fail(PK_ERR_SHAPE, "split_k must be >= 0");
+  cudaStream_t s = as_stream(stream);
+
+  if (decode_supported(M, N, K, group_size, scales, lda, a)) {
+    DecodeArgs p{};
+    p.a = a;
+    p.lda = lda;
+    p.wp = wp;
+    p.scales = scales;
+    p.scalar_scale = scales ? 1.0f : scalar_scale;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.out = out;
+    p.out_dtype = out_dtype;
+    p.ldo = ldo;
+    p.a_dtype = a_dtype;
+    int split = split_k > 0 ? split_k : decode_pick_split(M, N, K);
+    if (split > K / 128) split = static_cast<int>(K / 128);
+    p.split = split;
+    p.status = device_status_ptr();
+    if (split > 1) {
+      const size_t need = decode_workspace_bytes(M, N, K, split);
+      if (workspace == nullptr || workspace_bytes < need)
+        return fail(PK_ERR_WORKSPACE, "split-K needs %zu workspace bytes, got %zu", need,
+                    workspace_bytes);
+      if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+        return fail(PK_ERR_ALIGN, "workspace must be 256-byte aligned");
+      const int64_t tiles = N / 128;
+      const size_t sem_bytes = ((tiles * sizeof(unsigned) + 255) / 256) * 256;
+      p.sems = static_cast<unsigned*>(workspace);
+      p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + sem_bytes);
+    }
+    const char* why = "";
+    cudaError_t e = launch_w4a16_decode(p, s, &why);
+    if (e == cudaErrorInvalidValue && why[0] != '\0') return fail(PK_ERR_ALIGN, "%s", why);
+    if (e != cudaSuccess) return cuda_fail(e, "w4a16 decode launch");
+    ok();
+    return PK_OK;
+  }
+
+  cudaError_t e = launch_w4a16_simt(a, a_dtype, lda, wp, scales, scalar_scale, group_size, M, N,
+                                    K, out, out_dtype, ldo, s);
+  if (e != cudaSuccess) return cuda_fail(e, "w4a16 simt launch");
+  ok();
+  return PK_OK;
+}
+
+int pk_fp8_quantize(const void* x, int dtype, int64_t n, float scale, uint8_t* x8,
+                    void* stream) {
+  if (!x || !x8 || n <= 0) return fail(PK_ERR_SHAPE, "need a non-empty input");
+  if (dtype != PK_F16 && dtype != PK_BF16 && dtype != PK_F32)
+    return fail(PK_ERR_DTYPE, "fp8 quantize input must be f16, bf16 or f32");
+  cudaError_t e = launch_fp8_quantize(x, dtype, n, scale, x8, as_stream(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fp8 quantize launch");
+  ok();
+  return PK_OK;
+}
+
+int pk_fp8_gemm(const uint8_t* a8, const uint8_t* b8, int64_t M, int64_t N, int64_t K,
+                float out_scale, void* out, int out_dtype, void* stream) {
+  (void)a8; (void)b8; (void)M; (void)N; (void)K; (void)out_scale; (void)out; (void)out_dtype;
+  (void)stream;
+  return fail(PK_ERR_UNSUPPORTED, "pk_fp8_gemm is not built yet");
+}
+
+size_t pk_gemm_splitk_workspace_size(int64_t M, int64_t N, int64_t K, int split_k) {
+  (void)M; (void)N; (void)K; (void)split_k;
+  return 0;
+}
+
+int pk_gemm_splitk(const void* a, const void* b, int dtype, int64_t M, int64_t N, int64_t K,
+                   int split_k, float* out, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  (void)a; (void)b; (void)dtype; (void)M; (void)N; (void)K; (void)split_k; (void)out;
+  (void)workspace; (void)workspace_bytes; (void)stream;
+  return fail(PK_ERR_UNSUPPORTED, "pk_gemm_splitk is not built yet");
+}
+
+}  // extern "C"

@@ -1,0 +1,369 @@
+// Device-side building blocks shared by the sm_100a kernels: shared-memory
+// barriers with bounded waits, TMA tile loads, tcgen05 (TMEM + UMMA) wrappers
+// and the smem matrix descriptors the tensor core reads.
+//
+// Every wait in this library is bounded: a wait that does not complete within
+// PK_WAIT_NS nanoseconds records PK_ERR_TIMEOUT in the device status word and
+// returns false, and the caller unwinds (frees TMEM, returns) instead of
+// spinning forever.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "pk_internal.h"
+
+#ifndef PK_WAIT_NS
+#define PK_WAIT_NS 1000000000ull  // 1 s: every legitimate wait here is microseconds
+#endif
+
+namespace pk {
+
+// ---------------------------------------------------------------------------
+// status word
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void record_error(int* status, int code, int where) {
+  if (status != nullptr) {
+    if (atomicCAS(status, 0, code) == 0) status[1] = where;
+  }
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` to complete, for at most PK_WAIT_NS.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int where) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait(a, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(a, parity)) return true;
+    if (globaltimer() - t0 > PK_WAIT_NS) {
+      record_error(status, PK_ERR_TIMEOUT, where);
+      return false;
+    }
+  }
+}
+
+// Named barrier over `nthreads` threads (a multiple of 32) of this CTA.
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Make generic-proxy shared-memory writes visible to the async proxy
+// (TMA engine and tensor core).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// TMA (tiled bulk tensor copies global -> shared)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, uint64_t* bar, int c0,
+                                            int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* m, uint64_t* bar,
+                                                 int c0, int c1, uint64_t hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "l"(hint)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_store_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void tma_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void tma_store_wait_all() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// L2 eviction-priority hints (createpolicy), used as TMA cache hints.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05: tensor memory and the 5th-generation MMA
+// ---------------------------------------------------------------------------
+// Allocate `ncols` TMEM columns (power of two >= 32); whole warp executes.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]; 16-bit inputs, fp32 accumulate.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Same with 8-bit (e4m3) inputs.
+__device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once all previously issued tcgen05.mma of this thread finish.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// 32 TMEM lanes x 32 bit, 16 consecutive columns per lane.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// 32 TMEM lanes x 32 bit, 32 consecutive columns per lane.
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// UMMA shared-memory matrix descriptor (sm_100 format).
+//   bits  0-13 start address >> 4
+//   bits 16-29 leading-dimension byte offset >> 4
+//   bits 32-45 stride-dimension byte offset >> 4
+//   bits 46-47 descriptor version (1 on sm_100)
+//   bits 61-63 layout: 0 none, 2 = 128-byte swizzle
+// K-major, 128B swizzle: rows of 128 B, 8-row groups SBO apart (LBO unused).
+// MN-major, 128B swizzle: 128 B along MN x 8 K rows per atom; atoms along MN
+// are LBO apart, 8-row K groups SBO apart.
+// ---------------------------------------------------------------------------
+constexpr uint64_t kDescSwizzle128 = 2;
+
+__device__ __forceinline__ uint64_t make_smem_desc(uint32_t smem_addr, uint32_t lbo_bytes,
+                                                   uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= kDescSwizzle128 << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f16 / kind::f8f6f4 with fp32 accumulate.
+//   bits 4-5 D format (1 = f32), 7-9 A format, 10-12 B format,
+//   bit 15 A MN-major, bit 16 B MN-major, 17-22 N>>3, 24-28 M>>4.
+// A/B format: kind::f16 -> 0 f16, 1 bf16; kind::f8f6f4 -> 0 e4m3.
+__host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_format, bool a_mn_major,
+                                                  bool b_mn_major, int m, int n) {
+  return (1u << 4) | (ab_format << 7) | (ab_format << 10) | ((a_mn_major ? 1u : 0u) << 15) |
+         ((b_mn_major ? 1u : 0u) << 16) | ((static_cast<uint32_t>(n) >> 3) << 17) |
+         ((static_cast<uint32_t>(m) >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------
+// int4 -> 16-bit dequant helpers.
+// A packed byte holds column 2j in its low nibble and 2j+1 in its high nibble
+// (two's complement). Flipping the nibble's sign bit and OR-ing it into the
+// mantissa of 128.0 (bf16 0x4300) gives 136 + q exactly; subtracting 136
+// yields q. For fp16 the base is 1024.0 (0x6400) and the offset 1032.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t lop3_and_xor(uint32_t a, uint32_t b, uint32_t c) {
+  // (a & b) ^ c; LUT = f(0xF0, 0xCC, 0xAA) = (0xF0 & 0xCC) ^ 0xAA = 0x6A
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+template <typename T>
+struct Int4Magic;
+template <>
+struct Int4Magic<__nv_bfloat16> {
+  static constexpr uint32_t kOr = 0x43084308u;   // 128.0 | flipped sign bit, both halves
+  static constexpr uint32_t kBias = 0x43084308u; // 136.0 in both halves
+};
+template <>
+struct Int4Magic<__half> {
+  static constexpr uint32_t kOr = 0x64086408u;   // 1024.0 | flipped sign bit
+  static constexpr uint32_t kBias = 0x64086408u; // 1032.0
+};
+
+__device__ __forceinline__ uint32_t sub2(uint32_t a, uint32_t b, __nv_bfloat16*) {
+  uint32_t r;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t sub2(uint32_t a, uint32_t b, __half*) {
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b, __nv_bfloat16*) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b, __half*) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Dequantize one 32-bit word of packed int4 (8 consecutive columns c0..c7 of
+// one K row) into four 16-bit pairs (c0,c1) (c2,c3) (c4,c5) (c6,c7), each
+// multiplied by the matching scale pair s01, s23, s45, s67 (same type T).
+// With kScaled = false the codes are returned unscaled (exact integers).
+template <typename T, bool kScaled>
+__device__ __forceinline__ void dequant8(uint32_t w, uint32_t s01, uint32_t s23, uint32_t s45,
+                                         uint32_t s67, uint32_t (&out)[4]) {
+  constexpr uint32_t kMask = 0x000F000Fu;
+  // pairs (c0,c4) (c1,c5) (c2,c6) (c3,c7), biased by +kBias
+  uint32_t x04 = lop3_and_xor(w, kMask, Int4Magic<T>::kOr);
+  uint32_t x15 = lop3_and_xor(w >> 4, kMask, Int4Magic<T>::kOr);
+  uint32_t x26 = lop3_and_xor(w >> 8, kMask, Int4Magic<T>::kOr);
+  uint32_t x37 = lop3_and_xor(w >> 12, kMask, Int4Magic<T>::kOr);
+  // regroup into adjacent-column pairs
+  uint32_t p01 = prmt(x04, x15, 0x5410);
+  uint32_t p45 = prmt(x04, x15, 0x7632);
+  uint32_t p23 = prmt(x26, x37, 0x5410);
+  uint32_t p67 = prmt(x26, x37, 0x7632);
+  T* tag = nullptr;
+  p01 = sub2(p01, Int4Magic<T>::kBias, tag);
+  p23 = sub2(p23, Int4Magic<T>::kBias, tag);
+  p45 = sub2(p45, Int4Magic<T>::kBias, tag);
+  p67 = sub2(p67, Int4Magic<T>::kBias, tag);
+  if constexpr (kScaled) {
+    p01 = mul2(p01, s01, tag);
+    p23 = mul2(p23, s23, tag);
+    p45 = mul2(p45, s45, tag);
+    p67 = mul2(p67, s67, tag);
+  }
+  out[0] = p01;
+  out[1] = p23;
+  out[2] = p45;
+  out[3] = p67;
+}
+
+}  // namespace pk

@@ -1,0 +1,79 @@
+// Internal declarations shared between the kernel translation units and the
+// C-ABI layer (capi.cu). Launchers return cudaError_t; capi.cu validates
+// arguments, maps errors to pk_status and records messages.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "../../include/pico_b200.h"
+
+namespace pk {
+
+// Device status word: [0] first error code, [1] site that recorded it.
+int* device_status_ptr();  // per current device; nullptr on failure
+
+// Sites recorded with PK_ERR_TIMEOUT (which wait gave up).
+enum WaitSite : int {
+  kSiteDecodeFull = 101,
+  kSiteDecodeMma = 102,
+  kSiteDecodeFinal = 103,
+  kSiteGemmProducer = 201,
+  kSiteGemmMma = 202,
+  kSiteGemmEpilogue = 203,
+  kSiteGemmDequant = 204,
+};
+
+// Host-side tensor map encoding (cuTensorMapEncodeTiled via the runtime's
+// driver entry point; nothing links libcuda directly).
+bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                    uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                    uint32_t box_outer, CUtensorMapSwizzle swizzle, const char** why);
+
+int num_sms();  // SM count of the current device (cached)
+
+// ---- quant_pack.cu --------------------------------------------------------
+cudaError_t launch_quant_int4_group(const void* w, int w_dtype, int64_t K, int64_t N, int64_t ldw,
+                                    int group, uint8_t* packed, void* scales, int scale_dtype,
+                                    cudaStream_t s);
+cudaError_t launch_absmax(const void* x, int dtype, int64_t n, float* out, cudaStream_t s);
+cudaError_t launch_quant_int4_tensor(const void* w, int dtype, int64_t n, float scale,
+                                     int8_t* codes, cudaStream_t s);
+cudaError_t launch_pack_int4(const int8_t* q, int64_t K, int64_t N, uint8_t* p, cudaStream_t s);
+cudaError_t launch_unpack_int4(const uint8_t* p, int64_t K, int64_t N, int8_t* q,
+                               cudaStream_t s);
+cudaError_t launch_fp8_quantize(const void* x, int dtype, int64_t n, float scale, uint8_t* y,
+                                cudaStream_t s);
+
+// ---- w4a16_decode.cu -----------------------------------------------------
+struct DecodeArgs {
+  const void* a;
+  int64_t lda;
+  const uint8_t* wp;
+  const void* scales;  // nullptr -> scalar_scale
+  float scalar_scale;
+  int64_t M, N, K;
+  void* out;
+  int out_dtype;
+  int64_t ldo;
+  int split;           // >= 1
+  int a_dtype;
+  float* partials;     // [n_tiles][split][M][128] when split > 1
+  unsigned* sems;      // [n_tiles] arrival counters, zero between calls
+  int* status;
+};
+bool decode_supported(int64_t M, int64_t N, int64_t K, int group, const void* scales,
+                      int64_t lda, const void* a);
+int decode_pick_split(int64_t M, int64_t N, int64_t K);
+size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int split);
+cudaError_t launch_w4a16_decode(const DecodeArgs& args, cudaStream_t s, const char** why);
+
+// ---- w4a16_simt.cu (any shape; CUDA cores) -------------------------------
+cudaError_t launch_w4a16_simt(const void* a, int a_dtype, int64_t lda, const uint8_t* wp,
+                              const void* scales, float scalar_scale, int group, int64_t M,
+                              int64_t N, int64_t K, void* out, int out_dtype, int64_t ldo,
+                              cudaStream_t s);
+
+}  // namespace pk

@@ -1,0 +1,159 @@
+"""Packed int4 quantization and the W4A16 GEMM -- drop-in for pico-kernels'
+``gemm_int4`` module (gemm_int4.py), running hand-written sm_100a kernels.
+
+Same names, arguments, layouts and return types as the reference:
+
+* ``quantize_int4(w) -> (int8[K, N], float)``           gemm_int4.py:58-62
+* ``pack_int4_n(w_q) -> uint8[K, N//2]``                gemm_int4.py:65-72
+* ``int4_gemm(a, w_packed, scale, BLOCK_M, BLOCK_N, BLOCK_K) -> fp32[M, N]``
+                                                        gemm_int4.py:75-92
+
+Additions: ``quantize_int4_grouped`` (per-group int4 along K, the
+``quantize.quantize_col`` arithmetic emitted as packed codes + scales),
+``unpack_int4_n``, and keyword-only ``group_size``, ``out_dtype`` and
+``split_k`` on ``int4_gemm``. ``scale`` may be the reference's per-tensor
+float or a ``[ceil(K/group), N]`` tensor of group scales.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+__all__ = ["quantize_int4", "pack_int4_n", "unpack_int4_n", "quantize_int4_grouped",
+           "int4_gemm"]
+
+
+def quantize_int4(w: torch.Tensor) -> tuple[torch.Tensor, float]:
+    """Per-tensor symmetric int4 quantization of ``w`` (fp16/bf16/fp32).
+
+    ``scale = max|w| / 7`` (a Python float; this synchronises, like the
+    reference's ``.item()``), codes ``round(w / scale).clamp(-8, 7)`` as int8.
+    """
+    _lib.require_cuda(w)
+    lib = _lib.load()
+    w = w.contiguous()
+    dt = _lib.dtype_code(w.dtype)
+    amax = torch.empty((), dtype=torch.float32, device=w.device)
+    s = _lib.stream_of(w)
+    _lib.check(lib.pk_absmax(w.data_ptr(), dt, w.numel(), amax.data_ptr(), s), "absmax")
+    scale = amax.item() / 7.0
+    codes = torch.empty(w.shape, dtype=torch.int8, device=w.device)
+    _lib.check(lib.pk_quant_int4_tensor(w.data_ptr(), dt, w.numel(), scale, codes.data_ptr(), s),
+               "quantize_int4")
+    return codes, scale
+
+
+def pack_int4_n(w_q: torch.Tensor) -> torch.Tensor:
+    """Pack signed int4 codes 2-per-byte along N -> ``(K, N//2)`` uint8.
+
+    Low nibble = even column, high nibble = odd column.
+    """
+    _lib.require_cuda(w_q)
+    K, N = w_q.shape
+    if N % 2:
+        raise _lib.ShapeError(f"N must be even (got {N})")
+    q = w_q if w_q.dtype == torch.int8 else w_q.to(torch.int8)
+    q = q.contiguous()
+    out = torch.empty((K, N // 2), dtype=torch.uint8, device=q.device)
+    _lib.check(_lib.load().pk_pack_int4_n(q.data_ptr(), K, N, out.data_ptr(), _lib.stream_of(q)),
+               "pack_int4_n")
+    return out
+
+
+def unpack_int4_n(w_packed: torch.Tensor) -> torch.Tensor:
+    """Inverse of ``pack_int4_n``: sign-extended int8 codes ``(K, N)``."""
+    _lib.require_cuda(w_packed)
+    K, Nh = w_packed.shape
+    p = w_packed.contiguous()
+    out = torch.empty((K, 2 * Nh), dtype=torch.int8, device=p.device)
+    _lib.check(_lib.load().pk_unpack_int4_n(p.data_ptr(), K, 2 * Nh, out.data_ptr(),
+                                            _lib.stream_of(p)), "unpack_int4_n")
+    return out
+
+
+def quantize_int4_grouped(w: torch.Tensor, group_size: int = 128,
+                          scale_dtype: torch.dtype | None = None
+                          ) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-group symmetric int4 quantize + pack of ``w[K, N]``, groups along K.
+
+    Per column ``n`` and group ``g`` this is ``quantize.quantize_col``'s
+    arithmetic (quantize.py:42-60): ``scale = max|w|.clamp_min(1e-12) / 7``
+    in fp32 and ``q = clamp(round(w / scale), -7, 7)``; the codes are packed
+    with ``pack_int4_n``'s byte layout and the scale is stored rounded to
+    ``scale_dtype`` (default: ``w.dtype`` for fp16/bf16, fp32 otherwise).
+    Returns ``(packed uint8[K, N//2], scales[ceil(K/group_size), N])``.
+    """
+    _lib.require_cuda(w)
+    if w.dim() != 2:
+        raise _lib.ShapeError("w must be 2-D [K, N]")
+    K, N = w.shape
+    if N % 2:
+        raise _lib.ShapeError(f"N must be even (got {N})")
+    if scale_dtype is None:
+        scale_dtype = w.dtype if w.dtype in (torch.float16, torch.bfloat16) else torch.float32
+    if w.stride(1) != 1:
+        w = w.contiguous()
+    G = (K + group_size - 1) // group_size
+    packed = torch.empty((K, N // 2), dtype=torch.uint8, device=w.device)
+    scales = torch.empty((G, N), dtype=scale_dtype, device=w.device)
+    _lib.check(_lib.load().pk_quant_int4_group(
+        w.data_ptr(), _lib.dtype_code(w.dtype), K, N, w.stride(0), group_size, packed.data_ptr(),
+        scales.data_ptr(), _lib.dtype_code(scale_dtype), _lib.stream_of(w)), "quantize_int4_grouped")
+    return packed, scales
+
+
+def int4_gemm(a: torch.Tensor, w_packed: torch.Tensor, scale,
+              BLOCK_M: int = 64, BLOCK_N: int = 64, BLOCK_K: int = 64, *,
+              group_size: int | None = None, out_dtype: torch.dtype = torch.float32,
+              split_k: int = 0) -> torch.Tensor:
+    """``a @ (W_int4 * scale)`` where ``w_packed`` is ``(K, N//2)`` uint8.
+
+    ``scale``: the reference's per-tensor float, or a ``[G, N]`` tensor of
+    group scales (``group_size`` defaults to ``K // G``). ``BLOCK_*`` are
+    accepted for signature compatibility; the tile shape is fixed by the
+    sm_100a kernels. Output fp32 (or ``out_dtype=torch.bfloat16``).
+    """
+    del BLOCK_M, BLOCK_N, BLOCK_K
+    _lib.require_cuda(a, w_packed)
+    if a.dtype not in (torch.float16, torch.bfloat16):
+        raise _lib.DtypeError(f"a must be fp16 or bf16 (got {a.dtype})")
+    if a.dim() != 2 or w_packed.dim() != 2:
+        raise _lib.ShapeError("a and w_packed must be 2-D")
+    M, K = a.shape
+    K2, N_half = w_packed.shape
+    if K2 != K:
+        raise _lib.ShapeError(f"inner dimensions differ: a has K={K}, w_packed has K={K2}")
+    if w_packed.dtype != torch.uint8:
+        raise _lib.DtypeError("w_packed must be uint8")
+    N = 2 * N_half
+    if a.stride(1) != 1 or a.stride(0) < K:
+        a = a.contiguous()
+    w_packed = w_packed.contiguous()
+
+    scales = None
+    scalar = 1.0
+    group = 0
+    if isinstance(scale, torch.Tensor) and scale.numel() > 1:
+        _lib.require_cuda(scale)
+        if scale.dim() != 2 or scale.shape[1] != N:
+            raise _lib.ShapeError(f"group scales must be [G, N={N}] (got {tuple(scale.shape)})")
+        G = scale.shape[0]
+        group = group_size if group_size is not None else K // G
+        if group <= 0 or (K + group - 1) // group != G:
+            raise _lib.ShapeError(f"{G} scale rows do not tile K={K} with group_size={group}")
+        scales = scale if scale.dtype == a.dtype else scale.to(a.dtype)
+        scales = scales.contiguous()
+    else:
+        scalar = float(scale)
+
+    out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    lib = _lib.load()
+    ws_bytes = lib.pk_w4a16_workspace_size(M, N, K, split_k)
+    ws = _lib.workspace(a.device, ws_bytes)
+    _lib.check(lib.pk_w4a16_gemm(
+        a.data_ptr(), _lib.dtype_code(a.dtype), a.stride(0), w_packed.data_ptr(),
+        _lib.ptr(scales), scalar, group, M, N, K, out.data_ptr(), _lib.dtype_code(out_dtype), N,
+        split_k, _lib.ptr(ws), ws_bytes, _lib.stream_of(a)), "int4_gemm")
+    return out

@@ -1,0 +1,55 @@
+"""The C-ABI library loads without a GPU and exports what the header declares."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from pico_kernels_b200 import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def header_functions():
+    text = (ROOT / "include" / "pico_b200.h").read_text()
+    return sorted(set(re.findall(r"PK_API\s+[\w\s\*]+?\b(pk_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_boundary():
+    names = header_functions()
+    for must in ("pk_quant_int4_group", "pk_pack_int4_n", "pk_w4a16_gemm", "pk_fp8_gemm",
+                 "pk_gemm_splitk", "pk_w4a16_workspace_size", "pk_last_error_string"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    if not _lib.LIB_PATH.exists():
+        pytest.fail(f"{_lib.LIB_PATH} not built (run python -m pico_kernels_b200.build)")
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    missing = [n for n in header_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_the_header():
+    assert sorted(_lib.SIGNATURES) == header_functions()
+
+
+def test_host_only_calls_work_without_gpu():
+    lib = _lib.load()
+    assert lib.pk_version() >= 100
+    # shape validation happens on the host before any CUDA call
+    st = lib.pk_pack_int4_n(None, 4, 3, None, None)
+    assert st == _lib.PK_ERR_SHAPE
+    assert _lib.last_error() != ""
+    with pytest.raises(ValueError):
+        _lib.check(st, "pack")
+    with pytest.raises(AssertionError):  # the reference's error type still catches it
+        _lib.check(st, "pack")
+
+
+def test_workspace_size_is_host_only():
+    lib = _lib.load()
+    assert lib.pk_w4a16_workspace_size(1, 4096, 4096, 1) == 0
+    assert lib.pk_w4a16_workspace_size(1, 4096, 4096, 8) > 0
+    assert lib.pk_w4a16_workspace_size(1, 4096, 4096, 8) < lib.pk_w4a16_workspace_size(16, 4096, 4096, 8)

@@ -1,0 +1,119 @@
+"""GPU parity of the W4A16 GEMM against the oracle's dequantize-then-matmul in
+fp32 (the reference's own formula, tests/test_gemm_int4.py:26).
+
+Tolerances: the kernel rounds each dequantized weight q*s to the activation
+dtype before the MMA (unit roundoff 2^-8 for bf16, 2^-11 for fp16), then
+accumulates in fp32. For N(0,1) activations and N(0,0.02) weights that gives
+a relative Frobenius error near 2.3e-3 (bf16) / 3e-4 (fp16). Bounds:
+rel-Frobenius <= 5e-3 (bf16) / 1e-3 (fp16), max-abs <= 2e-2 * max|Y|.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import pico_kernels_b200 as pk
+from oracle import quant_ref as o
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.bfloat16: 5e-3, torch.float16: 1e-3}
+
+
+def make_case(M, N, K, dt, group=128, seed=0, wstd=0.02):
+    g = torch.Generator().manual_seed(seed)
+    w = (torch.randn(K, N, generator=g) * wstd).to(dt)
+    g1 = torch.Generator().manual_seed(seed + 1)
+    a = torch.randn(M, K, generator=g1).to(dt)
+    codes, s32 = o.group_quant_codes(w.float().numpy(), group)
+    s_stored = o.store_scales(s32, "bf16" if dt == torch.bfloat16 else "f16")
+    ref = o.w4a16_reference(a.float().numpy(), codes, s_stored, group)
+    return a, w, ref
+
+
+def check(y: torch.Tensor, ref: np.ndarray, dt, what=""):
+    y = y.float().cpu().numpy()
+    rel = np.linalg.norm(y - ref) / np.linalg.norm(ref)
+    mx = np.abs(y - ref).max()
+    assert rel <= TOL[dt], (what, rel)
+    assert mx <= 2e-2 * np.abs(ref).max(), (what, mx)
+    return rel
+
+
+@pytest.mark.parametrize("M", [1, 4, 16])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_decode_4096(M, dt):
+    a, w, ref = make_case(M, 4096, 4096, dt)
+    packed, scales = pk.quantize_int4_grouped(w.cuda(), 128)
+    y = pk.int4_gemm(a.cuda(), packed, scales)
+    assert y.dtype == torch.float32 and y.shape == (M, 4096)
+    check(y, ref, dt, f"M={M}")
+    assert pk.device_status() == (0, 0)
+
+
+@pytest.mark.parametrize("split", [1, 2, 3, 8, 32])
+def test_decode_split_k_deterministic(split):
+    a, w, ref = make_case(4, 4096, 4096, torch.bfloat16, seed=3)
+    packed, scales = pk.quantize_int4_grouped(w.cuda(), 128)
+    a = a.cuda()
+    y1 = pk.int4_gemm(a, packed, scales, split_k=split)
+    y2 = pk.int4_gemm(a, packed, scales, split_k=split)
+    assert torch.equal(y1, y2), "split-K reduction must be bitwise reproducible"
+    check(y1, ref, torch.bfloat16, f"split={split}")
+
+
+def test_decode_splits_agree():
+    a, w, _ = make_case(16, 2048, 4096, torch.bfloat16, seed=5)
+    packed, scales = pk.quantize_int4_grouped(w.cuda(), 128)
+    a = a.cuda()
+    y1 = pk.int4_gemm(a, packed, scales, split_k=1)
+    for s in (2, 4, 16):
+        ys = pk.int4_gemm(a, packed, scales, split_k=s)
+        assert (ys - y1).abs().max().item() <= 1e-4 * y1.abs().max().item()
+
+
+def test_decode_llama70b_shapes():
+    for (N, K) in ((28672, 8192), (8192, 28672)):
+        a, w, ref = make_case(1, N, K, torch.bfloat16, seed=7)
+        packed, scales = pk.quantize_int4_grouped(w.cuda(), 128)
+        check(pk.int4_gemm(a.cuda(), packed, scales), ref, torch.bfloat16, f"N={N} K={K}")
+
+
+def test_decode_bf16_output():
+    a, w, ref = make_case(2, 1024, 2048, torch.bfloat16, seed=9)
+    packed, scales = pk.quantize_int4_grouped(w.cuda(), 128)
+    y = pk.int4_gemm(a.cuda(), packed, scales, out_dtype=torch.bfloat16)
+    assert y.dtype == torch.bfloat16
+    check(y, ref, torch.bfloat16)
+
+
+def test_per_tensor_scale_reference_api():
+    """tests/test_gemm_int4.py:19-30 at a decode shape: per-tensor float scale."""
+    torch.manual_seed(0)
+    a = torch.randn(16, 256, device="cuda", dtype=torch.float16)
+    w = torch.randn(256, 512, device="cuda", dtype=torch.float16)
+    w_q, scale = pk.quantize_int4(w)
+    c = pk.int4_gemm(a, pk.pack_int4_n(w_q), scale)
+    ref = a.float() @ (w_q.float() * scale)
+    assert torch.allclose(c, ref, atol=1e-1, rtol=1e-2)
+    # codes are exact in fp16, so only fp32 summation order differs
+    assert (torch.norm(c - ref) / torch.norm(ref)).item() < 1e-5
+
+
+@pytest.mark.parametrize("M,N,K,group", [(3, 130, 200, 64), (20, 256, 384, 128), (1, 2, 7, 4)])
+def test_ragged_shapes_generic_kernel(M, N, K, group):
+    a, w, ref = make_case(M, N, K, torch.bfloat16, group=group, seed=11)
+    packed, scales = pk.quantize_int4_grouped(w.cuda(), group)
+    y = pk.int4_gemm(a.cuda(), packed, scales, group_size=group)
+    # the CUDA-core kernel dequantizes in fp32: only summation order differs
+    yy = y.cpu().numpy()
+    assert np.abs(yy - ref).max() <= 1e-4 * max(1.0, np.abs(ref).max())
+
+
+def test_errors_are_reference_compatible():
+    a = torch.randn(4, 256, device="cuda", dtype=torch.bfloat16)
+    wp = torch.zeros(128, 64, dtype=torch.uint8, device="cuda")
+    with pytest.raises(AssertionError):
+        pk.int4_gemm(a, wp, 1.0)
+    with pytest.raises(TypeError):
+        pk.int4_gemm(a.float(), torch.zeros(256, 64, dtype=torch.uint8, device="cuda"), 1.0)
