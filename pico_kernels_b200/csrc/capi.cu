@@ -245,9 +245,9 @@ int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t* wp, co
     if (split > K / 128) split = static_cast<int>(K / 128);
     p.split = split;
     p.status = device_status_ptr();
-    if (split > 1) {
+    if (split > 1 && workspace != nullptr) {
       const size_t need = decode_workspace_bytes(M, N, K, split);
-      if (workspace == nullptr || workspace_bytes < need)
+      if (workspace_bytes < need)
         return fail(PK_ERR_WORKSPACE, "split-K needs %zu workspace bytes, got %zu", need,
                     workspace_bytes);
       if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
@@ -257,9 +257,15 @@ int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t* wp, co
       p.sems = static_cast<unsigned*>(workspace);
       p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + sem_bytes);
     }
+    if (split > decode_max_cluster_split() && p.partials == nullptr)
+      return fail(PK_ERR_WORKSPACE, "split_k > %d needs %zu workspace bytes",
+                  decode_max_cluster_split(), decode_workspace_bytes(M, N, K, split));
     const char* why = "";
     cudaError_t e = launch_w4a16_decode(p, s, &why);
-    if (e == cudaErrorInvalidValue && why[0] != '\0') return fail(PK_ERR_ALIGN, "%s", why);
+    if (e == cudaErrorInvalidValue && why[0] != '\0') {
+      const bool ws = std::strstr(why, "workspace") != nullptr;
+      return fail(ws ? PK_ERR_WORKSPACE : PK_ERR_ALIGN, "%s", why);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "w4a16 decode launch");
     ok();
     return PK_OK;

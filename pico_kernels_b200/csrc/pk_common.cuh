@@ -3,7 +3,7 @@
 // and the smem matrix descriptors the tensor core reads.
 //
 // Every wait in this library is bounded: a wait that does not complete within
-// PK_WAIT_NS nanoseconds records PK_ERR_TIMEOUT in the device status word and
+// PK_WAIT_CYCLES SM cycles records PK_ERR_TIMEOUT in the device status word and
 // returns false, and the caller unwinds (frees TMEM, returns) instead of
 // spinning forever.
 #pragma once
@@ -16,8 +16,8 @@
 
 #include "pk_internal.h"
 
-#ifndef PK_WAIT_NS
-#define PK_WAIT_NS 1000000000ull  // 1 s: every legitimate wait here is microseconds
+#ifndef PK_WAIT_CYCLES
+#define PK_WAIT_CYCLES 4000000000ll  // ~2 s at 1.9 GHz; legitimate waits are microseconds
 #endif
 
 namespace pk {
@@ -74,20 +74,63 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return ok != 0;
 }
 
-// Wait for phase `parity` of `bar` to complete, for at most PK_WAIT_NS.
+// Wait for phase `parity` of `bar` to complete, for at most PK_WAIT_CYCLES SM
+// clock cycles (about 2 s at full clock). The bound is checked on the SM's
+// own cycle counter: cheap to read, unlike the global timer.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int where) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  const long long t0 = clock64();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 32; ++i)
+    for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(a, parity)) return true;
-    if (globaltimer() - t0 > PK_WAIT_NS) {
+    if (clock64() - t0 > PK_WAIT_CYCLES) {
       record_error(status, PK_ERR_TIMEOUT, where);
       return false;
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// programmatic dependent launch and thread-block clusters
+// ---------------------------------------------------------------------------
+// Wait until the grids this one depends on have completed and their memory
+// is visible (a no-op when the launch had no programmatic dependency).
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Allow the next grid in the stream (launched with programmatic serialization)
+// to start its prologue; it still waits for this grid in griddep_wait().
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// All threads of all CTAs in the cluster; release/acquire orders shared
+// memory writes before the barrier with distributed-shared reads after it.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
 }
 
 // Named barrier over `nthreads` threads (a multiple of 32) of this CTA.
@@ -145,6 +188,15 @@ __device__ __forceinline__ void tma_store_wait_read() {
 template <int N>
 __device__ __forceinline__ void tma_store_wait_all() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// 16-byte streaming load that bypasses L1 (read-only data read once).
+__device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
 }
 
 // L2 eviction-priority hints (createpolicy), used as TMA cache hints.
@@ -330,6 +382,23 @@ __device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b, __half*) {
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
+
+// Convert one 32-bit word of packed int4 (columns c0..c7 of one K row) into
+// exact 16-bit integer codes, four pairs in the order (c0,c4) (c1,c5) (c2,c6)
+// (c3,c7): the lanes of a 16-byte chunk hold columns 0,4,1,5,2,6,3,7, a fixed
+// permutation the consumer undoes. 3 shifts, 4 lop3 and 4 packed subtracts.
+template <typename T>
+__device__ __forceinline__ void int4_codes8(uint32_t w, uint32_t (&out)[4]) {
+  constexpr uint32_t kMask = 0x000F000Fu;
+  T* tag = nullptr;
+  out[0] = sub2(lop3_and_xor(w, kMask, Int4Magic<T>::kOr), Int4Magic<T>::kBias, tag);
+  out[1] = sub2(lop3_and_xor(w >> 4, kMask, Int4Magic<T>::kOr), Int4Magic<T>::kBias, tag);
+  out[2] = sub2(lop3_and_xor(w >> 8, kMask, Int4Magic<T>::kOr), Int4Magic<T>::kBias, tag);
+  out[3] = sub2(lop3_and_xor(w >> 12, kMask, Int4Magic<T>::kOr), Int4Magic<T>::kBias, tag);
+}
+
+// Column (0..7) held by lane j of a chunk written by int4_codes8.
+__host__ __device__ constexpr int int4_codes8_column(int j) { return (j >> 1) + 4 * (j & 1); }
 
 // Dequantize one 32-bit word of packed int4 (8 consecutive columns c0..c7 of
 // one K row) into four 16-bit pairs (c0,c1) (c2,c3) (c4,c5) (c6,c7), each

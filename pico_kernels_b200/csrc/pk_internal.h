@@ -60,10 +60,12 @@ struct DecodeArgs {
   int64_t ldo;
   int split;           // >= 1
   int a_dtype;
-  float* partials;     // [n_tiles][split][M][128] when split > 1
+  float* partials;     // [n_tiles][split][M][128] when split > 1 (global reduction)
   unsigned* sems;      // [n_tiles] arrival counters, zero between calls
+  bool force_workspace;  // reduce through the workspace even when a cluster would fit
   int* status;
 };
+int decode_max_cluster_split();
 bool decode_supported(int64_t M, int64_t N, int64_t K, int group, const void* scales,
                       int64_t lda, const void* a);
 int decode_pick_split(int64_t M, int64_t N, int64_t K);

@@ -1,47 +1,67 @@
 // W4A16 GEMM for decode shapes (M <= 16) on sm_100a.
 //
-// out[M, N] = A[M, K] @ (q[K, N] * s[K/128, N])  (gemm_int4.py:75-92 with
-// group scales; q unpacked from Wp[K, N/2] as in gemm_int4.py:43-50).
+// out[M, N] = A[M, K] @ (q[K, N] * s[K/128, N])  -- gemm_int4.int4_gemm
+// (gemm_int4.py:75-92) with group scales; q unpacked from Wp[K, N/2] with the
+// reference's nibble order (gemm_int4.py:43-50).
 //
-// Design (swap-AB): the weight tile is the MMA's M=128 operand (128 output
-// columns n), the activations are its N=16 operand (M padded to 16 by TMA
-// zero fill), so D[n, m] accumulates in 16 TMEM columns. One CTA owns 128
-// columns and a contiguous range of 128-row K stages; stages are TMA-loaded
-// into a ring of shared-memory slots (packed weights + activation tile +
-// group scales), all issued up front when they fit. 256 threads dequantize
-// each 64-row half stage in registers (int4 -> bf16/f16, times the group
-// scale) into a 128B-swizzled MN-major tile; thread 0 then issues four
-// tcgen05.mma (K=16 each). The K reduction is split over `split` CTAs per
-// column tile: each writes its fp32 partial to the workspace, bumps the
-// tile's arrival counter, and the last arriver sums all partials in split
-// order (deterministic) and writes the output, then re-arms the counter.
+// Swap-AB: the weight tile is the MMA's M = 128 operand (128 output columns),
+// the activations its N = 16 operand (M padded to 16 by TMA zero fill), so
+// D[n, m] lives in 16 TMEM columns. One CTA owns 128 columns and a contiguous
+// range of 128-row K stages (one quantization group each). Warp roles:
+//   warps 0-3  epilogue: per group, read the fp32 partial D_g from TMEM and
+//              accumulate s[g, n] * D_g in registers (the scale is applied in
+//              fp32, after an exact integer MMA); then the split-K reduction
+//              and the output store;
+//   warp 4     TMA producer: packed weights + activation tile per stage into a
+//              ring of shared-memory slots;
+//   warp 5     TMEM allocator and MMA issuer (one thread);
+//   warps 6-13 dequant: int4 -> exact 16-bit integer codes in registers,
+//              written as a 128B-swizzled MN-major operand tile.
+// All hand-offs are mbarriers with bounded waits.
+//
+// Split-K: the `split` CTAs of a column tile either form a thread-block
+// cluster and reduce their partials through distributed shared memory, or
+// (split > 8) write partials to a global workspace where the last arriver
+// reduces them. Both sum partials in split order starting from zero, so the
+// result is deterministic and identical between the two modes.
 #include "pk_common.cuh"
 
 namespace pk {
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kBN = 128;     // output columns per CTA (MMA M)
-constexpr int kBK = 128;     // K rows per stage (one quantization group)
-constexpr int kMmaN = 16;    // padded M (MMA N)
-constexpr int kSlots = 4;    // TMA stage ring
-constexpr int kDeqBufs = 3;  // dequantized 64-row half-stage ring
+constexpr int kEpiWarps = 4;
+constexpr int kTmaWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kDeqWarp0 = 6;
+constexpr int kDeqWarps = 8;
+constexpr int kThreads = (kDeqWarp0 + kDeqWarps) * 32;  // 448
+constexpr int kDeqThreads = kDeqWarps * 32;
 
-// shared memory layout (bytes from a 1024-aligned base)
-constexpr int kAtileBytes = 2 * kMmaN * 128;        // two 64-col SW128 boxes: 4096
-constexpr int kWBytes = kBK * (kBN / 2);            // 128 rows x 64 B: 8192
-constexpr int kScaleBytes = kBN * 2;                // 256
-constexpr int kSlotBytes = 13312;                   // A | W | scales, padded to 1 KB
+constexpr int kBN = 128;      // output columns per CTA (MMA M)
+constexpr int kBK = 128;      // K rows per stage = one quantization group
+constexpr int kMmaN = 16;     // padded M (MMA N)
+constexpr int kSlots = 4;     // TMA stage ring
+constexpr int kDeqBufs = 3;   // ring of dequantized 64-row half stages
+constexpr int kGroupSlots = 8;                       // TMEM ring of per-group partials
+constexpr int kTmemCols = kGroupSlots * kMmaN;       // 128
+constexpr int kMaxClusterSplit = 8;
+
+// shared memory (bytes from a 1024-aligned base)
+constexpr int kAtileBytes = 2 * kMmaN * 128;         // two 64-column SW128 boxes: 4096
+constexpr int kWBytes = kBK * (kBN / 2);             // 128 rows x 64 B: 8192
+constexpr int kSlotBytes = kAtileBytes + kWBytes;    // 12288
 constexpr int kSlotA = 0;
 constexpr int kSlotW = kAtileBytes;
-constexpr int kSlotS = kAtileBytes + kWBytes;
-constexpr int kDeqBytes = kBN * 64 * 2;             // 16384 per half stage
-constexpr int kDeqLBO = 8192;                       // between the two 64-column atoms
-constexpr int kDeqOff = kSlots * kSlotBytes;
-constexpr int kBarOff = kDeqOff + kDeqBufs * kDeqBytes;
-constexpr int kSmemBytes = kBarOff + 256 + 1024;    // + barriers + alignment slack
+constexpr int kDeqBytes = kBN * 64 * 2;              // 16384 per half stage
+constexpr int kDeqLBO = 8192;                        // between the two 64-column atoms
+constexpr int kDeqOff = kSlots * kSlotBytes;         // 49152
+constexpr int kBarOff = kDeqOff + kDeqBufs * kDeqBytes;  // 98304
+constexpr int kNumBars = 2 * kSlots + 2 * kDeqBufs + 2 * kGroupSlots;
+constexpr int kSmemBytes = kBarOff + kNumBars * 8 + 16 + 1024;
+constexpr int kRedOff = kDeqOff;                     // split-K partials reuse the dequant ring
 
-static_assert(kSlotS + kScaleBytes <= kSlotBytes, "slot layout");
+static_assert(kMmaN * kBN * 4 <= kDeqBufs * kDeqBytes, "reduction buffer fits");
+static_assert(kSmemBytes <= 113 * 1024, "two CTAs per SM");
 
 template <typename T>
 struct TypeFmt;
@@ -54,6 +74,9 @@ struct TypeFmt<__half> {
   static constexpr uint32_t kFmt = 0;
 };
 
+__device__ __forceinline__ float ld_scale(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ float ld_scale(const __half* p) { return __half2float(*p); }
+
 __device__ __forceinline__ void store_out(void* out, int out_dtype, int64_t idx, float v) {
   if (out_dtype == PK_BF16)
     static_cast<__nv_bfloat16*>(out)[idx] = __float2bfloat16_rn(v);
@@ -64,19 +87,22 @@ __device__ __forceinline__ void store_out(void* out, int out_dtype, int64_t idx,
 template <typename T, bool kGrouped>
 __global__ void __launch_bounds__(kThreads, 2)
     w4a16_decode_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmW,
-                        const __grid_constant__ CUtensorMap tmS, int M, int N, int K, int split,
-                        float scalar_scale, void* __restrict__ out, int out_dtype, int64_t ldo,
+                        const __grid_constant__ CUtensorMap tmW, const T* __restrict__ scales,
+                        int M, int N, int K, int split, int use_cluster, float scalar_scale,
+                        void* __restrict__ out, int out_dtype, int64_t ldo,
                         float* __restrict__ partials, unsigned* __restrict__ sems,
                         int* __restrict__ status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOff);
-  uint64_t* mma_done = full + kSlots;
-  uint64_t* final_bar = mma_done + kDeqBufs;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(final_bar + 1);
-  __shared__ int s_last;
+  uint64_t* slot_empty = full + kSlots;
+  uint64_t* deq_full = slot_empty + kSlots;
+  uint64_t* deq_empty = deq_full + kDeqBufs;
+  uint64_t* tm_full = deq_empty + kDeqBufs;
+  uint64_t* tm_empty = tm_full + kGroupSlots;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tm_empty + kGroupSlots);
+  int* s_flag = reinterpret_cast<int*>(tmem_holder + 1);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -88,155 +114,257 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int g_end = static_cast<int>((static_cast<int64_t>(ks + 1) * total_stages) / split);
   const int S = g_end - g_begin;
 
-  if (tid == 0) {
-    for (int i = 0; i < kSlots; ++i) mbar_init(&full[i], 1);
-    for (int i = 0; i < kDeqBufs; ++i) mbar_init(&mma_done[i], 1);
-    mbar_init(final_bar, 1);
+  if (warp == kTmaWarp && lane == 0) {
+    for (int i = 0; i < kSlots; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&slot_empty[i], 1);
+    }
+    for (int i = 0; i < kDeqBufs; ++i) {
+      mbar_init(&deq_full[i], kDeqWarps);
+      mbar_init(&deq_empty[i], 1);
+    }
+    for (int i = 0; i < kGroupSlots; ++i) {
+      mbar_init(&tm_full[i], 1);
+      mbar_init(&tm_empty[i], kEpiWarps);
+    }
     fence_barrier_init();
-  }
-  if (warp == 0) tmem_alloc(tmem_holder, 32);
-  if (tid == 32) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
-    if (kGrouped) tma_prefetch_desc(&tmS);
   }
+  if (warp == kMmaWarp) tmem_alloc(tmem_holder, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  constexpr uint32_t kStageTx = kAtileBytes + kWBytes + (kGrouped ? kScaleBytes : 0);
-  auto issue_stage = [&](int s) {
-    const int slot = s % kSlots;
-    uint8_t* base = smem + slot * kSlotBytes;
-    const int g = g_begin + s;
-    mbar_arrive_expect_tx(&full[slot], kStageTx);
-    tma_load_2d(base + kSlotA, &tmA, &full[slot], g * kBK, 0);
-    tma_load_2d(base + kSlotA + kMmaN * 128, &tmA, &full[slot], g * kBK + 64, 0);
-    tma_load_2d(base + kSlotW, &tmW, &full[slot], tile * (kBN / 2), g * kBK);
-    if (kGrouped) tma_load_2d(base + kSlotS, &tmS, &full[slot], tile * kBN, g);
-  };
-
-  int issued = 0;
-  if (tid == 0) {
-    const int pre = S < kSlots ? S : kSlots;
-    for (int s = 0; s < pre; ++s) issue_stage(s);
-    issued = pre;
-  }
-
-  constexpr uint32_t kIdesc = make_idesc(TypeFmt<T>::kFmt, true, false, 128, kMmaN);
-  const uint32_t deq_base = smem_u32(smem + kDeqOff);
-  const int w = tid & 15;          // 4-byte word within a 64-byte packed row: columns 8w..8w+7
-  const int rsub = tid >> 4;       // 0..15
-  const int atom = w >> 3, chunk = w & 7;
+  // Everything above overlaps the previous grid's tail; global memory is
+  // touched only after it has completed.
+  griddep_wait();
+  griddep_launch_dependents();
 
   bool fail = false;
-  const int halves = 2 * S;
-  for (int u = 0; u < halves; ++u) {
-    const int s = u >> 1, h = u & 1;
-    const int slot = s % kSlots;
-    const int buf = u % kDeqBufs;
-    uint8_t* base = smem + slot * kSlotBytes;
-    if (!fail && h == 0)
-      fail = !mbar_wait(&full[slot], (s / kSlots) & 1, status, kSiteDecodeFull);
-    if (!fail && u >= kDeqBufs)
-      fail = !mbar_wait(&mma_done[buf], ((u / kDeqBufs) - 1) & 1, status, kSiteDecodeMma);
-    // the MMAs of half u-3 are done: if that finished a stage, refill its slot
-    if (!fail && tid == 0 && u >= kDeqBufs && ((u - kDeqBufs) & 1) && issued < S) {
-      issue_stage(issued);
-      ++issued;
-    }
-    if (!fail) {
-      uint32_t s01 = 0, s23 = 0, s45 = 0, s67 = 0;
-      if (kGrouped) {
-        const uint4 sv = *reinterpret_cast<const uint4*>(base + kSlotS + w * 16);
-        s01 = sv.x; s23 = sv.y; s45 = sv.z; s67 = sv.w;
+  int issued = 0;
+  if (warp == kTmaWarp) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      for (int s = 0; s < S && !fail; ++s) {
+        const int slot = s % kSlots;
+        if (s >= kSlots)
+          fail = !mbar_wait(&slot_empty[slot], ((s / kSlots) - 1) & 1, status, kSiteDecodeFull);
+        if (fail) break;
+        uint8_t* base = smem + slot * kSlotBytes;
+        const int g = g_begin + s;
+        mbar_arrive_expect_tx(&full[slot], kSlotBytes);
+        tma_load_2d(base + kSlotW, &tmW, &full[slot], tile * (kBN / 2), g * kBK);
+        tma_load_2d(base + kSlotA, &tmA, &full[slot], g * kBK, 0);
+        tma_load_2d(base + kSlotA + kMmaN * 128, &tmA, &full[slot], g * kBK + 64, 0);
+        issued = s + 1;
       }
-      uint8_t* dq = smem + kDeqOff + buf * kDeqBytes;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = rsub + 16 * i;  // row within the half stage, 0..63
-        const uint32_t word =
-            *reinterpret_cast<const uint32_t*>(base + kSlotW + (64 * h + r) * 64 + w * 4);
-        uint32_t o[4];
-        dequant8<T, kGrouped>(word, s01, s23, s45, s67, o);
-        const int r8 = r & 7;
-        const int off = atom * kDeqLBO + (r >> 3) * 1024 + r8 * 128 + ((chunk ^ r8) << 4);
-        *reinterpret_cast<uint4*>(dq + off) = make_uint4(o[0], o[1], o[2], o[3]);
-      }
-      fence_proxy_async_smem();
     }
-    fail = __syncthreads_or(fail) != 0;
-    if (fail) break;
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t a_tile = smem_u32(base + kSlotA) + h * (kMmaN * 128);
-      const uint32_t d_tile = deq_base + buf * kDeqBytes;
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = make_idesc(TypeFmt<T>::kFmt, true, false, 128, kMmaN);
+      const uint32_t deq_base = smem_u32(smem + kDeqOff);
+      for (int s = 0; s < S && !fail; ++s) {
+        const int slot = s % kSlots;
+        const int gs = s % kGroupSlots;
+        if (kGrouped && s >= kGroupSlots)
+          fail = !mbar_wait(&tm_empty[gs], ((s / kGroupSlots) - 1) & 1, status, kSiteDecodeMma);
+        for (int h = 0; h < 2 && !fail; ++h) {
+          const int u = 2 * s + h;
+          const int buf = u % kDeqBufs;
+          fail = !mbar_wait(&deq_full[buf], (u / kDeqBufs) & 1, status, kSiteDecodeMma);
+          if (fail) break;
+          tc_fence_after();
+          const uint32_t a_tile = smem_u32(smem + slot * kSlotBytes + kSlotA) + h * (kMmaN * 128);
+          const uint32_t d_tile = deq_base + buf * kDeqBytes;
+          const uint32_t d_tmem = tmem + (kGrouped ? gs * kMmaN : 0);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint64_t adesc = make_smem_desc(d_tile + j * 2048, kDeqLBO, 1024);
-        const uint64_t bdesc = make_smem_desc(a_tile + j * 32, 16, 1024);
-        umma_f16(tmem, adesc, bdesc, kIdesc, (u > 0 || j > 0) ? 1u : 0u);
-      }
-      umma_commit(&mma_done[buf]);
-      if (u == halves - 1) umma_commit(final_bar);
-    }
-  }
-
-  if (!fail) fail = !mbar_wait(final_bar, 0, status, kSiteDecodeFinal);
-  fail = __syncthreads_or(fail) != 0;
-  tc_fence_after();
-
-  if (!fail && warp < 4) {
-    uint32_t raw[16];
-    tmem_ld_32x32b_x16(tmem + (static_cast<uint32_t>(warp * 32) << 16), raw);
-    tmem_ld_wait();
-    const int nl = warp * 32 + lane;
-    const int64_t n = static_cast<int64_t>(tile) * kBN + nl;
-    if (split == 1) {
-#pragma unroll
-      for (int m = 0; m < kMmaN; ++m)
-        if (m < M) store_out(out, out_dtype, m * ldo + n, __uint_as_float(raw[m]) * scalar_scale);
-    } else {
-      float* mine = partials + (static_cast<int64_t>(tile) * split + ks) * M * kBN;
-#pragma unroll
-      for (int m = 0; m < kMmaN; ++m)
-        if (m < M) __stcg(mine + m * kBN + nl, __uint_as_float(raw[m]));
-      __threadfence();
-      named_bar_sync(1, 128);
-      if (tid == 0) s_last = (atomicAdd(&sems[tile], 1u) == static_cast<unsigned>(split - 1));
-      named_bar_sync(1, 128);
-      if (s_last) {
-        __threadfence();
-        const float* tile_parts = partials + static_cast<int64_t>(tile) * split * M * kBN;
-#pragma unroll
-        for (int m = 0; m < kMmaN; ++m) {
-          if (m < M) {
-            float acc = 0.0f;
-            for (int j = 0; j < split; ++j) {
-              const float v = (j == ks) ? __uint_as_float(raw[m])
-                                        : __ldcg(tile_parts + (static_cast<int64_t>(j) * M + m) * kBN + nl);
-              acc += v;
-            }
-            store_out(out, out_dtype, m * ldo + n, acc * scalar_scale);
+          for (int j = 0; j < 4; ++j) {
+            const uint64_t adesc = make_smem_desc(d_tile + j * 2048, kDeqLBO, 1024);
+            const uint64_t bdesc = make_smem_desc(a_tile + j * 32, 16, 1024);
+            const uint32_t acc = kGrouped ? (h | j) : (s | h | j);
+            umma_f16(d_tmem, adesc, bdesc, kIdesc, acc != 0 ? 1u : 0u);
           }
+          umma_commit(&deq_empty[buf]);
         }
-        if (tid == 0) sems[tile] = 0u;  // re-arm for the next call
+        if (fail) break;
+        umma_commit(&slot_empty[slot]);
+        if (kGrouped || s == S - 1) umma_commit(&tm_full[kGrouped ? gs : 0]);
+      }
+    }
+  } else if (warp >= kDeqWarp0) {
+    // ---------------- dequant ----------------
+    const int dt = tid - kDeqWarp0 * 32;
+    const int wq = dt & 3;   // 16-byte quad of the 64-byte packed row: columns 32wq..32wq+31
+    const int r = dt >> 2;   // row within the 64-row half stage
+    const int r8 = r & 7;
+    const uint32_t row_off = (r >> 3) * 1024 + r8 * 128;
+    for (int s = 0; s < S && !fail; ++s) {
+      const int slot = s % kSlots;
+      fail = !mbar_wait(&full[slot], (s / kSlots) & 1, status, kSiteDecodeFull);
+      for (int h = 0; h < 2 && !fail; ++h) {
+        const int u = 2 * s + h;
+        const int buf = u % kDeqBufs;
+        if (u >= kDeqBufs)
+          fail = !mbar_wait(&deq_empty[buf], ((u / kDeqBufs) - 1) & 1, status, kSiteDecodeMma);
+        if (fail) break;
+        const uint4 wv = *reinterpret_cast<const uint4*>(smem + slot * kSlotBytes + kSlotW +
+                                                         (64 * h + r) * 64 + wq * 16);
+        uint8_t* dq = smem + kDeqOff + buf * kDeqBytes + row_off;
+        const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c = 4 * wq + i;  // 8-column chunk 0..15
+          uint32_t o[4];
+          int4_codes8<T>(words[i], o);
+          *reinterpret_cast<uint4*>(dq + (c >> 3) * kDeqLBO + (((c & 7) ^ r8) << 4)) =
+              make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&deq_full[buf]);
       }
     }
   }
 
-  if (fail && tid == 0) {
+  // ---------------- epilogue: per-group scale in fp32 ----------------
+  float acc[kMmaN];
+#pragma unroll
+  for (int m = 0; m < kMmaN; ++m) acc[m] = 0.0f;
+  const int p = tid;  // TMEM lane (epilogue threads only)
+  const int nl = (p & ~7) | int4_codes8_column(p & 7);
+  const int64_t n = static_cast<int64_t>(tile) * kBN + nl;
+  if (warp < kEpiWarps) {
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    if (kGrouped) {
+      const T* sp = scales + static_cast<int64_t>(g_begin) * N + n;
+      float sc_next = S > 0 ? ld_scale(sp) : 0.0f;
+      for (int s = 0; s < S && !fail; ++s) {
+        const float sc = sc_next;
+        if (s + 1 < S) sc_next = ld_scale(sp + static_cast<int64_t>(s + 1) * N);
+        const int gs = s % kGroupSlots;
+        fail = !mbar_wait(&tm_full[gs], (s / kGroupSlots) & 1, status, kSiteDecodeFinal);
+        if (fail) break;
+        tc_fence_after();
+        uint32_t raw[kMmaN];
+        tmem_ld_32x32b_x16(lane_base + gs * kMmaN, raw);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tm_empty[gs]);
+#pragma unroll
+        for (int m = 0; m < kMmaN; ++m) acc[m] = fmaf(sc, __uint_as_float(raw[m]), acc[m]);
+      }
+    } else if (S > 0) {
+      fail = !mbar_wait(&tm_full[0], 0, status, kSiteDecodeFinal);
+      if (!fail) {
+        tc_fence_after();
+        uint32_t raw[kMmaN];
+        tmem_ld_32x32b_x16(lane_base, raw);
+        tmem_ld_wait();
+#pragma unroll
+        for (int m = 0; m < kMmaN; ++m) acc[m] = __uint_as_float(raw[m]);
+      }
+    }
+  }
+
+  // ---------------- split-K reduction and output ----------------
+  fail = __syncthreads_or(fail) != 0;
+  if (use_cluster) {
+    float* red = reinterpret_cast<float*>(smem + kRedOff);
+    if (!fail && warp < kEpiWarps) {
+#pragma unroll
+      for (int m = 0; m < kMmaN; ++m)
+        if (m < M) red[m * kBN + nl] = acc[m];
+    }
+    cluster_sync();
+    if (!fail && warp < kEpiWarps) {
+      const int total = M * kBN;
+      const int lo = (ks * total) / split, hi = ((ks + 1) * total) / split;
+      const uint32_t red_addr = smem_u32(red);
+      for (int e = lo + tid; e < hi; e += kEpiWarps * 32) {
+        float sum = 0.0f;
+        for (int j = 0; j < split; ++j)
+          sum += ld_cluster_f32(cluster_map(red_addr + e * 4, static_cast<uint32_t>(j)));
+        const int m = e / kBN, l = e % kBN;
+        store_out(out, out_dtype, m * ldo + static_cast<int64_t>(tile) * kBN + l,
+                  sum * scalar_scale);
+      }
+    }
+    cluster_sync();  // keep every CTA's shared memory alive until all reads are done
+  } else if (split == 1) {
+    if (!fail && warp < kEpiWarps) {
+#pragma unroll
+      for (int m = 0; m < kMmaN; ++m)
+        if (m < M) store_out(out, out_dtype, m * ldo + n, acc[m] * scalar_scale);
+    }
+  } else if (!fail && warp < kEpiWarps) {
+    float* mine = partials + (static_cast<int64_t>(tile) * split + ks) * M * kBN;
+#pragma unroll
+    for (int m = 0; m < kMmaN; ++m)
+      if (m < M) __stcg(mine + m * kBN + nl, acc[m]);
+    __threadfence();
+    named_bar_sync(1, kEpiWarps * 32);
+    if (tid == 0) *s_flag = (atomicAdd(&sems[tile], 1u) == static_cast<unsigned>(split - 1));
+    named_bar_sync(1, kEpiWarps * 32);
+    if (*s_flag) {
+      __threadfence();
+      const float* tp = partials + static_cast<int64_t>(tile) * split * M * kBN;
+#pragma unroll
+      for (int m = 0; m < kMmaN; ++m) {
+        if (m < M) {
+          float sum = 0.0f;
+          for (int j = 0; j < split; ++j)
+            sum += (j == ks) ? acc[m] : __ldcg(tp + (static_cast<int64_t>(j) * M + m) * kBN + nl);
+          store_out(out, out_dtype, m * ldo + n, sum * scalar_scale);
+        }
+      }
+      if (tid == 0) sems[tile] = 0u;  // re-arm for the next call
+    }
+  }
+
+  if (fail && warp == kTmaWarp && lane == 0) {
     // let copies already issued land before the CTA's shared memory is released
     for (int s = 0; s < issued; ++s) mbar_wait(&full[s % kSlots], (s / kSlots) & 1, nullptr, 0);
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 32);
+  if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
 }
 
 CUtensorMapDataType tmap_type(int dt) {
   return dt == PK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+// Whether a cluster of `split` CTAs of this kernel can be resident (cached per
+// device and split; 0 unknown, 1 yes, 2 no).
+template <typename Kern>
+bool cluster_fits(Kern kernel, int split) {
+  static int cache[64][kMaxClusterSplit + 1] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  int& c = cache[dev][split];
+  if (c == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, split, 1);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 1;
+    attr.val.clusterDim.y = split;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    c = (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) == cudaSuccess && clusters > 0)
+            ? 1
+            : 2;
+    cudaGetLastError();
+  }
+  return c == 1;
 }
 
 }  // namespace
@@ -247,7 +375,7 @@ bool decode_supported(int64_t M, int64_t N, int64_t K, int group, const void* sc
   if (N % kBN != 0 || K % kBK != 0) return false;
   if (scales != nullptr && group != kBK) return false;
   if (lda % 8 != 0 || (reinterpret_cast<uintptr_t>(a) & 15) != 0) return false;
-  if (K > (1ll << 31) || N > (1ll << 31)) return false;
+  if (K > (1ll << 30) || N > (1ll << 30)) return false;
   return true;
 }
 
@@ -258,11 +386,14 @@ int decode_pick_split(int64_t M, int64_t N, int64_t K) {
   const int64_t slots = 2ll * num_sms();  // two CTAs per SM
   int64_t split = slots / (tiles > 0 ? tiles : 1);
   if (split < 1) split = 1;
+  if (split > kMaxClusterSplit) split = kMaxClusterSplit;
   if (split > stages) split = stages;
-  if (split > 32) split = 32;
   return static_cast<int>(split);
 }
 
+// Workspace of the global-memory reduction: arrival counters + fp32 partials.
+// Splits up to 8 normally reduce through distributed shared memory instead
+// and use it only when a cluster launch is unavailable.
 size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int split) {
   (void)K;
   if (split <= 1) return 0;
@@ -272,7 +403,7 @@ size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int split) {
 }
 
 cudaError_t launch_w4a16_decode(const DecodeArgs& p, cudaStream_t s, const char** why) {
-  CUtensorMap tmA, tmW, tmS;
+  CUtensorMap tmA, tmW;
   const CUtensorMapDataType dt = tmap_type(p.a_dtype);
   if (!encode_tmap_2d(&tmA, dt, p.a, p.K, p.M, p.lda * 2, 64, kMmaN,
                       CU_TENSOR_MAP_SWIZZLE_128B, why))
@@ -281,29 +412,56 @@ cudaError_t launch_w4a16_decode(const DecodeArgs& p, cudaStream_t s, const char*
                       kBK, CU_TENSOR_MAP_SWIZZLE_NONE, why))
     return cudaErrorInvalidValue;
   const bool grouped = p.scales != nullptr;
-  if (grouped) {
-    if (!encode_tmap_2d(&tmS, dt, p.scales, p.N, p.K / kBK, p.N * 2, kBN, 1,
-                        CU_TENSOR_MAP_SWIZZLE_NONE, why))
-      return cudaErrorInvalidValue;
-  } else {
-    tmS = tmW;  // unused
-  }
-  dim3 grid(static_cast<unsigned>(p.N / kBN), static_cast<unsigned>(p.split));
-  auto launch = [&](auto kernel) -> cudaError_t {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kSmemBytes);
+
+  auto launch = [&](auto kernel, auto scales_ptr) -> cudaError_t {
+    cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
-    kernel<<<grid, kThreads, kSmemBytes, s>>>(tmA, tmW, tmS, static_cast<int>(p.M),
-                                              static_cast<int>(p.N), static_cast<int>(p.K),
-                                              p.split, p.scalar_scale, p.out, p.out_dtype, p.ldo,
-                                              p.partials, p.sems, p.status);
-    return cudaGetLastError();
+    int use_cluster = 0;
+    if (p.split > 1) {
+      if (p.split <= kMaxClusterSplit && !p.force_workspace && cluster_fits(kernel, p.split)) {
+        use_cluster = 1;
+      } else if (p.partials == nullptr || p.sems == nullptr) {
+        *why = "this split-K launch needs a workspace (cluster reduction unavailable)";
+        return cudaErrorInvalidValue;
+      }
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(p.N / kBN), static_cast<unsigned>(p.split), 1);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attrs[2];
+    int na = 0;
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+    if (use_cluster) {
+      attrs[na].id = cudaLaunchAttributeClusterDimension;
+      attrs[na].val.clusterDim.x = 1;
+      attrs[na].val.clusterDim.y = p.split;
+      attrs[na].val.clusterDim.z = 1;
+      ++na;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, kernel, tmA, tmW, scales_ptr, static_cast<int>(p.M),
+                              static_cast<int>(p.N), static_cast<int>(p.K), p.split, use_cluster,
+                              p.scalar_scale, p.out, p.out_dtype, p.ldo, p.partials, p.sems,
+                              p.status);
   };
-  if (p.a_dtype == PK_BF16)
-    return grouped ? launch(w4a16_decode_kernel<__nv_bfloat16, true>)
-                   : launch(w4a16_decode_kernel<__nv_bfloat16, false>);
-  return grouped ? launch(w4a16_decode_kernel<__half, true>)
-                 : launch(w4a16_decode_kernel<__half, false>);
+  if (p.a_dtype == PK_BF16) {
+    auto sp = static_cast<const __nv_bfloat16*>(p.scales);
+    return grouped ? launch(w4a16_decode_kernel<__nv_bfloat16, true>, sp)
+                   : launch(w4a16_decode_kernel<__nv_bfloat16, false>, sp);
+  }
+  auto sp = static_cast<const __half*>(p.scales);
+  return grouped ? launch(w4a16_decode_kernel<__half, true>, sp)
+                 : launch(w4a16_decode_kernel<__half, false>, sp);
 }
 
+}  // namespace pk
+
+namespace pk {
+int decode_max_cluster_split() { return kMaxClusterSplit; }
 }  // namespace pk
