@@ -40,11 +40,22 @@ METRIC = "W4A16 GEMM µs & HBM GB/s at M=1/16, TFLOPS at M=4096; fp8 GEMM TFLOPS
 L2_BYTES = 126 * 2 ** 20
 
 WORKLOADS = {
+    # HBM-bound decode GEMMs: metric GB/s of algorithmic bytes
     "w4a16_decode_m1": dict(kind="w4a16", M=1, N=4096, K=4096),
     "w4a16_decode_m4": dict(kind="w4a16", M=4, N=4096, K=4096),
     "w4a16_decode_m16": dict(kind="w4a16", M=16, N=4096, K=4096),
+    # tensor-bound prefill GEMM: metric TFLOP/s
+    "w4a16_prefill": dict(kind="w4a16", M=4096, N=11008, K=4096),
+    # scaled e4m3 GEMMs: metric TFLOP/s, cast excluded as upstream
+    "fp8_2048": dict(kind="fp8", M=2048, N=2048, K=2048),
+    "fp8_4096": dict(kind="fp8", M=4096, N=4096, K=4096),
+    "fp8_8192": dict(kind="fp8", M=8192, N=8192, K=8192),
 }
 DEFAULT_WORKLOAD = "w4a16_decode_m1"
+
+
+def is_hbm_bound(wl: dict) -> bool:
+    return wl["kind"] == "w4a16" and wl["M"] <= 16
 
 
 # ---------------------------------------------------------------------------
@@ -165,29 +176,109 @@ def barrier(dist):
 
 
 # ---------------------------------------------------------------------------
-# W4A16 workload
+# workloads: device buffers, one step through the C ABI, algorithmic work
 # ---------------------------------------------------------------------------
-def w4a16_bytes(M: int, N: int, K: int) -> int:
-    """Algorithmic bytes of one GEMM: packed weights + bf16 scales + bf16 A + fp32 Y."""
-    return K * N // 2 + (K // 128) * N * 2 + M * K * 2 + M * N * 4
+class Workload:
+    """Rotating input sets (so each step's inputs are not L2-resident) and the
+    step that runs one GEMM on set i through the C ABI."""
+
+    def __init__(self, name: str, wl: dict, device: torch.device, split_k: int):
+        from pico_kernels_b200 import _lib
+        self.name, self.wl, self.device = name, wl, device
+        self.lib = _lib.load()
+        self._lib = _lib
+        self.M, self.N, self.K = wl["M"], wl["N"], wl["K"]
+        self.kind = wl["kind"]
+        self.split_k = split_k
+        self.hbm = is_hbm_bound(wl)
+        M, N, K = self.M, self.N, self.K
+        if self.kind == "w4a16":
+            per_set = K * N // 2 + (K // 128) * N * 2 + M * K * 2
+        else:
+            per_set = M * K + K * N
+        self.n_sets = max(2, int(2 * L2_BYTES // per_set) + 1)
+        self.set_bytes = per_set
+        g = torch.Generator(device=device).manual_seed(0)
+        self.sets = []
+        import pico_kernels_b200 as pk
+        from pico_kernels_b200 import gemm_fp8
+        for _ in range(self.n_sets):
+            if self.kind == "w4a16":
+                w = (torch.randn(K, N, device=device, generator=g) * 0.02).to(torch.bfloat16)
+                packed, scales = pk.quantize_int4_grouped(w, 128)
+                del w
+                a = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
+                self.sets.append((a, packed, scales))
+            else:
+                a8, sa = gemm_fp8.quantize(torch.randn(M, K, device=device, generator=g).to(torch.bfloat16))
+                b8, sb = gemm_fp8.quantize(torch.randn(K, N, device=device, generator=g).to(torch.bfloat16))
+                self.sets.append((a8, b8, 1.0 / (sa * sb)))
+        # decode outputs are tiny: one per set; large outputs share one buffer
+        n_out = self.n_sets if self.hbm else 1
+        self.outs = [torch.empty((M, N), dtype=torch.float32, device=device) for _ in range(n_out)]
+        self.ws_bytes = (self.lib.pk_w4a16_workspace_size(M, N, K, split_k)
+                         if self.kind == "w4a16" else 0)
+        self.ws = _lib.workspace(device, self.ws_bytes, tag="bench")
+        torch.cuda.synchronize()
+
+    def step(self, i: int) -> None:
+        lib, L, M, N, K = self.lib, self._lib, self.M, self.N, self.K
+        stream = torch.cuda.current_stream().cuda_stream
+        out = self.outs[i % len(self.outs)]
+        if self.kind == "w4a16":
+            a, packed, scales = self.sets[i]
+            st = lib.pk_w4a16_gemm(a.data_ptr(), L.PK_BF16, K, packed.data_ptr(), scales.data_ptr(),
+                                   1.0, 128, M, N, K, out.data_ptr(), L.PK_F32, N, self.split_k,
+                                   L.ptr(self.ws), self.ws_bytes, stream)
+        else:
+            a8, b8, out_scale = self.sets[i]
+            st = lib.pk_fp8_gemm(a8.data_ptr(), b8.data_ptr(), M, N, K, out_scale, out.data_ptr(),
+                                 L.PK_F32, stream)
+        L.check(st, self.name)
+
+    # algorithmic work of one step
+    def bytes_per_step(self) -> int:
+        M, N, K = self.M, self.N, self.K
+        if self.kind == "w4a16":
+            return K * N // 2 + (K // 128) * N * 2 + M * K * 2 + M * N * 4
+        return M * K + K * N + M * N * 4
+
+    def flops_per_step(self) -> int:
+        return 2 * self.M * self.N * self.K
+
+    def e2e_step_fn(self):
+        """Public-API step with host buffers: H2D of the activations, D2H of Y."""
+        import pico_kernels_b200 as pk
+        from pico_kernels_b200 import gemm_fp8
+        M, N, K = self.M, self.N, self.K
+        if self.kind == "w4a16":
+            a_host = torch.empty((M, K), dtype=torch.bfloat16).pin_memory()
+            a_host.copy_(self.sets[0][0])
+            a_dev = torch.empty((M, K), dtype=torch.bfloat16, device=self.device)
+            y_host = torch.empty((M, N), dtype=torch.float32).pin_memory()
+
+            def fn(i):
+                _, packed, scales = self.sets[i % self.n_sets]
+                a_dev.copy_(a_host, non_blocking=True)
+                y = pk.int4_gemm(a_dev, packed, scales)
+                y_host.copy_(y, non_blocking=True)
+            return fn, M * K * 2, M * N * 4
+        a8_host = torch.empty((M, K), dtype=torch.uint8).pin_memory()
+        a8_host.copy_(self.sets[0][0].view(torch.uint8))
+        a8_dev = torch.empty((M, K), dtype=torch.float8_e4m3fn, device=self.device)
+        y_host = torch.empty((M, N), dtype=torch.float32).pin_memory()
+
+        def fn(i):
+            _, b8, out_scale = self.sets[i % self.n_sets]
+            a8_dev.view(torch.uint8).copy_(a8_host, non_blocking=True)
+            y = gemm_fp8.fp8_gemm_precast(a8_dev, 1.0, b8, 1.0 / out_scale)
+            y_host.copy_(y, non_blocking=True)
+        return fn, M * K, M * N * 4
 
 
-def make_w4a16_sets(M, N, K, n_sets, device, seed=0):
-    import pico_kernels_b200 as pk
-    g = torch.Generator(device=device).manual_seed(seed)
-    sets = []
-    for i in range(n_sets):
-        w = (torch.randn(K, N, device=device, generator=g) * 0.02).to(torch.bfloat16)
-        packed, scales = pk.quantize_int4_grouped(w, 128)
-        a = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
-        sets.append((a, packed, scales))
-        del w
-    torch.cuda.synchronize()
-    return sets
-
-
-def time_graph_steps(step_fn, n_sets: int, steps: int, chunk: int = 1000):
-    """Capture `step_fn(i)` for i in a chunk into graphs; return (run(K), n_graph_steps)."""
+def capture_runner(step_fn, n_sets: int, steps: int, chunk: int = 1000):
+    """CUDA graphs of `chunk` consecutive steps (cycling the input sets); returns
+    (graph, replays, remainder_graph) covering exactly `steps` steps."""
     chunk = max(1, min(chunk, steps))
     graphs = {}
 
@@ -197,7 +288,7 @@ def time_graph_steps(step_fn, n_sets: int, steps: int, chunk: int = 1000):
             s = torch.cuda.Stream()
             s.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(s):
-                step_fn(0)  # make sure lazily created buffers exist outside capture
+                step_fn(0)  # lazily created state exists before capture
                 torch.cuda.synchronize()
                 with torch.cuda.graph(g, stream=s):
                     for i in range(n):
@@ -206,49 +297,27 @@ def time_graph_steps(step_fn, n_sets: int, steps: int, chunk: int = 1000):
             graphs[n] = g
         return graphs[n]
 
-    def run(k):
-        full, rem = divmod(k, chunk)
-        gfull = graph_for(chunk) if full else None
-        grem = graph_for(rem) if rem else None
-        return gfull, full, grem
-
-    return run
+    full, rem = divmod(steps, chunk)
+    return (graph_for(chunk) if full else None), full, (graph_for(rem) if rem else None)
 
 
 def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
     import pico_kernels_b200 as pk
-    from pico_kernels_b200 import _lib
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     dist = init_dist(world, local)
     peaks = load_peaks()
-    M, N, K = wl["M"], wl["N"], wl["K"]
-    per_step = w4a16_bytes(M, N, K)
-    n_sets = max(4, int(2 * L2_BYTES // (K * N // 2 + (K // 128) * N * 2)) + 1)
-    sets = make_w4a16_sets(M, N, K, n_sets, device)
-    outs = [torch.empty((M, N), dtype=torch.float32, device=device) for _ in range(n_sets)]
-    lib = _lib.load()
-    split = args.split_k
-    ws_bytes = lib.pk_w4a16_workspace_size(M, N, K, split)
-    ws = _lib.workspace(device, ws_bytes, tag="bench")
+    work = Workload(args.workload, wl, device, args.split_k)
     sms = torch.cuda.get_device_properties(device).multi_processor_count
+    chunk = 1000 if work.hbm else 20
 
-    def step(i):
-        a, packed, scales = sets[i]
-        _lib.check(lib.pk_w4a16_gemm(a.data_ptr(), _lib.PK_BF16, K, packed.data_ptr(),
-                                     scales.data_ptr(), 1.0, 128, M, N, K, outs[i].data_ptr(),
-                                     _lib.PK_F32, N, split, _lib.ptr(ws), ws_bytes,
-                                     torch.cuda.current_stream().cuda_stream), "w4a16")
-
-    runner = time_graph_steps(step, n_sets, args.steps)
-    # warm-up: W steps through the same graphs
-    gw, nw, gwr = runner(args.warmup)
+    gw, nw, gwr = capture_runner(work.step, work.n_sets, args.warmup, chunk)
     for _ in range(nw):
         gw.replay()
     if gwr is not None:
         gwr.replay()
-    gfull, nfull, grem = runner(args.steps)
+    gfull, nfull, grem = capture_runner(work.step, work.n_sets, args.steps, chunk)
     torch.cuda.synchronize()
 
     clocks = ClockSampler(local)
@@ -274,28 +343,17 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
     if code != 0:
         raise RuntimeError(f"device status {code} at site {where}")
 
-    # end-to-end through the public API: pinned host A in, fp32 Y out, every step
-    e2e_steps = min(args.steps, args.e2e_steps)
-    a_host = [torch.empty((M, K), dtype=torch.bfloat16).pin_memory() for _ in range(4)]
-    y_host = [torch.empty((M, N), dtype=torch.float32).pin_memory() for _ in range(4)]
-    for h, (a, _, _) in zip(a_host, sets):
-        h.copy_(a)
-    a_dev = torch.empty((M, K), dtype=torch.bfloat16, device=device)
-
-    def e2e_step(i):
-        _, packed, scales = sets[i % n_sets]
-        a_dev.copy_(a_host[i % 4], non_blocking=True)
-        y = pk.int4_gemm(a_dev, packed, scales)
-        y_host[i % 4].copy_(y, non_blocking=True)
-
-    for i in range(max(3, args.warmup // 100)):
-        e2e_step(i)
+    # end to end through the public API, host buffers in and out every step
+    e2e_fn, h2d, d2h = work.e2e_step_fn()
+    e2e_steps = min(args.steps, args.e2e_steps if work.hbm else max(3, args.e2e_steps // 100))
+    for i in range(3):
+        e2e_fn(i)
     torch.cuda.synchronize()
     barrier(dist)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(e2e_steps):
-        e2e_step(i)
+        e2e_fn(i)
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(dist, e0.elapsed_time(e1))
@@ -305,55 +363,78 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
             dist.destroy_process_group()
         return
 
-    ms_per_step = ms_max / args.steps
-    value = world * per_step * args.steps / (ms_max * 1e-3) / 1e9
-    achieved = per_step / (ms / args.steps * 1e-3) / 1e9
-    e2e_value = world * per_step * e2e_steps / (e2e_ms * 1e-3) / 1e9
+    sec = ms_max * 1e-3
+    sec_per_step_local = ms * 1e-3 / args.steps
+    if work.hbm:
+        per = work.bytes_per_step()
+        unit, scale = "GB/s", 1e9
+        peak, bound, punit = peaks["hbm_gbs"], "hbm", "GB/s"
+        peak_note = peaks["source"]
+    else:
+        per = work.flops_per_step()
+        unit, scale = "TFLOP/s", 1e12
+        long_region = sec > 1.0
+        bf16 = peaks["bf16_tflops_sustained"] if long_region else peaks["bf16_tflops"]
+        if work.kind == "fp8":
+            peak = 2.0 * bf16
+            peak_note = f"2x {'sustained' if long_region else 'burst'} bf16 ({peaks['source']}); no fp8 peak measured"
+        else:
+            peak = bf16
+            peak_note = f"{'sustained' if long_region else 'burst'} bf16 ({peaks['source']})"
+        bound, punit = "tensor", "TFLOP/s"
+    value = world * per * args.steps / sec / scale
+    achieved = per / sec_per_step_local / scale
+    e2e_value = world * per * e2e_steps / (e2e_ms * 1e-3) / scale
+    wl_cfg = {"workload": args.workload, "M": work.M, "N": work.N, "K": work.K}
+    if work.kind == "w4a16":
+        wl_cfg.update({"group_size": 128, "weights": "int4 packed [K, N/2] + bf16 scales [K/128, N]",
+                       "activations": "bf16", "output": "fp32",
+                       "split_k": args.split_k if args.split_k > 0 else "auto"})
+    else:
+        wl_cfg.update({"inputs": "e4m3 [M,K] x e4m3 [K,N], per-tensor scales", "output": "fp32",
+                       "cast": "excluded from the timed region (gemm_fp8.py:144)"})
+    wl_cfg.update({
+        "l2": f"{work.n_sets} rotating input sets ({work.n_sets * work.set_bytes / 2**20:.0f} MiB > 126 MiB L2)",
+        "launch": "CUDA graphs of back-to-back GEMMs",
+        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+    })
     line = {
         "metric": METRIC,
-        "value": round(value, 2),
-        "unit": "GB/s",
+        "value": round(value, 3),
+        "unit": unit,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": ms_per_step,
-        "us_per_gemm": round(ms_per_step * 1e3, 4),
+        "ms_per_step": ms_max / args.steps,
+        "us_per_gemm": round(ms_max / args.steps * 1e3, 4),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16",
+        "dtype": "bf16" if work.kind == "w4a16" else "e4m3",
         "data": "synthetic (seeded N(0,0.02) weights quantized on device, N(0,1) activations)",
-        "config": {
-            "workload": args.workload, "M": M, "N": N, "K": K, "group_size": 128,
-            "weights": "int4 packed [K, N/2] + bf16 scales [K/128, N]",
-            "activations": "bf16", "output": "fp32",
-            "split_k": split if split > 0 else "auto",
-            "l2": f"{n_sets} rotating weight sets ({n_sets * (K * N // 2 + K // 128 * N * 2) / 2**20:.0f} MiB > 126 MiB L2)",
-            "launch": "CUDA graphs of back-to-back GEMMs",
-            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-        },
+        "config": wl_cfg,
         "roofline": {
-            "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
-            "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-            "peak_source": peaks["source"], "traffic": args.traffic,
-            "algorithmic_bytes_per_launch": per_step, "sms": sms,
+            "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": punit,
+            "frac": round(achieved / peak, 4), "peak_source": peak_note, "traffic": args.traffic,
+            ("algorithmic_bytes_per_launch" if work.hbm else "algorithmic_flops_per_launch"): per,
+            "sms": sms,
         },
-        "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
-                "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 4,
-                "steps": e2e_steps, "us_per_step": round(e2e_ms / e2e_steps * 1e3, 3),
-                "path": "pico_kernels_b200.int4_gemm (ctypes C ABI) with pinned host buffers"},
+        "e2e": {"value": round(e2e_value, 4), "unit": unit, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "us_per_step": round(e2e_ms / e2e_steps * 1e3, 3),
+                "path": "pico_kernels_b200 public API (ctypes C ABI), pinned host buffers"},
         "gpu_launches": args.steps,
         "clocks": clocks.summary(t0, t1),
     }
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(M, N, K, budget_s=args.cpu_seconds)
+        line["cpu_baseline"] = cpu_baseline(wl, budget_s=args.cpu_seconds)
     print(json.dumps(line), flush=True)
     if dist is not None:
         dist.destroy_process_group()
 
 
 # ---------------------------------------------------------------------------
-# CPU reference path (oracle restatement of the reference's torch CPU path)
+# CPU reference path (the oracle's restatement of the reference's torch path)
 # ---------------------------------------------------------------------------
 def _cpu_threads() -> int:
     try:
@@ -364,47 +445,80 @@ def _cpu_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_baseline(M: int, N: int, K: int, budget_s: float = 10.0) -> dict:
-    """Time unpack + dequantize + fp32 matmul per step on the host (numpy)."""
+def cpu_baseline(wl: dict, budget_s: float = 10.0) -> dict:
+    """Time the reference's CPU path on a bounded sample of the workload.
+
+    W4A16: unpack + dequantize + fp32 matmul (tests/test_gemm_int4.py:26);
+    fp8: (a8.float()/sa) @ (b8.float()/sb) (gemm_fp8.py:132). Large GEMMs are
+    sampled by output rows; the rate is scaled to the full step's unit.
+    """
     from oracle import quant_ref as o
+    M, N, K = wl["M"], wl["N"], wl["K"]
     rng = np.random.default_rng(0)
-    w = (rng.standard_normal((K, N), dtype=np.float32) * 0.02)
-    codes, s32 = o.group_quant_codes(w, 128)
-    packed = o.pack_int4_n(codes)
-    scales = o.store_scales(s32, "bf16")
-    a = o.round_to_bf16(rng.standard_normal((M, K), dtype=np.float32))
-    per_step = w4a16_bytes(M, N, K)
+    rows = M if M <= 16 else max(16, min(M, int(2e9 // (2 * N * K)) or 16))
+    if wl["kind"] == "w4a16":
+        w = rng.standard_normal((K, N), dtype=np.float32) * 0.02
+        codes, s32 = o.group_quant_codes(w, 128)
+        packed = o.pack_int4_n(codes)
+        scales = o.store_scales(s32, "bf16")
+        a = o.round_to_bf16(rng.standard_normal((rows, K), dtype=np.float32))
+
+        def once():  # per step: unpack + dequantize the weights
+            return o.dequant_weight(o.unpack_int4_n(packed), scales, 128)
+
+        def per_rows(wd):  # fp32 matmul of `rows` activation rows
+            return a @ wd
+    else:
+        a8, sa = o.fp8_quantize(rng.standard_normal((rows, K), dtype=np.float32), "bf16")
+        b8, sb = o.fp8_quantize(rng.standard_normal((K, N), dtype=np.float32), "bf16")
+
+        def once():
+            return o.e4m3_bits_to_f32(b8) / np.float32(sb)
+
+        def per_rows(bd):
+            return (o.e4m3_bits_to_f32(a8) / np.float32(sa)) @ bd
     n = 0
+    t_once = t_rows = 0.0
     t0 = time.perf_counter()
     while True:
-        q = o.unpack_int4_n(packed)
-        o.w4a16_reference(a, q, scales, 128)
+        ta = time.perf_counter()
+        wd = once()
+        tb = time.perf_counter()
+        per_rows(wd)
+        tc = time.perf_counter()
+        t_once += tb - ta
+        t_rows += tc - tb
         n += 1
-        el = time.perf_counter() - t0
+        el = tc - t0
         if el >= budget_s and n >= 2:
             break
-    return {"value": round(per_step * n / el / 1e9, 5), "unit": "GB/s",
-            "cores": _cpu_threads(), "kind": "port",
-            "sample": f"{n} steps of unpack+dequant+fp32 matmul, M={M} N={N} K={K}, {el:.1f} s",
-            "ms_per_step": round(el / n * 1e3, 3)}
+    # one full step = one dequant + the matmul over all M rows
+    sec_per_step = t_once / n + (t_rows / n) * (M / rows)
+    hbm = is_hbm_bound(wl)
+    if hbm:
+        per = K * N // 2 + (K // 128) * N * 2 + M * K * 2 + M * N * 4
+        value, unit = per / sec_per_step / 1e9, "GB/s"
+    else:
+        value, unit = 2 * M * N * K / sec_per_step / 1e12, "TFLOP/s"
+    return {"value": round(value, 6), "unit": unit, "cores": _cpu_threads(), "kind": "port",
+            "sample": f"{n} repetitions of (weight dequant + matmul of {rows} of {M} rows), "
+                      f"M={M} N={N} K={K}, {el:.1f} s, scaled to all rows; numpy restatement "
+                      f"of the reference's torch CPU path",
+            "ms_per_step": round(sec_per_step * 1e3, 3)}
 
 
 def run_reference(args, wl: dict, world: int, rank: int) -> None:
     if rank != 0:
         return
-    M, N, K = wl["M"], wl["N"], wl["K"]
-    steps = args.steps
-    # each step is a bounded sample: the CPU path is ~1e4x slower than the GPU
-    budget = args.cpu_seconds
-    base = cpu_baseline(M, N, K, budget_s=budget)
+    base = cpu_baseline(wl, budget_s=args.cpu_seconds)
     line = {
-        "metric": METRIC, "value": base["value"], "unit": "GB/s", "n_gpus": world,
-        "steps": steps, "warmup": args.warmup, "ms_per_step": base["ms_per_step"],
+        "metric": METRIC, "value": base["value"], "unit": base["unit"], "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": base["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "impl": "reference",
-        "config": {"workload": args.workload, "M": M, "N": N, "K": K, "group_size": 128},
+        "config": {"workload": args.workload, "M": wl["M"], "N": wl["N"], "K": wl["K"]},
         "cpu_baseline": base,
-        "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+        "e2e": {"value": base["value"], "unit": base["unit"], "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -413,8 +527,9 @@ def run_reference(args, wl: dict, world: int, rank: int) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100000)
-    ap.add_argument("--warmup", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: 100000 for decode, 200 otherwise)")
+    ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--split-k", type=int, default=0)
@@ -424,10 +539,15 @@ def main() -> None:
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per launch from an ncu capture, reported as-is")
     args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    hbm = is_hbm_bound(wl)
+    if args.steps is None:
+        args.steps = 100000 if hbm else 200
+    if args.warmup is None:
+        args.warmup = 2000 if hbm else 20
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     world, rank, local = dist_env()
-    wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         run_reference(args, wl, world, rank)
     else:

@@ -271,6 +271,40 @@ int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t* wp, co
     return PK_OK;
   }
 
+  // Tensor-core prefill path: 64-row K stages, scales on 64-row boundaries.
+  const bool prefill_ok = (K % 64) == 0 && (N % 32) == 0 && (lda % 8) == 0 &&
+                          (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
+                          (reinterpret_cast<uintptr_t>(wp) & 15) == 0 &&
+                          (scales == nullptr || ((group_size % 64) == 0 &&
+                                                 (reinterpret_cast<uintptr_t>(scales) & 15) == 0)) &&
+                          M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31);
+  if (prefill_ok) {
+    GemmArgs g{};
+    g.kind = GemmArgs::kW4A16;
+    g.a = a;
+    g.a_dtype = a_dtype;
+    g.lda = lda;
+    g.b = wp;
+    g.ldb = N / 2;
+    g.scales = scales;
+    g.group = group_size;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.split = 1;
+    g.out = out;
+    g.out_dtype = out_dtype;
+    g.ldc = ldo;
+    g.out_scale = scales ? 1.0f : scalar_scale;
+    g.status = device_status_ptr();
+    const char* why = "";
+    cudaError_t e = launch_gemm_tc(g, s, &why);
+    if (e == cudaErrorInvalidValue && why[0] != '\0') return fail(PK_ERR_ALIGN, "%s", why);
+    if (e != cudaSuccess) return cuda_fail(e, "w4a16 prefill launch");
+    ok();
+    return PK_OK;
+  }
+
   cudaError_t e = launch_w4a16_simt(a, a_dtype, lda, wp, scales, scalar_scale, group_size, M, N,
                                     K, out, out_dtype, ldo, s);
   if (e != cudaSuccess) return cuda_fail(e, "w4a16 simt launch");
@@ -291,22 +325,94 @@ int pk_fp8_quantize(const void* x, int dtype, int64_t n, float scale, uint8_t* x
 
 int pk_fp8_gemm(const uint8_t* a8, const uint8_t* b8, int64_t M, int64_t N, int64_t K,
                 float out_scale, void* out, int out_dtype, void* stream) {
-  (void)a8; (void)b8; (void)M; (void)N; (void)K; (void)out_scale; (void)out; (void)out_dtype;
-  (void)stream;
-  return fail(PK_ERR_UNSUPPORTED, "pk_fp8_gemm is not built yet");
+  if (!a8 || !b8 || !out) return fail(PK_ERR_SHAPE, "null pointer");
+  if (M <= 0 || N <= 0 || K <= 0) return fail(PK_ERR_SHAPE, "need M, N, K > 0");
+  if ((K % 16) != 0 || (N % 16) != 0)
+    return fail(PK_ERR_SHAPE, "fp8 GEMM needs K and N multiples of 16 (16-byte TMA rows)");
+  if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31))
+    return fail(PK_ERR_SHAPE, "dimension too large");
+  if (out_dtype != PK_F32 && out_dtype != PK_BF16)
+    return fail(PK_ERR_DTYPE, "output must be f32 or bf16");
+  if ((reinterpret_cast<uintptr_t>(a8) & 15) || (reinterpret_cast<uintptr_t>(b8) & 15))
+    return fail(PK_ERR_ALIGN, "fp8 operands must be 16-byte aligned");
+  GemmArgs g{};
+  g.kind = GemmArgs::kFp8;
+  g.a = a8;
+  g.a_dtype = PK_E4M3;
+  g.lda = K;
+  g.b = b8;
+  g.ldb = N;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.split = 1;
+  g.out = out;
+  g.out_dtype = out_dtype;
+  g.ldc = N;
+  g.out_scale = out_scale;
+  g.status = device_status_ptr();
+  const char* why = "";
+  cudaError_t e = launch_gemm_tc(g, as_stream(stream), &why);
+  if (e == cudaErrorInvalidValue && why[0] != '\0') return fail(PK_ERR_ALIGN, "%s", why);
+  if (e != cudaSuccess) return cuda_fail(e, "fp8 GEMM launch");
+  ok();
+  return PK_OK;
 }
 
 size_t pk_gemm_splitk_workspace_size(int64_t M, int64_t N, int64_t K, int split_k) {
-  (void)M; (void)N; (void)K; (void)split_k;
-  return 0;
+  (void)K;
+  if (M <= 0 || N <= 0 || split_k <= 1) return 0;
+  return gemm_splitk_workspace_bytes(M, N, split_k);
 }
 
 int pk_gemm_splitk(const void* a, const void* b, int dtype, int64_t M, int64_t N, int64_t K,
                    int split_k, float* out, void* workspace, size_t workspace_bytes,
                    void* stream) {
-  (void)a; (void)b; (void)dtype; (void)M; (void)N; (void)K; (void)split_k; (void)out;
-  (void)workspace; (void)workspace_bytes; (void)stream;
-  return fail(PK_ERR_UNSUPPORTED, "pk_gemm_splitk is not built yet");
+  if (!a || !b || !out) return fail(PK_ERR_SHAPE, "null pointer");
+  if (M <= 0 || N <= 0 || K <= 0) return fail(PK_ERR_SHAPE, "need M, N, K > 0");
+  if (!is16(dtype)) return fail(PK_ERR_DTYPE, "split-K GEMM inputs must be f16 or bf16");
+  if ((K % 8) != 0 || (N % 8) != 0)
+    return fail(PK_ERR_SHAPE, "split-K GEMM needs K and N multiples of 8 (16-byte TMA rows)");
+  if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31))
+    return fail(PK_ERR_SHAPE, "dimension too large");
+  if (split_k < 1 || split_k > (K + 63) / 64)
+    return fail(PK_ERR_SHAPE, "split_k must be in [1, ceil(K/64)] (got %d)", split_k);
+  if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15))
+    return fail(PK_ERR_ALIGN, "operands must be 16-byte aligned");
+  GemmArgs g{};
+  g.kind = GemmArgs::kDense16;
+  g.a = a;
+  g.a_dtype = dtype;
+  g.lda = K;
+  g.b = b;
+  g.ldb = N;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.split = split_k;
+  g.out = out;
+  g.out_dtype = PK_F32;
+  g.ldc = N;
+  g.out_scale = 1.0f;
+  g.status = device_status_ptr();
+  if (split_k > 1) {
+    const size_t need = gemm_splitk_workspace_bytes(M, N, split_k);
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail(PK_ERR_WORKSPACE, "split-K needs %zu workspace bytes, got %zu", need,
+                  workspace_bytes);
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+      return fail(PK_ERR_ALIGN, "workspace must be 256-byte aligned");
+    const int64_t tiles = gemm_tiles(M, N);
+    const size_t sem_bytes = ((tiles * sizeof(unsigned) + 255) / 256) * 256;
+    g.sems = static_cast<unsigned*>(workspace);
+    g.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + sem_bytes);
+  }
+  const char* why = "";
+  cudaError_t e = launch_gemm_tc(g, as_stream(stream), &why);
+  if (e == cudaErrorInvalidValue && why[0] != '\0') return fail(PK_ERR_ALIGN, "%s", why);
+  if (e != cudaSuccess) return cuda_fail(e, "split-K GEMM launch");
+  ok();
+  return PK_OK;
 }
 
 }  // extern "C"

@@ -1,0 +1,484 @@
+// Persistent tcgen05 GEMM for sm_100a: C[M, N] = A[M, K] @ B[K, N].
+//
+// One CTA per SM walks output tiles of 128 x 256 (grouped raster for L2
+// reuse). Operands are staged by TMA into 128B-swizzled shared-memory tiles:
+// A K-major (row-major [M, K]), B MN-major (row-major [K, N], read by the
+// tensor core through the descriptor's MN-major mode, so no transpose pass).
+// The fp32 accumulator lives in TMEM, double-buffered (2 x 256 columns) so
+// the epilogue of one tile overlaps the main loop of the next.
+//
+// Used by three entry points:
+//   * fp8 (e4m3 x e4m3, kind::f8f6f4, K = 32 per MMA), epilogue x out_scale
+//     -- gemm_fp8.fp8_gemm_kernel (gemm_fp8.py:38-86);
+//   * dense fp16/bf16 (kind::f16) with an optional deterministic split-K
+//     -- gemm_splitk.gemm_splitk_kernel (gemm_splitk.py:26-64);
+//   * W4A16 prefill: B is produced in shared memory by dequant warps from the
+//     packed int4 weights and group scales (q * s rounded to A's dtype)
+//     -- gemm_int4.int4_gemm_kernel (gemm_int4.py:21-55).
+//
+// Warp roles: 0 TMA producer, 1 MMA issuer (+ TMEM owner), 2-5 epilogue
+// (TMEM lanes 0-127), 6-13 dequant (int4 only).
+#include "pk_common.cuh"
+
+namespace pk {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kTmaWarp = 0, kMmaWarp = 1, kEpiWarp0 = 2, kEpiWarps = 4, kDeqWarp0 = 6;
+constexpr int kDeqWarps = 8;
+constexpr int kGroupM = 8;
+
+enum Kind { kF16 = 0, kF8 = 1 };
+
+template <int kKind, bool kInt4>
+struct Cfg {
+  static constexpr int kElem = kKind == kF16 ? 2 : 1;       // bytes per A/B element
+  static constexpr int kBK = 128 / kElem;                    // one 128-byte swizzle row of K
+  static constexpr int kMmaK = kKind == kF16 ? 16 : 32;
+  static constexpr int kKSteps = kBK / kMmaK;                // 4
+  static constexpr int kATile = kBM * 128;                   // 16 KB
+  static constexpr int kBTile = kBK * kBN * kElem;           // 32 KB
+  static constexpr int kBAtomN = 128 / kElem;                // N per MN-major swizzle atom
+  static constexpr int kBBoxes = kBN / kBAtomN;              // TMA boxes per B tile
+  static constexpr int kBLBO = kBK * 128;                    // bytes between N atoms
+  static constexpr int kBStepBytes = (kMmaK / 8) * 1024;     // B advance per MMA K step
+  // int4: packed weights (kBK rows x 128 B) + one row of group scales per stage
+  static constexpr int kWTile = kInt4 ? kBK * (kBN / 2) : 0;  // 8 KB
+  static constexpr int kSTile = kInt4 ? kBN * 2 : 0;          // 512 B
+  static constexpr int kStages = kInt4 ? 4 : 4;
+  static constexpr int kBBufs = kInt4 ? 2 : 0;                // dequantized B ring
+  static constexpr int kStageBytes = kATile + (kInt4 ? kWTile + 1024 : kBTile);
+  static constexpr int kStageOff = 0;
+  static constexpr int kBBufOff = kStages * kStageBytes;
+  static constexpr int kBarOff = kBBufOff + kBBufs * kBTile;
+  static constexpr int kSmem = kBarOff + 256 + 1024;
+  static constexpr int kThreads = (kInt4 ? kDeqWarp0 + kDeqWarps : kDeqWarp0) * 32;
+  static constexpr uint32_t kIdesc =
+      make_idesc(kKind == kF16 ? 1u : 0u, false, true, kBM, kBN);  // bf16 / e4m3
+  static constexpr uint32_t kIdescF16 = make_idesc(0u, false, true, kBM, kBN);
+};
+
+struct Params {
+  int M, N, K;
+  int split;             // K splits (dense split-K); 1 otherwise
+  int num_m, num_n;      // tiles
+  int out_dtype;         // PK_F32 / PK_BF16
+  int64_t ldc;
+  float out_scale;
+  void* out;
+  float* partials;       // split-K workspace
+  unsigned* sems;
+  const void* scales;    // int4: [G, N] (A's dtype)
+  int group;             // int4 group size
+  int grouped;           // int4: 1 = group scales in the dequant, 0 = scalar out_scale
+  int a_is_f16;          // 16-bit kinds: A dtype is fp16 (else bf16)
+  int* status;
+};
+
+__device__ __forceinline__ void tile_coords(int t, const Params& p, int& tm, int& tn, int& ks) {
+  ks = t % p.split;
+  t /= p.split;
+  const int per_group = kGroupM * p.num_n;
+  const int g = t / per_group;
+  const int first_m = g * kGroupM;
+  const int gm = min(p.num_m - first_m, kGroupM);
+  tm = first_m + (t % per_group) % gm;
+  tn = (t % per_group) / gm;
+}
+
+__device__ __forceinline__ void store8(void* out, int out_dtype, int64_t idx, const float* v,
+                                       bool full, int valid) {
+  if (out_dtype == PK_BF16) {
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + idx;
+    if (full && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+      uint4 u;
+      __nv_bfloat162 t0 = __floats2bfloat162_rn(v[0], v[1]);
+      __nv_bfloat162 t1 = __floats2bfloat162_rn(v[2], v[3]);
+      __nv_bfloat162 t2 = __floats2bfloat162_rn(v[4], v[5]);
+      __nv_bfloat162 t3 = __floats2bfloat162_rn(v[6], v[7]);
+      u.x = *reinterpret_cast<uint32_t*>(&t0);
+      u.y = *reinterpret_cast<uint32_t*>(&t1);
+      u.z = *reinterpret_cast<uint32_t*>(&t2);
+      u.w = *reinterpret_cast<uint32_t*>(&t3);
+      *reinterpret_cast<uint4*>(o) = u;
+    } else {
+      for (int i = 0; i < valid; ++i) o[i] = __float2bfloat16_rn(v[i]);
+    }
+  } else {
+    float* o = static_cast<float*>(out) + idx;
+    if (full && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+      reinterpret_cast<float4*>(o)[0] = make_float4(v[0], v[1], v[2], v[3]);
+      reinterpret_cast<float4*>(o)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+      for (int i = 0; i < valid; ++i) o[i] = v[i];
+    }
+  }
+}
+
+template <int kKind, bool kInt4>
+__global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmS, const Params p) {
+  using C = Cfg<kKind, kInt4>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* bfull = acc_empty + 2;
+  uint64_t* bempty = bfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bempty + 2);
+  int* s_flag = reinterpret_cast<int*>(tmem_holder + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int k_tiles_total = (p.K + C::kBK - 1) / C::kBK;
+  const int num_units = p.num_m * p.num_n * p.split;
+
+  if (warp == kTmaWarp && lane == 0) {
+    for (int i = 0; i < C::kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kInt4 ? 1 + kDeqWarps : 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kEpiWarps);
+      mbar_init(&bfull[i], kDeqWarps);
+      mbar_init(&bempty[i], 1);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (kInt4) tma_prefetch_desc(&tmS);
+  }
+  if (warp == kMmaWarp) tmem_alloc(tmem_holder, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  griddep_wait();
+
+  bool fail = false;
+  if (warp == kTmaWarp) {
+    // ------------------------------- producer -------------------------------
+    if (lane == 0) {
+      int it = 0;
+      for (int u = blockIdx.x; u < num_units && !fail; u += gridDim.x) {
+        int tm, tn, ks;
+        tile_coords(u, p, tm, tn, ks);
+        const int kt0 = (ks * k_tiles_total) / p.split, kt1 = ((ks + 1) * k_tiles_total) / p.split;
+        for (int kt = kt0; kt < kt1 && !fail; ++kt, ++it) {
+          const int st = it % C::kStages;
+          if (it >= C::kStages)
+            fail = !mbar_wait(&empty[st], ((it / C::kStages) - 1) & 1, p.status, kSiteGemmProducer);
+          if (fail) break;
+          uint8_t* base = smem + C::kStageOff + st * C::kStageBytes;
+          const int k0 = kt * C::kBK;
+          if (kInt4) {
+            mbar_arrive_expect_tx(&full[st], C::kATile + C::kWTile + (p.grouped ? C::kSTile : 0));
+            tma_load_2d(base, &tmA, &full[st], k0, tm * kBM);
+            tma_load_2d(base + C::kATile, &tmB, &full[st], tn * (kBN / 2), k0);
+            if (p.grouped)
+              tma_load_2d(base + C::kATile + C::kWTile, &tmS, &full[st], tn * kBN, k0 / p.group);
+          } else {
+            mbar_arrive_expect_tx(&full[st], C::kATile + C::kBTile);
+            tma_load_2d(base, &tmA, &full[st], k0, tm * kBM);
+#pragma unroll
+            for (int b = 0; b < C::kBBoxes; ++b)
+              tma_load_2d(base + C::kATile + b * C::kBLBO, &tmB, &full[st],
+                          tn * kBN + b * C::kBAtomN, k0);
+          }
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      int it = 0, bit = 0, local = 0;
+      for (int u = blockIdx.x; u < num_units && !fail; u += gridDim.x, ++local) {
+        int tm, tn, ks;
+        tile_coords(u, p, tm, tn, ks);
+        const int kt0 = (ks * k_tiles_total) / p.split, kt1 = ((ks + 1) * k_tiles_total) / p.split;
+        const int ab = local & 1;
+        if (local >= 2)
+          fail = !mbar_wait(&acc_empty[ab], ((local >> 1) - 1) & 1, p.status, kSiteGemmMma);
+        if (fail) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + ab * kBN;
+        for (int kt = kt0; kt < kt1 && !fail; ++kt, ++it) {
+          const int st = it % C::kStages;
+          fail = !mbar_wait(&full[st], (it / C::kStages) & 1, p.status, kSiteGemmMma);
+          int bb = 0;
+          if (kInt4 && !fail) {
+            bb = bit % C::kBBufs;
+            fail = !mbar_wait(&bfull[bb], (bit / C::kBBufs) & 1, p.status, kSiteGemmMma);
+          }
+          if (fail) break;
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + C::kStageOff + st * C::kStageBytes);
+          const uint32_t b_base = kInt4 ? smem_u32(smem + C::kBBufOff + bb * C::kBTile)
+                                        : a_base + C::kATile;
+#pragma unroll
+          for (int j = 0; j < C::kKSteps; ++j) {
+            const uint64_t ad = make_smem_desc(a_base + j * 32, 16, 1024);
+            const uint64_t bd = make_smem_desc(b_base + j * C::kBStepBytes, C::kBLBO, 1024);
+            const uint32_t acc = (kt > kt0 || j > 0) ? 1u : 0u;
+            if (kKind == kF8)
+              umma_f8(d_tmem, ad, bd, C::kIdesc, acc);
+            else if (p.a_is_f16)
+              umma_f16(d_tmem, ad, bd, C::kIdescF16, acc);
+            else
+              umma_f16(d_tmem, ad, bd, C::kIdesc, acc);
+          }
+          umma_commit(&empty[st]);
+          if (kInt4) {
+            umma_commit(&bempty[bb]);
+            ++bit;
+          }
+        }
+        if (fail) break;
+        umma_commit(&acc_full[ab]);
+      }
+    }
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kEpiWarps) {
+    // ------------------------------- epilogue -------------------------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int local = 0;
+    for (int u = blockIdx.x; u < num_units && !fail; u += gridDim.x, ++local) {
+      int tm, tn, ks;
+      tile_coords(u, p, tm, tn, ks);
+      const int ab = local & 1;
+      fail = !mbar_wait(&acc_full[ab], (local >> 1) & 1, p.status, kSiteGemmEpilogue);
+      if (fail) break;
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(tm) * kBM + row_in_tile;
+      const int col0 = tn * kBN;
+      const bool row_ok = row < p.M;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + ab * kBN;
+      float* part = nullptr;
+      if (p.split > 1)
+        part = p.partials + ((static_cast<int64_t>(tm) * p.num_n + tn) * p.split + ks) * (kBM * kBN) +
+               row_in_tile * kBN;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t raw[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, raw);
+        tmem_ld_wait();
+        if (p.split > 1) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            __stcg(reinterpret_cast<float4*>(part + c * 32 + i),
+                   make_float4(__uint_as_float(raw[i]), __uint_as_float(raw[i + 1]),
+                               __uint_as_float(raw[i + 2]), __uint_as_float(raw[i + 3])));
+        } else if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            float v[8];
+            // int4 B tiles hold each 8-column chunk in the order int4_codes8
+            // emits; column e of the chunk sits at position (e%4)*2 + e/4.
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              v[e] = __uint_as_float(raw[i + (kInt4 ? ((e & 3) * 2 + (e >> 2)) : e)]) * p.out_scale;
+            const int col = col0 + c * 32 + i;
+            if (col < p.N)
+              store8(p.out, p.out_dtype, row * p.ldc + col, v, col + 8 <= p.N, min(8, p.N - col));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
+
+      if (p.split > 1) {
+        // deterministic split-K: the last of the `split` units of this tile sums
+        // the partials in split order
+        __threadfence();
+        named_bar_sync(1, kEpiWarps * 32);
+        const int tile_id = tm * p.num_n + tn;
+        if (tid == kEpiWarp0 * 32)
+          *s_flag = (atomicAdd(&p.sems[tile_id], 1u) == static_cast<unsigned>(p.split - 1));
+        named_bar_sync(1, kEpiWarps * 32);
+        if (*s_flag) {
+          __threadfence();
+          const float* base = p.partials + static_cast<int64_t>(tile_id) * p.split * (kBM * kBN) +
+                              row_in_tile * kBN;
+#pragma unroll 1
+          for (int c = 0; c < kBN / 8 && row_ok; ++c) {
+            float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int j = 0; j < p.split; ++j) {
+              const float4 x0 = __ldcg(reinterpret_cast<const float4*>(base + j * (kBM * kBN) + c * 8));
+              const float4 x1 =
+                  __ldcg(reinterpret_cast<const float4*>(base + j * (kBM * kBN) + c * 8 + 4));
+              v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
+              v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] *= p.out_scale;
+            const int col = col0 + c * 8;
+            if (col < p.N)
+              store8(p.out, p.out_dtype, row * p.ldc + col, v, col + 8 <= p.N, min(8, p.N - col));
+          }
+          named_bar_sync(1, kEpiWarps * 32);
+          if (tid == kEpiWarp0 * 32) p.sems[tile_id] = 0u;  // re-arm
+        }
+      }
+    }
+  } else if (kInt4 && warp >= kDeqWarp0) {
+    // ------------------------ dequant (W4A16 prefill) ------------------------
+    // Stage: packed rows [kBK = 64][128 B] -> B tile [64 k][256 n] MN-major.
+    const int dt = tid - kDeqWarp0 * 32;   // 0..255
+    const int wq = dt & 7;                  // 16-byte quad: columns 32wq..32wq+31
+    const int r0 = dt >> 3;                 // rows r0 and r0 + 32
+    int it = 0, bit = 0;
+    for (int u = blockIdx.x; u < num_units && !fail; u += gridDim.x) {
+      int tm, tn, ks;
+      tile_coords(u, p, tm, tn, ks);
+      const int kt0 = (ks * k_tiles_total) / p.split, kt1 = ((ks + 1) * k_tiles_total) / p.split;
+      for (int kt = kt0; kt < kt1 && !fail; ++kt, ++it, ++bit) {
+        const int st = it % C::kStages;
+        const int bb = bit % C::kBBufs;
+        fail = !mbar_wait(&full[st], (it / C::kStages) & 1, p.status, kSiteGemmDequant);
+        if (!fail && bit >= C::kBBufs)
+          fail = !mbar_wait(&bempty[bb], ((bit / C::kBBufs) - 1) & 1, p.status, kSiteGemmDequant);
+        if (fail) break;
+        const uint8_t* stage = smem + C::kStageOff + st * C::kStageBytes;
+        const uint8_t* wsm = stage + C::kATile;
+        // scales for this thread's 32 columns, as pairs in the order int4_codes8 emits
+        const uint32_t* sc = reinterpret_cast<const uint32_t*>(stage + C::kATile + C::kWTile);
+        uint8_t* bt = smem + C::kBBufOff + bb * C::kBTile;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int r = r0 + 32 * hh;
+          const uint4 wv = *reinterpret_cast<const uint4*>(wsm + r * 128 + wq * 16);
+          const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int c = 4 * wq + i;  // 8-column chunk 0..31
+            const uint4 s4 = *reinterpret_cast<const uint4*>(sc + c * 4);
+            // scale pairs regrouped to (c0,c4) (c1,c5) (c2,c6) (c3,c7)
+            const uint32_t s04 = prmt(s4.x, s4.z, 0x5410), s15 = prmt(s4.x, s4.z, 0x7632);
+            const uint32_t s26 = prmt(s4.y, s4.w, 0x5410), s37 = prmt(s4.y, s4.w, 0x7632);
+            uint32_t v[4];
+            if (p.a_is_f16) {
+              int4_codes8<__half>(words[i], v);
+              if (p.grouped) {
+                __half* tag = nullptr;
+                v[0] = mul2(v[0], s04, tag); v[1] = mul2(v[1], s15, tag);
+                v[2] = mul2(v[2], s26, tag); v[3] = mul2(v[3], s37, tag);
+              }
+            } else {
+              int4_codes8<__nv_bfloat16>(words[i], v);
+              if (p.grouped) {
+                __nv_bfloat16* tag = nullptr;
+                v[0] = mul2(v[0], s04, tag); v[1] = mul2(v[1], s15, tag);
+                v[2] = mul2(v[2], s26, tag); v[3] = mul2(v[3], s37, tag);
+              }
+            }
+            const int r8 = r & 7;
+            const int off = (c >> 3) * C::kBLBO + (r >> 3) * 1024 + r8 * 128 + (((c & 7) ^ r8) << 4);
+            *reinterpret_cast<uint4*>(bt + off) = make_uint4(v[0], v[1], v[2], v[3]);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bfull[bb]);
+          mbar_arrive(&empty[st]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace
+}  // namespace pk
+
+namespace pk {
+namespace {
+
+CUtensorMapDataType elem_tmap(int dt) {
+  switch (dt) {
+    case PK_BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    case PK_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    default: return CU_TENSOR_MAP_DATA_TYPE_UINT8;  // e4m3 moves as bytes
+  }
+}
+
+template <int kKind, bool kInt4>
+cudaError_t launch_typed(const GemmArgs& g, cudaStream_t s, const char** why) {
+  using C = Cfg<kKind, kInt4>;
+  const int elem = C::kElem;
+  CUtensorMap tmA, tmB, tmS;
+  if (!encode_tmap_2d(&tmA, elem_tmap(g.a_dtype), g.a, g.K, g.M, g.lda * elem, C::kBK, kBM,
+                      CU_TENSOR_MAP_SWIZZLE_128B, why))
+    return cudaErrorInvalidValue;
+  if (kInt4) {
+    if (!encode_tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.b, g.N / 2, g.K, g.N / 2, kBN / 2,
+                        C::kBK, CU_TENSOR_MAP_SWIZZLE_NONE, why))
+      return cudaErrorInvalidValue;
+    if (g.scales != nullptr) {
+      const int64_t G = (g.K + g.group - 1) / g.group;
+      if (!encode_tmap_2d(&tmS, elem_tmap(g.a_dtype), g.scales, g.N, G, g.N * 2, kBN, 1,
+                          CU_TENSOR_MAP_SWIZZLE_NONE, why))
+        return cudaErrorInvalidValue;
+    } else {
+      tmS = tmB;  // unused
+    }
+  } else {
+    if (!encode_tmap_2d(&tmB, elem_tmap(g.a_dtype), g.b, g.N, g.K, g.ldb * elem, C::kBAtomN,
+                        C::kBK, CU_TENSOR_MAP_SWIZZLE_128B, why))
+      return cudaErrorInvalidValue;
+    tmS = tmB;
+  }
+  Params p{};
+  p.M = static_cast<int>(g.M);
+  p.N = static_cast<int>(g.N);
+  p.K = static_cast<int>(g.K);
+  p.split = g.split;
+  p.num_m = static_cast<int>((g.M + kBM - 1) / kBM);
+  p.num_n = static_cast<int>((g.N + kBN - 1) / kBN);
+  p.out_dtype = g.out_dtype;
+  p.ldc = g.ldc;
+  p.out_scale = g.out_scale;
+  p.out = g.out;
+  p.partials = g.partials;
+  p.sems = g.sems;
+  p.scales = g.scales;
+  p.group = g.group > 0 ? g.group : 1;
+  p.grouped = g.scales != nullptr;
+  p.a_is_f16 = g.a_dtype == PK_F16;
+  p.status = g.status;
+  const int units = p.num_m * p.num_n * p.split;
+  const int grid = units < num_sms() ? units : num_sms();
+  auto kernel = gemm_tc_kernel<kKind, kInt4>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  if (e != cudaSuccess) return e;
+  kernel<<<grid, C::kThreads, C::kSmem, s>>>(tmA, tmB, tmS, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int64_t gemm_tiles(int64_t M, int64_t N) { return ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN); }
+
+size_t gemm_splitk_workspace_bytes(int64_t M, int64_t N, int split) {
+  if (split <= 1) return 0;
+  const int64_t tiles = gemm_tiles(M, N);
+  const size_t sem_bytes = ((tiles * sizeof(unsigned) + 255) / 256) * 256;
+  return sem_bytes + static_cast<size_t>(tiles) * split * kBM * kBN * sizeof(float);
+}
+
+cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t s, const char** why) {
+  if (g.kind == GemmArgs::kFp8) return launch_typed<kF8, false>(g, s, why);
+  if (g.kind == GemmArgs::kW4A16) return launch_typed<kF16, true>(g, s, why);
+  return launch_typed<kF16, false>(g, s, why);
+}
+
+}  // namespace pk

@@ -72,6 +72,30 @@ int decode_pick_split(int64_t M, int64_t N, int64_t K);
 size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int split);
 cudaError_t launch_w4a16_decode(const DecodeArgs& args, cudaStream_t s, const char** why);
 
+// ---- gemm_tc.cu (persistent tcgen05 GEMM: fp8, dense split-K, W4A16 prefill)
+struct GemmArgs {
+  enum Kind { kDense16 = 0, kFp8 = 1, kW4A16 = 2 } kind;
+  const void* a;        // [M, K] row-major (ld lda), dtype a_dtype
+  int a_dtype;          // PK_F16 / PK_BF16 / PK_E4M3
+  int64_t lda;
+  const void* b;        // dense/fp8: [K, N] row-major (ld ldb); W4A16: packed uint8 [K, N/2]
+  int64_t ldb;
+  const void* scales;   // W4A16: [ceil(K/group), N] in a_dtype
+  int group;
+  int64_t M, N, K;
+  int split;            // K splits (dense), else 1
+  void* out;
+  int out_dtype;        // PK_F32 / PK_BF16
+  int64_t ldc;
+  float out_scale;
+  float* partials;      // split-K workspace
+  unsigned* sems;
+  int* status;
+};
+int64_t gemm_tiles(int64_t M, int64_t N);
+size_t gemm_splitk_workspace_bytes(int64_t M, int64_t N, int split);
+cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t s, const char** why);
+
 // ---- w4a16_simt.cu (any shape; CUDA cores) -------------------------------
 cudaError_t launch_w4a16_simt(const void* a, int a_dtype, int64_t lda, const uint8_t* wp,
                               const void* scales, float scalar_scale, int group, int64_t M,

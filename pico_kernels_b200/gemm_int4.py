@@ -140,7 +140,10 @@ def int4_gemm(a: torch.Tensor, w_packed: torch.Tensor, scale,
         if scale.dim() != 2 or scale.shape[1] != N:
             raise _lib.ShapeError(f"group scales must be [G, N={N}] (got {tuple(scale.shape)})")
         G = scale.shape[0]
-        group = group_size if group_size is not None else K // G
+        if group_size is not None:
+            group = group_size
+        else:  # several sizes can give G groups when the last one is ragged: prefer 128
+            group = next((g for g in (128, K // G) if g > 0 and (K + g - 1) // g == G), K // G)
         if group <= 0 or (K + group - 1) // group != G:
             raise _lib.ShapeError(f"{G} scale rows do not tile K={K} with group_size={group}")
         scales = scale if scale.dtype == a.dtype else scale.to(a.dtype)

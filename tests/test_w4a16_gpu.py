@@ -100,14 +100,23 @@ def test_per_tensor_scale_reference_api():
     assert (torch.norm(c - ref) / torch.norm(ref)).item() < 1e-5
 
 
-@pytest.mark.parametrize("M,N,K,group", [(3, 130, 200, 64), (20, 256, 384, 128), (1, 2, 7, 4)])
+@pytest.mark.parametrize("M,N,K,group", [(3, 130, 200, 64), (1, 2, 7, 4), (40, 70, 128, 32)])
 def test_ragged_shapes_generic_kernel(M, N, K, group):
+    """Shapes no tensor-core path takes run on the CUDA-core kernel, which
+    dequantizes in fp32: only summation order differs from the oracle."""
     a, w, ref = make_case(M, N, K, torch.bfloat16, group=group, seed=11)
     packed, scales = pk.quantize_int4_grouped(w.cuda(), group)
     y = pk.int4_gemm(a.cuda(), packed, scales, group_size=group)
-    # the CUDA-core kernel dequantizes in fp32: only summation order differs
     yy = y.cpu().numpy()
     assert np.abs(yy - ref).max() <= 1e-4 * max(1.0, np.abs(ref).max())
+
+
+@pytest.mark.parametrize("M,N,K", [(20, 256, 384), (33, 96, 192)])
+def test_small_m_prefill_path(M, N, K):
+    """M > 16 with K % 64 == 0 takes the tensor-core prefill kernel (bf16 q*s)."""
+    a, w, ref = make_case(M, N, K, torch.bfloat16, seed=12)
+    packed, scales = pk.quantize_int4_grouped(w.cuda(), 128)
+    check(pk.int4_gemm(a.cuda(), packed, scales), ref, torch.bfloat16, f"M={M}")
 
 
 def test_errors_are_reference_compatible():
