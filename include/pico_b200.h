@@ -126,6 +126,25 @@ PK_API int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t*
                   int out_dtype, int64_t ldo, int split_k, void* workspace,
                   size_t workspace_bytes, void* stream);
 
+/* Decode W4A16 GEMM that allocates nothing and takes no workspace. It has no
+ * counterpart in the reference. It exists for callers that cannot call
+ * cudaMalloc: a runtime that plans all device memory itself and forbids
+ * libraries from allocating, or a latency-critical decode loop that cannot
+ * afford cudaMalloc's implicit synchronization. Same arguments and result as
+ * pk_w4a16_gemm minus the workspace, for decode shapes only (M <= 16,
+ * N % 128 == 0, K % 128 == 0, group 128 or a scalar scale). Its split-K
+ * partials live in a static 4 MiB device array owned by the library (plus
+ * arrival counters for up to 4096 column tiles), held on every GPU that loads
+ * the library until exit; a request needing more (tiles * split * M * 512
+ * bytes) fails with PK_ERR_WORKSPACE before launching. The first call on a
+ * device looks up the array's address; make it before any stream capture.
+ * All calls on a device share the array: each clears the counters it uses on
+ * its stream, and calls that overlap on the GPU race. */
+PK_API int pk_w4a16_gemm_noalloc(const void* a, int a_dtype, int64_t lda, const uint8_t* wp,
+                                 const void* scales, float scalar_scale, int group_size, int64_t M,
+                                 int64_t N, int64_t K, void* out, int out_dtype, int64_t ldo,
+                                 int split_k, void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* fp8 (e4m3) GEMM                                                         */
 /* ---------------------------------------------------------------------- */

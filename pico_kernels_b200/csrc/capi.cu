@@ -66,6 +66,11 @@ bool is16(int dt) { return dt == PK_F16 || dt == PK_BF16; }
 
 }  // namespace
 
+void set_error_message(const char* msg) {
+  std::strncpy(g_msg, msg, sizeof(g_msg) - 1);
+  g_msg[sizeof(g_msg) - 1] = '\0';
+}
+
 int* device_status_ptr() {
   const int d = current_device();
   if (d < 0) return nullptr;

@@ -15,6 +15,9 @@ namespace pk {
 // Device status word: [0] first error code, [1] site that recorded it.
 int* device_status_ptr();  // per current device; nullptr on failure
 
+// Message returned by pk_last_error_string() on this host thread.
+void set_error_message(const char* msg);
+
 // Sites recorded with PK_ERR_TIMEOUT (which wait gave up).
 enum WaitSite : int {
   kSiteDecodeFull = 101,
