@@ -277,7 +277,7 @@ int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t* wp, co
   }
 
   // Tensor-core prefill path: 64-row K stages, scales on 64-row boundaries.
-  const bool prefill_ok = (K % 64) == 0 && (N % 32) == 0 && (lda % 8) == 0 &&
+  const bool prefill_ok = (K % 64) == 0 && (N % 64) == 0 && (lda % 8) == 0 &&
                           (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
                           (reinterpret_cast<uintptr_t>(wp) & 15) == 0 &&
                           (scales == nullptr || ((group_size % 64) == 0 &&

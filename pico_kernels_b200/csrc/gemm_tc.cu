@@ -181,7 +181,8 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
             tma_load_2d(base, &tmA, &full[st], k0, tm * kBM);
             tma_load_2d(base + C::kATile, &tmB, &full[st], tn * (kBN / 2), k0);
             if (p.grouped)
-              tma_load_2d(base + C::kATile + C::kWTile, &tmS, &full[st], tn * kBN, k0 / p.group);
+              tma_load_2d(base + C::kATile + C::kWTile, &tmS, &full[st], 0,
+                          (k0 / p.group) * (p.N / 64) + tn * (kBN / 64));
           } else {
             mbar_arrive_expect_tx(&full[st], C::kATile + C::kBTile);
             tma_load_2d(base, &tmA, &full[st], k0, tm * kBM);
@@ -329,9 +330,13 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
   } else if (kInt4 && warp >= kDeqWarp0) {
     // ------------------------ dequant (W4A16 prefill) ------------------------
     // Stage: packed rows [kBK = 64][128 B] -> B tile [64 k][256 n] MN-major.
+    // Lane mapping: a 16-byte shared access is serviced a quarter-warp (8
+    // lanes) at a time, so each quarter reads 8 different 16-byte quads of the
+    // packed rows and writes 8 different bank groups of the swizzled B tile:
+    // lane t of quarter k takes quad wq = t of row 4*warp + ((t/2 + k) & 3).
     const int dt = tid - kDeqWarp0 * 32;   // 0..255
-    const int wq = dt & 7;                  // 16-byte quad: columns 32wq..32wq+31
-    const int r0 = dt >> 3;                 // rows r0 and r0 + 32
+    const int wq = lane & 7;                // 16-byte quad: columns 32wq..32wq+31
+    const int r0 = 4 * (dt >> 5) + (((wq >> 1) + (lane >> 3)) & 3);  // rows r0 and r0 + 32
     int it = 0, bit = 0;
     for (int u = blockIdx.x; u < num_units && !fail; u += gridDim.x) {
       int tm, tn, ks;
@@ -346,8 +351,23 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
         if (fail) break;
         const uint8_t* stage = smem + C::kStageOff + st * C::kStageBytes;
         const uint8_t* wsm = stage + C::kATile;
-        // scales for this thread's 32 columns, as pairs in the order int4_codes8 emits
-        const uint32_t* sc = reinterpret_cast<const uint32_t*>(stage + C::kATile + C::kWTile);
+        // Group scales of this thread's 32 columns, regrouped into the pair order
+        // int4_codes8 emits: (c0,c4) (c1,c5) (c2,c6) (c3,c7) per 8-column chunk.
+        // The scale row arrives 128B-swizzled (chunk c at row c/8, position
+        // (c%8) ^ (c/8)), so these reads are conflict-free too.
+        uint32_t sp[4][4];
+        if (p.grouped) {
+          const uint8_t* sc = stage + C::kATile + C::kWTile;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int c = 4 * wq + i;
+            const uint4 s4 = *reinterpret_cast<const uint4*>(sc + (c >> 3) * 128 + (((c & 7) ^ (c >> 3)) << 4));
+            sp[i][0] = prmt(s4.x, s4.z, 0x5410);
+            sp[i][1] = prmt(s4.x, s4.z, 0x7632);
+            sp[i][2] = prmt(s4.y, s4.w, 0x5410);
+            sp[i][3] = prmt(s4.y, s4.w, 0x7632);
+          }
+        }
         uint8_t* bt = smem + C::kBBufOff + bb * C::kBTile;
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
@@ -357,10 +377,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int c = 4 * wq + i;  // 8-column chunk 0..31
-            const uint4 s4 = *reinterpret_cast<const uint4*>(sc + c * 4);
-            // scale pairs regrouped to (c0,c4) (c1,c5) (c2,c6) (c3,c7)
-            const uint32_t s04 = prmt(s4.x, s4.z, 0x5410), s15 = prmt(s4.x, s4.z, 0x7632);
-            const uint32_t s26 = prmt(s4.y, s4.w, 0x5410), s37 = prmt(s4.y, s4.w, 0x7632);
+            const uint32_t s04 = sp[i][0], s15 = sp[i][1], s26 = sp[i][2], s37 = sp[i][3];
             uint32_t v[4];
             if (p.a_is_f16) {
               int4_codes8<__half>(words[i], v);
@@ -425,8 +442,9 @@ cudaError_t launch_typed(const GemmArgs& g, cudaStream_t s, const char** why) {
       return cudaErrorInvalidValue;
     if (g.scales != nullptr) {
       const int64_t G = (g.K + g.group - 1) / g.group;
-      if (!encode_tmap_2d(&tmS, elem_tmap(g.a_dtype), g.scales, g.N, G, g.N * 2, kBN, 1,
-                          CU_TENSOR_MAP_SWIZZLE_NONE, why))
+      // the scales viewed as rows of 64 (128 bytes), four rows per 256-column tile
+      if (!encode_tmap_2d(&tmS, elem_tmap(g.a_dtype), g.scales, 64, G * (g.N / 64), 128, 64, 4,
+                          CU_TENSOR_MAP_SWIZZLE_128B, why))
         return cudaErrorInvalidValue;
     } else {
       tmS = tmB;  // unused

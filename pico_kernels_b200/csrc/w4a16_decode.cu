@@ -196,9 +196,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   } else if (warp >= kDeqWarp0) {
     // ---------------- dequant ----------------
+    // Lane mapping: 16-byte shared accesses are serviced a quarter-warp (8
+    // lanes) at a time, so each quarter must read 8 different bank groups of
+    // the 64-byte packed rows and write 8 different bank groups of the
+    // swizzled tile. Quarter k of warp w covers rows 8w + 4(k/2) .. +3: lane t
+    // takes quad q = t % 4 of row 8w + 4(k/2) + 2((q/2) ^ (k%2)) + t/4.
     const int dt = tid - kDeqWarp0 * 32;
-    const int wq = dt & 3;   // 16-byte quad of the 64-byte packed row: columns 32wq..32wq+31
-    const int r = dt >> 2;   // row within the 64-row half stage
+    const int qk = lane >> 3, qt = lane & 7;
+    const int wq = qt & 3;   // 16-byte quad of the 64-byte packed row: columns 32wq..32wq+31
+    const int r = 8 * (dt >> 5) + 4 * (qk >> 1) + 2 * ((wq >> 1) ^ (qk & 1)) + (qt >> 2);
     const int r8 = r & 7;
     const uint32_t row_off = (r >> 3) * 1024 + r8 * 128;
     for (int s = 0; s < S && !fail; ++s) {
