@@ -1,20 +1,22 @@
 // Persistent tcgen05 GEMM for sm_100a: C[M, N] = A[M, K] @ B[K, N].
 //
-// One CTA per SM walks output tiles of 128 x 256 (grouped raster for L2
-// reuse). Operands are staged by TMA into 128B-swizzled shared-memory tiles:
-// A K-major (row-major [M, K]), B MN-major (row-major [K, N], read by the
-// tensor core through the descriptor's MN-major mode, so no transpose pass).
-// The fp32 accumulator lives in TMEM, double-buffered (2 x 256 columns) so
-// the epilogue of one tile overlaps the main loop of the next.
+// One CTA per SM walks output tiles (grouped raster for L2 reuse). Operands
+// are staged by TMA into 128B-swizzled shared-memory tiles: A K-major
+// (row-major [M, K]), B MN-major (row-major [K, N], read by the tensor core
+// through the descriptor's MN-major mode, so no transpose pass). fp32
+// accumulators live in TMEM, double-buffered so the epilogue of one tile
+// overlaps the main loop of the next.
 //
 // Used by three entry points:
-//   * fp8 (e4m3 x e4m3, kind::f8f6f4, K = 32 per MMA), epilogue x out_scale
-//     -- gemm_fp8.fp8_gemm_kernel (gemm_fp8.py:38-86);
-//   * dense fp16/bf16 (kind::f16) with an optional deterministic split-K
-//     -- gemm_splitk.gemm_splitk_kernel (gemm_splitk.py:26-64);
-//   * W4A16 prefill: B is produced in shared memory by dequant warps from the
-//     packed int4 weights and group scales (q * s rounded to A's dtype)
-//     -- gemm_int4.int4_gemm_kernel (gemm_int4.py:21-55).
+//   * fp8 (e4m3 x e4m3, kind::f8f6f4, K = 32 per MMA), 128 x 256 tiles,
+//     epilogue x out_scale -- gemm_fp8.fp8_gemm_kernel (gemm_fp8.py:38-86);
+//   * dense fp16/bf16 (kind::f16), 128 x 256 tiles, optional deterministic
+//     split-K -- gemm_splitk.gemm_splitk_kernel (gemm_splitk.py:26-64);
+//   * W4A16 prefill: 128 x 256 tiles; B is produced in shared memory by
+//     dequant warps from the packed int4 weights and group scales (q * s
+//     rounded to A's dtype) -- gemm_int4.int4_gemm_kernel (gemm_int4.py:21-55).
+//     (256 x 128 tiles, two M = 128 MMAs per dequantized B tile, halve the
+//     dequant work but re-read B from shared memory twice and measured slower.)
 //
 // Warp roles: 0 TMA producer, 1 MMA issuer (+ TMEM owner), 2-5 epilogue
 // (TMEM lanes 0-127), 6-13 dequant (int4 only).
@@ -23,8 +25,6 @@
 namespace pk {
 namespace {
 
-constexpr int kBM = 128;
-constexpr int kBN = 256;
 constexpr int kTmaWarp = 0, kMmaWarp = 1, kEpiWarp0 = 2, kEpiWarps = 4, kDeqWarp0 = 6;
 constexpr int kDeqWarps = 8;
 constexpr int kGroupM = 8;
@@ -37,16 +37,24 @@ struct Cfg {
   static constexpr int kBK = 128 / kElem;                    // one 128-byte swizzle row of K
   static constexpr int kMmaK = kKind == kF16 ? 16 : 32;
   static constexpr int kKSteps = kBK / kMmaK;                // 4
-  static constexpr int kATile = kBM * 128;                   // 16 KB
-  static constexpr int kBTile = kBK * kBN * kElem;           // 32 KB
+  // W4A16 tiles: kInt4Wide = 128 x 256 (one MMA per k-step reads each B slice
+  // once); otherwise 256 x 128 (two M = 128 MMAs share each dequantized B
+  // tile, halving dequant per FLOP but re-reading B from shared memory).
+  static constexpr bool kInt4Wide = true;
+  static constexpr int kMSub = (kInt4 && !kInt4Wide) ? 2 : 1;  // M = 128 MMAs per k-step
+  static constexpr int kBM = 128 * kMSub;                    // CTA tile rows
+  static constexpr int kBN = (kInt4 && !kInt4Wide) ? 128 : 256;  // CTA tile columns (= MMA N)
+  static constexpr int kATile = kBM * 128;                   // 16 / 32 KB
+  static constexpr int kBTile = kBK * kBN * kElem;           // 32 / 16 KB
   static constexpr int kBAtomN = 128 / kElem;                // N per MN-major swizzle atom
   static constexpr int kBBoxes = kBN / kBAtomN;              // TMA boxes per B tile
   static constexpr int kBLBO = kBK * 128;                    // bytes between N atoms
   static constexpr int kBStepBytes = (kMmaK / 8) * 1024;     // B advance per MMA K step
-  // int4: packed weights (kBK rows x 128 B) + one row of group scales per stage
-  static constexpr int kWTile = kInt4 ? kBK * (kBN / 2) : 0;  // 8 KB
-  static constexpr int kSTile = kInt4 ? kBN * 2 : 0;          // 512 B
-  static constexpr int kStages = kInt4 ? 4 : 4;
+  // int4: packed weights (kBK rows x kBN/2 bytes) + kBN group scales per stage
+  static constexpr int kWTile = kInt4 ? kBK * (kBN / 2) : 0;  // 8 / 4 KB
+  static constexpr int kSRows = kBN / 64;                     // scale rows of 64 (128 B)
+  static constexpr int kSTile = kInt4 ? kBN * 2 : 0;          // 512 / 256 B
+  static constexpr int kStages = 4;
   static constexpr int kBBufs = kInt4 ? 2 : 0;                // dequantized B ring
   static constexpr int kStageBytes = kATile + (kInt4 ? kWTile + 1024 : kBTile);
   static constexpr int kStageOff = 0;
@@ -54,9 +62,12 @@ struct Cfg {
   static constexpr int kBarOff = kBBufOff + kBBufs * kBTile;
   static constexpr int kSmem = kBarOff + 256 + 1024;
   static constexpr int kThreads = (kInt4 ? kDeqWarp0 + kDeqWarps : kDeqWarp0) * 32;
+  static constexpr int kAccCols = kMSub * kBN;                // TMEM columns per accumulator set
   static constexpr uint32_t kIdesc =
-      make_idesc(kKind == kF16 ? 1u : 0u, false, true, kBM, kBN);  // bf16 / e4m3
-  static constexpr uint32_t kIdescF16 = make_idesc(0u, false, true, kBM, kBN);
+      make_idesc(kKind == kF16 ? 1u : 0u, false, true, 128, kBN);  // bf16 / e4m3
+  static constexpr uint32_t kIdescF16 = make_idesc(0u, false, true, 128, kBN);
+  static_assert(2 * kAccCols <= 512, "two accumulator sets fit TMEM");
+  static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
 struct Params {
@@ -69,7 +80,6 @@ struct Params {
   void* out;
   float* partials;       // split-K workspace
   unsigned* sems;
-  const void* scales;    // int4: [G, N] (A's dtype)
   int group;             // int4 group size
   int grouped;           // int4: 1 = group scales in the dequant, 0 = scalar out_scale
   int a_is_f16;          // 16-bit kinds: A dtype is fp16 (else bf16)
@@ -121,6 +131,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmS, const Params p) {
   using C = Cfg<kKind, kInt4>;
+  constexpr int BM = C::kBM, BN = C::kBN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -178,18 +189,18 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
           const int k0 = kt * C::kBK;
           if (kInt4) {
             mbar_arrive_expect_tx(&full[st], C::kATile + C::kWTile + (p.grouped ? C::kSTile : 0));
-            tma_load_2d(base, &tmA, &full[st], k0, tm * kBM);
-            tma_load_2d(base + C::kATile, &tmB, &full[st], tn * (kBN / 2), k0);
+            tma_load_2d(base, &tmA, &full[st], k0, tm * BM);
+            tma_load_2d(base + C::kATile, &tmB, &full[st], tn * (BN / 2), k0);
             if (p.grouped)
               tma_load_2d(base + C::kATile + C::kWTile, &tmS, &full[st], 0,
-                          (k0 / p.group) * (p.N / 64) + tn * (kBN / 64));
+                          (k0 / p.group) * (p.N / 64) + tn * C::kSRows);
           } else {
             mbar_arrive_expect_tx(&full[st], C::kATile + C::kBTile);
-            tma_load_2d(base, &tmA, &full[st], k0, tm * kBM);
+            tma_load_2d(base, &tmA, &full[st], k0, tm * BM);
 #pragma unroll
             for (int b = 0; b < C::kBBoxes; ++b)
               tma_load_2d(base + C::kATile + b * C::kBLBO, &tmB, &full[st],
-                          tn * kBN + b * C::kBAtomN, k0);
+                          tn * BN + b * C::kBAtomN, k0);
           }
         }
       }
@@ -207,7 +218,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
           fail = !mbar_wait(&acc_empty[ab], ((local >> 1) - 1) & 1, p.status, kSiteGemmMma);
         if (fail) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem + ab * kBN;
+        const uint32_t d_tmem = tmem + ab * C::kAccCols;
         for (int kt = kt0; kt < kt1 && !fail; ++kt, ++it) {
           const int st = it % C::kStages;
           fail = !mbar_wait(&full[st], (it / C::kStages) & 1, p.status, kSiteGemmMma);
@@ -223,15 +234,19 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
                                         : a_base + C::kATile;
 #pragma unroll
           for (int j = 0; j < C::kKSteps; ++j) {
-            const uint64_t ad = make_smem_desc(a_base + j * 32, 16, 1024);
             const uint64_t bd = make_smem_desc(b_base + j * C::kBStepBytes, C::kBLBO, 1024);
             const uint32_t acc = (kt > kt0 || j > 0) ? 1u : 0u;
-            if (kKind == kF8)
-              umma_f8(d_tmem, ad, bd, C::kIdesc, acc);
-            else if (p.a_is_f16)
-              umma_f16(d_tmem, ad, bd, C::kIdescF16, acc);
-            else
-              umma_f16(d_tmem, ad, bd, C::kIdesc, acc);
+#pragma unroll
+            for (int h = 0; h < C::kMSub; ++h) {
+              const uint64_t ad = make_smem_desc(a_base + h * 16384 + j * 32, 16, 1024);
+              const uint32_t d = d_tmem + h * BN;
+              if (kKind == kF8)
+                umma_f8(d, ad, bd, C::kIdesc, acc);
+              else if (p.a_is_f16)
+                umma_f16(d, ad, bd, C::kIdescF16, acc);
+              else
+                umma_f16(d, ad, bd, C::kIdesc, acc);
+            }
           }
           umma_commit(&empty[st]);
           if (kInt4) {
@@ -246,7 +261,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kEpiWarps) {
     // ------------------------------- epilogue -------------------------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = q * 32 + lane;
+    const int row_in_sub = q * 32 + lane;
     int local = 0;
     for (int u = blockIdx.x; u < num_units && !fail; u += gridDim.x, ++local) {
       int tm, tn, ks;
@@ -255,37 +270,43 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
       fail = !mbar_wait(&acc_full[ab], (local >> 1) & 1, p.status, kSiteGemmEpilogue);
       if (fail) break;
       tc_fence_after();
-      const int64_t row = static_cast<int64_t>(tm) * kBM + row_in_tile;
-      const int col0 = tn * kBN;
-      const bool row_ok = row < p.M;
-      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + ab * kBN;
-      float* part = nullptr;
-      if (p.split > 1)
-        part = p.partials + ((static_cast<int64_t>(tm) * p.num_n + tn) * p.split + ks) * (kBM * kBN) +
-               row_in_tile * kBN;
+      const int col0 = tn * BN;
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t raw[32];
-        tmem_ld_32x32b_x32(taddr + c * 32, raw);
-        tmem_ld_wait();
-        if (p.split > 1) {
+      for (int h = 0; h < C::kMSub; ++h) {
+        const int row_in_tile = h * 128 + row_in_sub;
+        const int64_t row = static_cast<int64_t>(tm) * BM + row_in_tile;
+        const bool row_ok = row < p.M;
+        const uint32_t taddr =
+            tmem + (static_cast<uint32_t>(q * 32) << 16) + ab * C::kAccCols + h * BN;
+        float* part = nullptr;
+        if (p.split > 1)
+          part = p.partials +
+                 ((static_cast<int64_t>(tm) * p.num_n + tn) * p.split + ks) * (BM * BN) +
+                 row_in_tile * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t raw[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, raw);
+          tmem_ld_wait();
+          if (p.split > 1) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            __stcg(reinterpret_cast<float4*>(part + c * 32 + i),
-                   make_float4(__uint_as_float(raw[i]), __uint_as_float(raw[i + 1]),
-                               __uint_as_float(raw[i + 2]), __uint_as_float(raw[i + 3])));
-        } else if (row_ok) {
+            for (int i = 0; i < 32; i += 4)
+              __stcg(reinterpret_cast<float4*>(part + c * 32 + i),
+                     make_float4(__uint_as_float(raw[i]), __uint_as_float(raw[i + 1]),
+                                 __uint_as_float(raw[i + 2]), __uint_as_float(raw[i + 3])));
+          } else if (row_ok) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            float v[8];
-            // int4 B tiles hold each 8-column chunk in the order int4_codes8
-            // emits; column e of the chunk sits at position (e%4)*2 + e/4.
+            for (int i = 0; i < 32; i += 8) {
+              float v[8];
+              // int4 B tiles hold each 8-column chunk in the order int4_codes8
+              // emits; column e of the chunk sits at position (e%4)*2 + e/4.
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
-              v[e] = __uint_as_float(raw[i + (kInt4 ? ((e & 3) * 2 + (e >> 2)) : e)]) * p.out_scale;
-            const int col = col0 + c * 32 + i;
-            if (col < p.N)
-              store8(p.out, p.out_dtype, row * p.ldc + col, v, col + 8 <= p.N, min(8, p.N - col));
+              for (int e = 0; e < 8; ++e)
+                v[e] = __uint_as_float(raw[i + (kInt4 ? ((e & 3) * 2 + (e >> 2)) : e)]) * p.out_scale;
+              const int col = col0 + c * 32 + i;
+              if (col < p.N)
+                store8(p.out, p.out_dtype, row * p.ldc + col, v, col + 8 <= p.N, min(8, p.N - col));
+            }
           }
         }
       }
@@ -304,23 +325,28 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
         named_bar_sync(1, kEpiWarps * 32);
         if (*s_flag) {
           __threadfence();
-          const float* base = p.partials + static_cast<int64_t>(tile_id) * p.split * (kBM * kBN) +
-                              row_in_tile * kBN;
 #pragma unroll 1
-          for (int c = 0; c < kBN / 8 && row_ok; ++c) {
-            float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            for (int j = 0; j < p.split; ++j) {
-              const float4 x0 = __ldcg(reinterpret_cast<const float4*>(base + j * (kBM * kBN) + c * 8));
-              const float4 x1 =
-                  __ldcg(reinterpret_cast<const float4*>(base + j * (kBM * kBN) + c * 8 + 4));
-              v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
-              v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
-            }
+          for (int h = 0; h < C::kMSub; ++h) {
+            const int row_in_tile = h * 128 + row_in_sub;
+            const int64_t row = static_cast<int64_t>(tm) * BM + row_in_tile;
+            const float* base = p.partials + static_cast<int64_t>(tile_id) * p.split * (BM * BN) +
+                                row_in_tile * BN;
+#pragma unroll 1
+            for (int c = 0; c < BN / 8 && row < p.M; ++c) {
+              float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+              for (int j = 0; j < p.split; ++j) {
+                const float4 x0 = __ldcg(reinterpret_cast<const float4*>(base + j * (BM * BN) + c * 8));
+                const float4 x1 =
+                    __ldcg(reinterpret_cast<const float4*>(base + j * (BM * BN) + c * 8 + 4));
+                v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
+                v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
+              }
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] *= p.out_scale;
-            const int col = col0 + c * 8;
-            if (col < p.N)
-              store8(p.out, p.out_dtype, row * p.ldc + col, v, col + 8 <= p.N, min(8, p.N - col));
+              for (int e = 0; e < 8; ++e) v[e] *= p.out_scale;
+              const int col = col0 + c * 8;
+              if (col < p.N)
+                store8(p.out, p.out_dtype, row * p.ldc + col, v, col + 8 <= p.N, min(8, p.N - col));
+            }
           }
           named_bar_sync(1, kEpiWarps * 32);
           if (tid == kEpiWarp0 * 32) p.sems[tile_id] = 0u;  // re-arm
@@ -329,14 +355,27 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
     }
   } else if (kInt4 && warp >= kDeqWarp0) {
     // ------------------------ dequant (W4A16 prefill) ------------------------
-    // Stage: packed rows [kBK = 64][128 B] -> B tile [64 k][256 n] MN-major.
-    // Lane mapping: a 16-byte shared access is serviced a quarter-warp (8
-    // lanes) at a time, so each quarter reads 8 different 16-byte quads of the
-    // packed rows and writes 8 different bank groups of the swizzled B tile:
-    // lane t of quarter k takes quad wq = t of row 4*warp + ((t/2 + k) & 3).
+    // Stage: packed rows [kBK = 64][kBN/2 bytes] -> B tile [64 k][kBN n],
+    // MN-major. A 16-byte shared access is serviced a quarter-warp (8 lanes) at
+    // a time, so each quarter reads 8 different bank groups of the packed rows
+    // and writes 8 different bank groups of the swizzled tile:
+    //  * 128-byte rows (kBN = 256): quarter k of warp w, lane t takes quad t of
+    //    rows 4w + ((t/2 + k) & 3) and that row + 32;
+    //  * 64-byte rows (kBN = 128): quarter k of warp w, lane t takes quad t % 4
+    //    of row 8w + 4(k/2) + 2((q/2) ^ (k%2)) + t/4.
+    constexpr int kRowBytes = BN / 2;
+    constexpr int kQuads = kRowBytes / 16;             // 16-byte quads per packed row
+    constexpr int kRowsPerThread = (C::kBK * kQuads) / (kDeqWarps * 32);  // 2 or 1
     const int dt = tid - kDeqWarp0 * 32;   // 0..255
-    const int wq = lane & 7;                // 16-byte quad: columns 32wq..32wq+31
-    const int r0 = 4 * (dt >> 5) + (((wq >> 1) + (lane >> 3)) & 3);  // rows r0 and r0 + 32
+    const int qk = lane >> 3, qt = lane & 7;
+    int wq, rbase;
+    if (kQuads == 8) {
+      wq = qt;
+      rbase = 4 * (dt >> 5) + (((qt >> 1) + qk) & 3);
+    } else {
+      wq = qt & 3;
+      rbase = 8 * (dt >> 5) + 4 * (qk >> 1) + 2 * ((wq >> 1) ^ (qk & 1)) + (qt >> 2);
+    }
     int it = 0, bit = 0;
     for (int u = blockIdx.x; u < num_units && !fail; u += gridDim.x) {
       int tm, tn, ks;
@@ -350,53 +389,53 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
           fail = !mbar_wait(&bempty[bb], ((bit / C::kBBufs) - 1) & 1, p.status, kSiteGemmDequant);
         if (fail) break;
         const uint8_t* stage = smem + C::kStageOff + st * C::kStageBytes;
-        const uint8_t* wsm = stage + C::kATile;
-        // Group scales of this thread's 32 columns, regrouped into the pair order
-        // int4_codes8 emits: (c0,c4) (c1,c5) (c2,c6) (c3,c7) per 8-column chunk.
-        // The scale row arrives 128B-swizzled (chunk c at row c/8, position
-        // (c%8) ^ (c/8)), so these reads are conflict-free too.
+        const uint8_t* sc = stage + C::kATile + C::kWTile;
+        // Group scales of this thread's 32 columns, regrouped to the pair order
+        // int4_codes8 emits; the scale row arrives 128B-swizzled (chunk c at row
+        // c/8, position (c%8) ^ (c/8)), so these reads are conflict-free.
         uint32_t sp[4][4];
         if (p.grouped) {
-          const uint8_t* sc = stage + C::kATile + C::kWTile;
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int c = 4 * wq + i;
-            const uint4 s4 = *reinterpret_cast<const uint4*>(sc + (c >> 3) * 128 + (((c & 7) ^ (c >> 3)) << 4));
+            const uint4 s4 =
+                *reinterpret_cast<const uint4*>(sc + (c >> 3) * 128 + (((c & 7) ^ (c >> 3)) << 4));
             sp[i][0] = prmt(s4.x, s4.z, 0x5410);
             sp[i][1] = prmt(s4.x, s4.z, 0x7632);
             sp[i][2] = prmt(s4.y, s4.w, 0x5410);
             sp[i][3] = prmt(s4.y, s4.w, 0x7632);
           }
         }
-        uint8_t* bt = smem + C::kBBufOff + bb * C::kBTile;
+        uint8_t* btile = smem + C::kBBufOff + bb * C::kBTile;
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int r = r0 + 32 * hh;
-          const uint4 wv = *reinterpret_cast<const uint4*>(wsm + r * 128 + wq * 16);
+        for (int rr = 0; rr < kRowsPerThread; ++rr) {
+          const int r = rbase + 32 * rr;
+          const int r8 = r & 7;
+          const uint4 wv =
+              *reinterpret_cast<const uint4*>(stage + C::kATile + r * kRowBytes + wq * 16);
           const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+          uint8_t* bt = btile + (r >> 3) * 1024 + r8 * 128;
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int c = 4 * wq + i;  // 8-column chunk 0..31
-            const uint32_t s04 = sp[i][0], s15 = sp[i][1], s26 = sp[i][2], s37 = sp[i][3];
+            const int c = 4 * wq + i;  // 8-column chunk
             uint32_t v[4];
-            if (p.a_is_f16) {
+            if (p.a_is_f16)
               int4_codes8<__half>(words[i], v);
-              if (p.grouped) {
-                __half* tag = nullptr;
-                v[0] = mul2(v[0], s04, tag); v[1] = mul2(v[1], s15, tag);
-                v[2] = mul2(v[2], s26, tag); v[3] = mul2(v[3], s37, tag);
-              }
-            } else {
+            else
               int4_codes8<__nv_bfloat16>(words[i], v);
-              if (p.grouped) {
+            if (p.grouped) {
+              if (p.a_is_f16) {
+                __half* tag = nullptr;
+                v[0] = mul2(v[0], sp[i][0], tag); v[1] = mul2(v[1], sp[i][1], tag);
+                v[2] = mul2(v[2], sp[i][2], tag); v[3] = mul2(v[3], sp[i][3], tag);
+              } else {
                 __nv_bfloat16* tag = nullptr;
-                v[0] = mul2(v[0], s04, tag); v[1] = mul2(v[1], s15, tag);
-                v[2] = mul2(v[2], s26, tag); v[3] = mul2(v[3], s37, tag);
+                v[0] = mul2(v[0], sp[i][0], tag); v[1] = mul2(v[1], sp[i][1], tag);
+                v[2] = mul2(v[2], sp[i][2], tag); v[3] = mul2(v[3], sp[i][3], tag);
               }
             }
-            const int r8 = r & 7;
-            const int off = (c >> 3) * C::kBLBO + (r >> 3) * 1024 + r8 * 128 + (((c & 7) ^ r8) << 4);
-            *reinterpret_cast<uint4*>(bt + off) = make_uint4(v[0], v[1], v[2], v[3]);
+            *reinterpret_cast<uint4*>(bt + (c >> 3) * C::kBLBO + (((c & 7) ^ r8) << 4)) =
+                make_uint4(v[0], v[1], v[2], v[3]);
           }
         }
         fence_proxy_async_smem();
@@ -414,12 +453,6 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
   if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
 }
 
-}  // namespace
-}  // namespace pk
-
-namespace pk {
-namespace {
-
 CUtensorMapDataType elem_tmap(int dt) {
   switch (dt) {
     case PK_BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -433,18 +466,18 @@ cudaError_t launch_typed(const GemmArgs& g, cudaStream_t s, const char** why) {
   using C = Cfg<kKind, kInt4>;
   const int elem = C::kElem;
   CUtensorMap tmA, tmB, tmS;
-  if (!encode_tmap_2d(&tmA, elem_tmap(g.a_dtype), g.a, g.K, g.M, g.lda * elem, C::kBK, kBM,
+  if (!encode_tmap_2d(&tmA, elem_tmap(g.a_dtype), g.a, g.K, g.M, g.lda * elem, C::kBK, C::kBM,
                       CU_TENSOR_MAP_SWIZZLE_128B, why))
     return cudaErrorInvalidValue;
   if (kInt4) {
-    if (!encode_tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.b, g.N / 2, g.K, g.N / 2, kBN / 2,
-                        C::kBK, CU_TENSOR_MAP_SWIZZLE_NONE, why))
+    if (!encode_tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.b, g.N / 2, g.K, g.N / 2,
+                        C::kBN / 2, C::kBK, CU_TENSOR_MAP_SWIZZLE_NONE, why))
       return cudaErrorInvalidValue;
     if (g.scales != nullptr) {
       const int64_t G = (g.K + g.group - 1) / g.group;
-      // the scales viewed as rows of 64 (128 bytes), four rows per 256-column tile
-      if (!encode_tmap_2d(&tmS, elem_tmap(g.a_dtype), g.scales, 64, G * (g.N / 64), 128, 64, 4,
-                          CU_TENSOR_MAP_SWIZZLE_128B, why))
+      // the scales viewed as rows of 64 (128 bytes), kSRows rows per column tile
+      if (!encode_tmap_2d(&tmS, elem_tmap(g.a_dtype), g.scales, 64, G * (g.N / 64), 128, 64,
+                          C::kSRows, CU_TENSOR_MAP_SWIZZLE_128B, why))
         return cudaErrorInvalidValue;
     } else {
       tmS = tmB;  // unused
@@ -460,15 +493,14 @@ cudaError_t launch_typed(const GemmArgs& g, cudaStream_t s, const char** why) {
   p.N = static_cast<int>(g.N);
   p.K = static_cast<int>(g.K);
   p.split = g.split;
-  p.num_m = static_cast<int>((g.M + kBM - 1) / kBM);
-  p.num_n = static_cast<int>((g.N + kBN - 1) / kBN);
+  p.num_m = static_cast<int>((g.M + C::kBM - 1) / C::kBM);
+  p.num_n = static_cast<int>((g.N + C::kBN - 1) / C::kBN);
   p.out_dtype = g.out_dtype;
   p.ldc = g.ldc;
   p.out_scale = g.out_scale;
   p.out = g.out;
   p.partials = g.partials;
   p.sems = g.sems;
-  p.scales = g.scales;
   p.group = g.group > 0 ? g.group : 1;
   p.grouped = g.scales != nullptr;
   p.a_is_f16 = g.a_dtype == PK_F16;
@@ -482,15 +514,20 @@ cudaError_t launch_typed(const GemmArgs& g, cudaStream_t s, const char** why) {
   return cudaGetLastError();
 }
 
+// dense split-K tiles (the only configuration that uses the workspace)
+using DenseCfg = Cfg<kF16, false>;
+
 }  // namespace
 
-int64_t gemm_tiles(int64_t M, int64_t N) { return ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN); }
+int64_t gemm_tiles(int64_t M, int64_t N) {
+  return ((M + DenseCfg::kBM - 1) / DenseCfg::kBM) * ((N + DenseCfg::kBN - 1) / DenseCfg::kBN);
+}
 
 size_t gemm_splitk_workspace_bytes(int64_t M, int64_t N, int split) {
   if (split <= 1) return 0;
   const int64_t tiles = gemm_tiles(M, N);
   const size_t sem_bytes = ((tiles * sizeof(unsigned) + 255) / 256) * 256;
-  return sem_bytes + static_cast<size_t>(tiles) * split * kBM * kBN * sizeof(float);
+  return sem_bytes + static_cast<size_t>(tiles) * split * DenseCfg::kBM * DenseCfg::kBN * sizeof(float);
 }
 
 cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t s, const char** why) {
