@@ -50,12 +50,28 @@ WORKLOADS = {
     "fp8_2048": dict(kind="fp8", M=2048, N=2048, K=2048),
     "fp8_4096": dict(kind="fp8", M=4096, N=4096, K=4096),
     "fp8_8192": dict(kind="fp8", M=8192, N=8192, K=8192),
+    # Llama-70B MLP layers sharded along N over the ranks, output all-gathered
+    # with NCCL; strong scaling: the layer is fixed, ranks split it
+    "llama70b_up_m1": dict(kind="w4a16", M=1, N=28672, K=8192, sharded=True),
+    "llama70b_up_m32": dict(kind="w4a16", M=32, N=28672, K=8192, sharded=True),
+    "llama70b_up_m256": dict(kind="w4a16", M=256, N=28672, K=8192, sharded=True),
+    "llama70b_down_m1": dict(kind="w4a16", M=1, N=8192, K=28672, sharded=True),
+    "llama70b_down_m32": dict(kind="w4a16", M=32, N=8192, K=28672, sharded=True),
+    "llama70b_down_m256": dict(kind="w4a16", M=256, N=8192, K=28672, sharded=True),
+    "llama70b_up_fp8_m4096": dict(kind="fp8", M=4096, N=28672, K=8192, sharded=True),
 }
 DEFAULT_WORKLOAD = "w4a16_decode_m1"
 
 
 def is_hbm_bound(wl: dict) -> bool:
-    return wl["kind"] == "w4a16" and wl["M"] <= 16
+    """Decode-sized W4A16 GEMMs are bound by streaming the weights; the rest by
+    the tensor cores (2*M*N*K at the bf16 peak vs the weight bytes at HBM peak)."""
+    if wl["kind"] != "w4a16":
+        return False
+    M, N, K = wl["M"], wl["N"], wl["K"]
+    t_flops = 2.0 * M * N * K / 1654e12
+    t_bytes = (K * N / 2 + K / 128 * N * 2) / 6553e9
+    return t_bytes >= t_flops
 
 
 # ---------------------------------------------------------------------------
@@ -180,9 +196,14 @@ def barrier(dist):
 # ---------------------------------------------------------------------------
 class Workload:
     """Rotating input sets (so each step's inputs are not L2-resident) and the
-    step that runs one GEMM on set i through the C ABI."""
+    step that runs one GEMM on set i through the C ABI.
 
-    def __init__(self, name: str, wl: dict, device: torch.device, split_k: int):
+    Sharded workloads: every rank builds the same seeded layer and keeps its
+    contiguous slice of N columns; a step is the local GEMM, then the NCCL
+    all-gather of the [M, N/p] blocks into [M, N] (reordered for M > 1)."""
+
+    def __init__(self, name: str, wl: dict, device: torch.device, split_k: int,
+                 world: int = 1, rank: int = 0, dist=None):
         from pico_kernels_b200 import _lib
         self.name, self.wl, self.device = name, wl, device
         self.lib = _lib.load()
@@ -191,11 +212,19 @@ class Workload:
         self.kind = wl["kind"]
         self.split_k = split_k
         self.hbm = is_hbm_bound(wl)
+        self.sharded = bool(wl.get("sharded"))
+        self.world = world if self.sharded else 1
+        self.rank = rank if self.sharded else 0
+        self.dist = dist
         M, N, K = self.M, self.N, self.K
+        if self.sharded and (N % self.world or (N // self.world) % 128):
+            raise ValueError(f"N={N} does not shard over {self.world} ranks")
+        self.NL = N // self.world                      # local columns
+        n0 = self.rank * self.NL
         if self.kind == "w4a16":
-            per_set = K * N // 2 + (K // 128) * N * 2 + M * K * 2
+            per_set = K * self.NL // 2 + (K // 128) * self.NL * 2 + M * K * 2
         else:
-            per_set = M * K + K * N
+            per_set = M * K + K * self.NL
         self.n_sets = max(2, int(2 * L2_BYTES // per_set) + 1)
         self.set_bytes = per_set
         g = torch.Generator(device=device).manual_seed(0)
@@ -207,41 +236,72 @@ class Workload:
                 w = (torch.randn(K, N, device=device, generator=g) * 0.02).to(torch.bfloat16)
                 packed, scales = pk.quantize_int4_grouped(w, 128)
                 del w
+                if self.sharded:
+                    packed = packed[:, n0 // 2:(n0 + self.NL) // 2].contiguous()
+                    scales = scales[:, n0:n0 + self.NL].contiguous()
                 a = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
                 self.sets.append((a, packed, scales))
             else:
                 a8, sa = gemm_fp8.quantize(torch.randn(M, K, device=device, generator=g).to(torch.bfloat16))
                 b8, sb = gemm_fp8.quantize(torch.randn(K, N, device=device, generator=g).to(torch.bfloat16))
+                if self.sharded:
+                    b8 = b8[:, n0:n0 + self.NL].contiguous()
                 self.sets.append((a8, b8, 1.0 / (sa * sb)))
+        torch.cuda.empty_cache()
+        # fp8 layers write bf16 (configs[3]: "bf16 output rescaled in the epilogue")
+        self.out_dtype = torch.float32 if self.kind == "w4a16" else torch.bfloat16
+        self.out_code = _lib.PK_F32 if self.kind == "w4a16" else _lib.PK_BF16
         # decode outputs are tiny: one per set; large outputs share one buffer
         n_out = self.n_sets if self.hbm else 1
-        self.outs = [torch.empty((M, N), dtype=torch.float32, device=device) for _ in range(n_out)]
-        self.ws_bytes = (self.lib.pk_w4a16_workspace_size(M, N, K, split_k)
+        self.outs = [torch.empty((M, self.NL), dtype=self.out_dtype, device=device)
+                     for _ in range(n_out)]
+        if self.sharded and self.world > 1:
+            self.gather = torch.empty((self.world * M, self.NL), dtype=self.out_dtype, device=device)
+            self.full = torch.empty((M, N), dtype=self.out_dtype, device=device)
+        self.ws_bytes = (self.lib.pk_w4a16_workspace_size(M, self.NL, K, split_k)
                          if self.kind == "w4a16" else 0)
         self.ws = _lib.workspace(device, self.ws_bytes, tag="bench")
         torch.cuda.synchronize()
 
-    def step(self, i: int) -> None:
-        lib, L, M, N, K = self.lib, self._lib, self.M, self.N, self.K
+    def gemm(self, i: int) -> torch.Tensor:
+        lib, L, M, K, NL = self.lib, self._lib, self.M, self.K, self.NL
         stream = torch.cuda.current_stream().cuda_stream
         out = self.outs[i % len(self.outs)]
         if self.kind == "w4a16":
             a, packed, scales = self.sets[i]
             st = lib.pk_w4a16_gemm(a.data_ptr(), L.PK_BF16, K, packed.data_ptr(), scales.data_ptr(),
-                                   1.0, 128, M, N, K, out.data_ptr(), L.PK_F32, N, self.split_k,
-                                   L.ptr(self.ws), self.ws_bytes, stream)
+                                   1.0, 128, M, NL, K, out.data_ptr(), self.out_code, NL,
+                                   self.split_k, L.ptr(self.ws), self.ws_bytes, stream)
         else:
             a8, b8, out_scale = self.sets[i]
-            st = lib.pk_fp8_gemm(a8.data_ptr(), b8.data_ptr(), M, N, K, out_scale, out.data_ptr(),
-                                 L.PK_F32, stream)
+            st = lib.pk_fp8_gemm(a8.data_ptr(), b8.data_ptr(), M, NL, K, out_scale, out.data_ptr(),
+                                 self.out_code, stream)
         L.check(st, self.name)
+        return out
 
-    # algorithmic work of one step
+    def all_gather(self, local: torch.Tensor) -> None:
+        self.dist.all_gather_into_tensor(self.gather, local)
+        if self.M > 1:
+            self.full.copy_(self.gather.view(self.world, self.M, self.NL).permute(1, 0, 2)
+                            .reshape(self.M, self.N))
+
+    def step(self, i: int) -> None:
+        out = self.gemm(i)
+        if self.sharded and self.world > 1:
+            self.all_gather(out)
+
+    def gemm_only(self, i: int) -> None:
+        self.gemm(i)
+
+    def gather_only(self, i: int) -> None:
+        self.all_gather(self.outs[i % len(self.outs)])
+
+    # algorithmic work of one step (the whole layer, all ranks together)
     def bytes_per_step(self) -> int:
         M, N, K = self.M, self.N, self.K
         if self.kind == "w4a16":
             return K * N // 2 + (K // 128) * N * 2 + M * K * 2 + M * N * 4
-        return M * K + K * N + M * N * 4
+        return M * K + K * N + M * N * 2
 
     def flops_per_step(self) -> int:
         return 2 * self.M * self.N * self.K
@@ -249,31 +309,32 @@ class Workload:
     def e2e_step_fn(self):
         """Public-API step with host buffers: H2D of the activations, D2H of Y."""
         import pico_kernels_b200 as pk
-        from pico_kernels_b200 import gemm_fp8
-        M, N, K = self.M, self.N, self.K
+        from pico_kernels_b200 import gemm_fp8, sharded
+        M, N, K, NL = self.M, self.N, self.K, self.NL
+        y_host = torch.empty((M, N), dtype=self.out_dtype).pin_memory()
+        world = self.world if self.sharded else 1
         if self.kind == "w4a16":
             a_host = torch.empty((M, K), dtype=torch.bfloat16).pin_memory()
             a_host.copy_(self.sets[0][0])
             a_dev = torch.empty((M, K), dtype=torch.bfloat16, device=self.device)
-            y_host = torch.empty((M, N), dtype=torch.float32).pin_memory()
 
             def fn(i):
                 _, packed, scales = self.sets[i % self.n_sets]
                 a_dev.copy_(a_host, non_blocking=True)
-                y = pk.int4_gemm(a_dev, packed, scales)
+                y = sharded.sharded_int4_gemm(a_dev, packed, scales, 128, world)
                 y_host.copy_(y, non_blocking=True)
             return fn, M * K * 2, M * N * 4
         a8_host = torch.empty((M, K), dtype=torch.uint8).pin_memory()
         a8_host.copy_(self.sets[0][0].view(torch.uint8))
         a8_dev = torch.empty((M, K), dtype=torch.float8_e4m3fn, device=self.device)
-        y_host = torch.empty((M, N), dtype=torch.float32).pin_memory()
 
         def fn(i):
             _, b8, out_scale = self.sets[i % self.n_sets]
             a8_dev.view(torch.uint8).copy_(a8_host, non_blocking=True)
-            y = gemm_fp8.fp8_gemm_precast(a8_dev, 1.0, b8, 1.0 / out_scale)
+            y = sharded.sharded_fp8_gemm(a8_dev, 1.0, b8, 1.0 / out_scale, world,
+                                         out_dtype=torch.bfloat16)
             y_host.copy_(y, non_blocking=True)
-        return fn, M * K, M * N * 4
+        return fn, M * K, M * N * 2
 
 
 def capture_runner(step_fn, n_sets: int, steps: int, chunk: int = 1000):
@@ -301,6 +362,22 @@ def capture_runner(step_fn, n_sets: int, steps: int, chunk: int = 1000):
     return (graph_for(chunk) if full else None), full, (graph_for(rem) if rem else None)
 
 
+def _time_graphs(runner_out, dist) -> float:
+    """Replay (graph, n, remainder) on the device; return ms (max over ranks)."""
+    g, n, grem = runner_out
+    barrier(dist)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        g.replay()
+    if grem is not None:
+        grem.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return max_over_ranks(dist, e0.elapsed_time(e1))
+
+
 def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
     import pico_kernels_b200 as pk
 
@@ -308,16 +385,17 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
     torch.cuda.set_device(device)
     dist = init_dist(world, local)
     peaks = load_peaks()
-    work = Workload(args.workload, wl, device, args.split_k)
+    work = Workload(args.workload, wl, device, args.split_k, world, rank, dist)
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     chunk = 1000 if work.hbm else 20
+    gathered = work.sharded and world > 1
 
-    gw, nw, gwr = capture_runner(work.step, work.n_sets, args.warmup, chunk)
-    for _ in range(nw):
-        gw.replay()
-    if gwr is not None:
-        gwr.replay()
-    gfull, nfull, grem = capture_runner(work.step, work.n_sets, args.steps, chunk)
+    warm = capture_runner(work.step, work.n_sets, args.warmup, chunk)
+    for _ in range(warm[1]):
+        warm[0].replay()
+    if warm[2] is not None:
+        warm[2].replay()
+    timed = capture_runner(work.step, work.n_sets, args.steps, chunk)
     torch.cuda.synchronize()
 
     clocks = ClockSampler(local)
@@ -328,10 +406,10 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
     ev0.record()
-    for _ in range(nfull):
-        gfull.replay()
-    if grem is not None:
-        grem.replay()
+    for _ in range(timed[1]):
+        timed[0].replay()
+    if timed[2] is not None:
+        timed[2].replay()
     ev1.record()
     torch.cuda.synchronize()
     t1 = time.perf_counter()
@@ -342,6 +420,20 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
     code, where = pk.device_status()
     if code != 0:
         raise RuntimeError(f"device status {code} at site {where}")
+
+    # sharded layers: time the local GEMM and the all-gather on their own too
+    breakdown = None
+    gemm_ms_local = ms
+    if gathered:
+        nb = min(args.steps, 1000 if work.hbm else 50)
+        g_gemm = capture_runner(work.gemm_only, work.n_sets, nb, chunk)
+        g_gath = capture_runner(work.gather_only, work.n_sets, nb, chunk)
+        gemm_ms = _time_graphs(g_gemm, dist)
+        gath_ms = _time_graphs(g_gath, dist)
+        gemm_ms_local = gemm_ms * args.steps / nb
+        breakdown = {"gemm_us": round(gemm_ms / nb * 1e3, 3),
+                     "allgather_us": round(gath_ms / nb * 1e3, 3), "steps": nb}
+        del g_gemm, g_gath
 
     # end to end through the public API, host buffers in and out every step
     e2e_fn, h2d, d2h = work.e2e_step_fn()
@@ -357,6 +449,8 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(dist, e0.elapsed_time(e1))
+    del warm, timed  # graphs holding NCCL calls go before the process group
+    torch.cuda.synchronize()
 
     if rank != 0:
         if dist is not None:
@@ -364,14 +458,19 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
         return
 
     sec = ms_max * 1e-3
-    sec_per_step_local = ms * 1e-3 / args.steps
+    # roofline of the dominant kernel: this rank's GEMM launch
+    sec_per_launch = gemm_ms_local * 1e-3 / args.steps
+    replicas = 1 if work.sharded else world
     if work.hbm:
         per = work.bytes_per_step()
+        local_per = per if not work.sharded else (
+            work.K * work.NL // 2 + (work.K // 128) * work.NL * 2 + work.M * work.K * 2 + work.M * work.NL * 4)
         unit, scale = "GB/s", 1e9
         peak, bound, punit = peaks["hbm_gbs"], "hbm", "GB/s"
         peak_note = peaks["source"]
     else:
         per = work.flops_per_step()
+        local_per = per // (world if work.sharded else 1)
         unit, scale = "TFLOP/s", 1e12
         long_region = sec > 1.0
         bf16 = peaks["bf16_tflops_sustained"] if long_region else peaks["bf16_tflops"]
@@ -382,21 +481,27 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
             peak = bf16
             peak_note = f"{'sustained' if long_region else 'burst'} bf16 ({peaks['source']})"
         bound, punit = "tensor", "TFLOP/s"
-    value = world * per * args.steps / sec / scale
-    achieved = per / sec_per_step_local / scale
-    e2e_value = world * per * e2e_steps / (e2e_ms * 1e-3) / scale
+    value = replicas * per * args.steps / sec / scale
+    achieved = local_per / sec_per_launch / scale
+    e2e_value = replicas * per * e2e_steps / (e2e_ms * 1e-3) / scale
     wl_cfg = {"workload": args.workload, "M": work.M, "N": work.N, "K": work.K}
     if work.kind == "w4a16":
         wl_cfg.update({"group_size": 128, "weights": "int4 packed [K, N/2] + bf16 scales [K/128, N]",
                        "activations": "bf16", "output": "fp32",
                        "split_k": args.split_k if args.split_k > 0 else "auto"})
     else:
-        wl_cfg.update({"inputs": "e4m3 [M,K] x e4m3 [K,N], per-tensor scales", "output": "fp32",
+        wl_cfg.update({"inputs": "e4m3 [M,K] x e4m3 [K,N], per-tensor scales",
+                       "output": "bf16 (rescaled in the epilogue)",
                        "cast": "excluded from the timed region (gemm_fp8.py:144)"})
+    if work.sharded:
+        par = (f"N sharded over {world} GPUs ({work.NL} columns each), NCCL all-gather of the output"
+               if world > 1 else "single GPU (unsharded)")
+    else:
+        par = f"replicas x{world}" if world > 1 else "single GPU"
     wl_cfg.update({
-        "l2": f"{work.n_sets} rotating input sets ({work.n_sets * work.set_bytes / 2**20:.0f} MiB > 126 MiB L2)",
-        "launch": "CUDA graphs of back-to-back GEMMs",
-        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+        "l2": f"{work.n_sets} rotating input sets per GPU ({work.n_sets * work.set_bytes / 2**20:.0f} MiB > 126 MiB L2)",
+        "launch": "CUDA graphs of back-to-back steps",
+        "parallelism": par,
     })
     line = {
         "metric": METRIC,
@@ -408,7 +513,7 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
         "ms_per_step": ms_max / args.steps,
         "us_per_gemm": round(ms_max / args.steps * 1e3, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if work.sharded else "weak",
         "vs_baseline": None,
         "dtype": "bf16" if work.kind == "w4a16" else "e4m3",
         "data": "synthetic (seeded N(0,0.02) weights quantized on device, N(0,1) activations)",
@@ -416,7 +521,7 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
         "roofline": {
             "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": punit,
             "frac": round(achieved / peak, 4), "peak_source": peak_note, "traffic": args.traffic,
-            ("algorithmic_bytes_per_launch" if work.hbm else "algorithmic_flops_per_launch"): per,
+            ("algorithmic_bytes_per_launch" if work.hbm else "algorithmic_flops_per_launch"): local_per,
             "sms": sms,
         },
         "e2e": {"value": round(e2e_value, 4), "unit": unit, "h2d_bytes_per_step": h2d,
@@ -426,6 +531,8 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
         "gpu_launches": args.steps,
         "clocks": clocks.summary(t0, t1),
     }
+    if breakdown is not None:
+        line["breakdown"] = breakdown
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(wl, budget_s=args.cpu_seconds)
     print(json.dumps(line), flush=True)

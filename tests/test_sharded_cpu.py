@@ -1,0 +1,90 @@
+"""Host logic of the N-sharded layers on world_size-2 gloo ranks (no GPU).
+
+The local GEMM is injected (the oracle's dequantize-then-matmul on CPU), so
+these tests check the sharding, the all-gather and the reassembly of
+rank-major column blocks, against the unsharded oracle result.
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import quant_ref as o
+from pico_kernels_b200 import sharded
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _cpu_int4_gemm(a, packed, scales, group_size=128):
+    codes = o.unpack_int4_n(packed.numpy())
+    y = o.w4a16_reference(a.float().numpy(), codes, scales.float().numpy(), group_size)
+    return torch.from_numpy(y)
+
+
+def _cpu_fp8_gemm(a8, sa, b8, sb):
+    return torch.from_numpy(o.fp8_gemm_reference(a8.numpy(), sa, b8.numpy(), sb))
+
+
+def _worker(rank, world, port, M, N, K, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(0)
+        w = rng.standard_normal((K, N), dtype=np.float32) * 0.02
+        codes, s32 = o.group_quant_codes(w, 128)
+        packed = torch.from_numpy(o.pack_int4_n(codes))
+        scales = torch.from_numpy(s32)
+        a = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32))
+        p_r, s_r = sharded.shard_int4(packed, scales, world, rank)
+        y = sharded.sharded_int4_gemm(a, p_r, s_r, 128, world, local_gemm=_cpu_int4_gemm)
+        ref = o.w4a16_reference(a.numpy(), codes, s32, 128)
+        ok_int4 = bool(np.allclose(y.numpy(), ref, rtol=1e-5, atol=1e-5))
+
+        a8, sa = o.fp8_quantize(a.numpy(), "f32")
+        b8, sb = o.fp8_quantize(rng.standard_normal((K, N), dtype=np.float32), "f32")
+        n0, n1 = sharded.shard_columns(N, world, rank)
+        yf = sharded.sharded_fp8_gemm(torch.from_numpy(a8), sa,
+                                      torch.from_numpy(np.ascontiguousarray(b8[:, n0:n1])), sb,
+                                      world, local_gemm=_cpu_fp8_gemm)
+        reff = o.fp8_gemm_reference(a8, sa, b8, sb)
+        ok_fp8 = bool(np.allclose(yf.numpy(), reff, rtol=1e-6, atol=1e-6))
+        q.put((rank, ok_int4, ok_fp8, tuple(y.shape)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("M", [1, 3])
+def test_sharded_layers_two_gloo_ranks(M):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, M, 512, 256, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    results = sorted(q.get(timeout=5) for _ in range(2))
+    for rank, ok_int4, ok_fp8, shape in results:
+        assert shape == (M, 512)
+        assert ok_int4, f"rank {rank} int4"
+        assert ok_fp8, f"rank {rank} fp8"
+
+
+def test_shard_columns_rules():
+    assert sharded.shard_columns(28672, 8, 7) == (25088, 28672)
+    assert sharded.shard_columns(8192, 8, 0) == (0, 1024)
+    with pytest.raises(ValueError):
+        sharded.shard_columns(1000, 8, 0)

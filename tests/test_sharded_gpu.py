@@ -1,0 +1,85 @@
+"""N-sharded W4A16 / fp8 layers on GPUs with NCCL (one process per GPU).
+
+With at least two GPUs, two ranks each compute their column slice with the
+sm_100a kernels and all-gather the output over NVLink; the result must equal
+the unsharded kernel's output (same kernels, same per-column arithmetic).
+With one GPU the single-rank path is checked.
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import pico_kernels_b200 as pk
+from pico_kernels_b200 import gemm_fp8, sharded
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _layer(M, N, K, device):
+    g = torch.Generator(device=device).manual_seed(0)
+    w = (torch.randn(K, N, device=device, generator=g) * 0.02).to(torch.bfloat16)
+    a = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
+    packed, scales = pk.quantize_int4_grouped(w, 128)
+    return a, packed, scales
+
+
+def _worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        ok = []
+        for M, N, K in ((1, 2048, 1024), (16, 1024, 2048), (40, 1024, 512)):
+            a, packed, scales = _layer(M, N, K, dev)
+            full = pk.int4_gemm(a, packed, scales)
+            p_r, s_r = sharded.shard_int4(packed, scales, world, rank)
+            y = sharded.sharded_int4_gemm(a, p_r, s_r, 128, world)
+            # the unsharded and sharded runs may pick different split-K factors
+            rel = (torch.norm(y - full) / torch.norm(full)).item()
+            ok.append(rel < 1e-5)
+        a8, sa = gemm_fp8.quantize(torch.randn(256, 512, device=dev))
+        b8, sb = gemm_fp8.quantize(torch.randn(512, 1024, device=dev))
+        full = gemm_fp8.fp8_gemm_precast(a8, sa, b8, sb)
+        n0, n1 = sharded.shard_columns(1024, world, rank)
+        y = sharded.sharded_fp8_gemm(a8, sa, b8[:, n0:n1].contiguous(), sb, world)
+        ok.append(bool(torch.equal(y, full)))
+        q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_single_rank_path():
+    a, packed, scales = _layer(4, 1024, 1024, torch.device("cuda"))
+    y = sharded.sharded_int4_gemm(a, packed, scales, 128, world=1)
+    assert torch.equal(y, pk.int4_gemm(a, packed, scales))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_nccl_all_gather():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
+    for rank, ok in sorted(q.get(timeout=5) for _ in range(2)):
+        assert all(ok), (rank, ok)
