@@ -53,8 +53,9 @@ def _worker(rank, world, port, q):
             # the unsharded and sharded runs may pick different split-K factors
             rel = (torch.norm(y - full) / torch.norm(full)).item()
             ok.append(rel < 1e-5)
-        a8, sa = gemm_fp8.quantize(torch.randn(256, 512, device=dev))
-        b8, sb = gemm_fp8.quantize(torch.randn(512, 1024, device=dev))
+        g = torch.Generator(device=dev).manual_seed(1)  # the same inputs on every rank
+        a8, sa = gemm_fp8.quantize(torch.randn(256, 512, device=dev, generator=g))
+        b8, sb = gemm_fp8.quantize(torch.randn(512, 1024, device=dev, generator=g))
         full = gemm_fp8.fp8_gemm_precast(a8, sa, b8, sb)
         n0, n1 = sharded.shard_columns(1024, world, rank)
         y = sharded.sharded_fp8_gemm(a8, sa, b8[:, n0:n1].contiguous(), sb, world)
