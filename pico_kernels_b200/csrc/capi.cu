@@ -210,10 +210,16 @@ int pk_unpack_int4_n(const uint8_t* packed, int64_t K, int64_t N, int8_t* q, voi
 
 size_t pk_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int split_k) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  if (!decode_supported(M, N, K, 128, nullptr, 8, reinterpret_cast<const void*>(16)))
-    return 0;
-  const int split = split_k > 0 ? split_k : decode_pick_split(M, N, K);
-  return decode_workspace_bytes(M, N, K, split);
+  const void* aligned = reinterpret_cast<const void*>(16);
+  size_t bytes = 0;
+  if (split_k == 0 && gemv_supported(M, N, K, 128, aligned, 8, aligned, aligned))
+    bytes = gemv_workspace_bytes(M, N, K);
+  if (decode_supported(M, N, K, 128, nullptr, 8, aligned)) {
+    const int split = split_k > 0 ? split_k : decode_pick_split(M, N, K);
+    const size_t d = decode_workspace_bytes(M, N, K, split);
+    if (d > bytes) bytes = d;
+  }
+  return bytes;
 }
 
 int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t* wp, const void* scales,
@@ -232,12 +238,55 @@ int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t* wp, co
   if (split_k < 0) return fail(PK_ERR_SHAPE, "split_k must be >= 0");
   cudaStream_t s = as_stream(stream);
 
+  // M <= 4 with the automatic split: the CUDA-core GEMV (a weight stream).
+  if (split_k == 0 && gemv_supported(M, N, K, group_size, scales, lda, a, wp)) {
+    const size_t need = gemv_workspace_bytes(M, N, K);
+    bool have_ws = need == 0;
+    if (need > 0 && workspace != nullptr) {
+      if (workspace_bytes < need)
+        return fail(PK_ERR_WORKSPACE, "the GEMV needs %zu workspace bytes, got %zu", need,
+                    workspace_bytes);
+      if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+        return fail(PK_ERR_ALIGN, "workspace must be 256-byte aligned");
+      have_ws = true;
+    }
+    if (have_ws) {  // without a workspace the tensor-core decode below reduces in clusters
+      DecodeArgs p{};
+      p.a = a;
+      p.lda = lda;
+      p.wp = wp;
+      p.scales = scales;
+      p.group = group_size;
+      p.scalar_scale = scales ? 1.0f : scalar_scale;
+      p.M = M;
+      p.N = N;
+      p.K = K;
+      p.out = out;
+      p.out_dtype = out_dtype;
+      p.ldo = ldo;
+      p.a_dtype = a_dtype;
+      p.split = 1;
+      p.status = device_status_ptr();
+      if (need > 0) {
+        p.sems = ws_counters(workspace);
+        p.partials = ws_partials(workspace);
+      }
+      const char* why = "";
+      cudaError_t e = launch_w4a16_gemv(p, s, &why);
+      if (e == cudaErrorInvalidValue && why[0] != '\0') return fail(PK_ERR_ALIGN, "%s", why);
+      if (e != cudaSuccess) return cuda_fail(e, "w4a16 gemv launch");
+      ok();
+      return PK_OK;
+    }
+  }
+
   if (decode_supported(M, N, K, group_size, scales, lda, a)) {
     DecodeArgs p{};
     p.a = a;
     p.lda = lda;
     p.wp = wp;
     p.scales = scales;
+    p.group = group_size;
     p.scalar_scale = scales ? 1.0f : scalar_scale;
     p.M = M;
     p.N = N;
@@ -257,10 +306,8 @@ int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t* wp, co
                     workspace_bytes);
       if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
         return fail(PK_ERR_ALIGN, "workspace must be 256-byte aligned");
-      const int64_t tiles = N / 128;
-      const size_t sem_bytes = ((tiles * sizeof(unsigned) + 255) / 256) * 256;
-      p.sems = static_cast<unsigned*>(workspace);
-      p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + sem_bytes);
+      p.sems = ws_counters(workspace);
+      p.partials = ws_partials(workspace);
     }
     if (split > decode_max_cluster_split() && p.partials == nullptr)
       return fail(PK_ERR_WORKSPACE, "split_k > %d needs %zu workspace bytes",
@@ -407,10 +454,11 @@ int pk_gemm_splitk(const void* a, const void* b, int dtype, int64_t M, int64_t N
                   workspace_bytes);
     if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
       return fail(PK_ERR_ALIGN, "workspace must be 256-byte aligned");
-    const int64_t tiles = gemm_tiles(M, N);
-    const size_t sem_bytes = ((tiles * sizeof(unsigned) + 255) / 256) * 256;
-    g.sems = static_cast<unsigned*>(workspace);
-    g.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + sem_bytes);
+    if (gemm_tiles(M, N) > kMaxCounters)
+      return fail(PK_ERR_UNSUPPORTED, "split-K over more than %lld output tiles",
+                  static_cast<long long>(kMaxCounters));
+    g.sems = ws_counters(workspace);
+    g.partials = ws_partials(workspace);
   }
   const char* why = "";
   cudaError_t e = launch_gemm_tc(g, as_stream(stream), &why);

@@ -526,8 +526,8 @@ int64_t gemm_tiles(int64_t M, int64_t N) {
 size_t gemm_splitk_workspace_bytes(int64_t M, int64_t N, int split) {
   if (split <= 1) return 0;
   const int64_t tiles = gemm_tiles(M, N);
-  const size_t sem_bytes = ((tiles * sizeof(unsigned) + 255) / 256) * 256;
-  return sem_bytes + static_cast<size_t>(tiles) * split * DenseCfg::kBM * DenseCfg::kBN * sizeof(float);
+  return kCounterBytes +
+         static_cast<size_t>(tiles) * split * DenseCfg::kBM * DenseCfg::kBN * sizeof(float);
 }
 
 cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t s, const char** why) {

@@ -27,6 +27,8 @@ enum WaitSite : int {
   kSiteGemmMma = 202,
   kSiteGemmEpilogue = 203,
   kSiteGemmDequant = 204,
+  kSiteGemvProducer = 301,
+  kSiteGemvConsumer = 302,
 };
 
 // Host-side tensor map encoding (cuTensorMapEncodeTiled via the runtime's
@@ -36,6 +38,18 @@ bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* bas
                     uint32_t box_outer, CUtensorMapSwizzle swizzle, const char** why);
 
 int num_sms();  // SM count of the current device (cached)
+
+// Split-K workspaces. Every kernel that reduces through a caller's workspace
+// keeps its arrival counters in the first kCounterBytes and its fp32 partials
+// after them. Counters are zero between calls (each call re-arms the ones it
+// used) and partials are scratch, so one workspace can serve calls of any
+// shape and kernel in turn: no call's partials overlay another's counters.
+constexpr size_t kCounterBytes = 64 * 1024;
+constexpr int64_t kMaxCounters = static_cast<int64_t>(kCounterBytes / sizeof(unsigned));
+inline unsigned* ws_counters(void* ws) { return static_cast<unsigned*>(ws); }
+inline float* ws_partials(void* ws) {
+  return reinterpret_cast<float*>(static_cast<unsigned char*>(ws) + kCounterBytes);
+}
 
 // ---- quant_pack.cu --------------------------------------------------------
 cudaError_t launch_quant_int4_group(const void* w, int w_dtype, int64_t K, int64_t N, int64_t ldw,
@@ -56,6 +70,7 @@ struct DecodeArgs {
   int64_t lda;
   const uint8_t* wp;
   const void* scales;  // nullptr -> scalar_scale
+  int group;           // rows per scale group (scales != nullptr)
   float scalar_scale;
   int64_t M, N, K;
   void* out;
@@ -74,6 +89,12 @@ bool decode_supported(int64_t M, int64_t N, int64_t K, int group, const void* sc
 int decode_pick_split(int64_t M, int64_t N, int64_t K);
 size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int split);
 cudaError_t launch_w4a16_decode(const DecodeArgs& args, cudaStream_t s, const char** why);
+
+// ---- w4a16_gemv.cu (M <= 4 on the CUDA cores; stream-K over SMs) -------
+bool gemv_supported(int64_t M, int64_t N, int64_t K, int group, const void* scales, int64_t lda,
+                    const void* a, const void* wp);
+size_t gemv_workspace_bytes(int64_t M, int64_t N, int64_t K);  // 0: no split-K fixup needed
+cudaError_t launch_w4a16_gemv(const DecodeArgs& args, cudaStream_t s, const char** why);
 
 // ---- gemm_tc.cu (persistent tcgen05 GEMM: fp8, dense split-K, W4A16 prefill)
 struct GemmArgs {

@@ -379,6 +379,7 @@ bool decode_supported(int64_t M, int64_t N, int64_t K, int group, const void* sc
                       int64_t lda, const void* a) {
   if (M < 1 || M > kMmaN) return false;
   if (N % kBN != 0 || K % kBK != 0) return false;
+  if (N / kBN > kMaxCounters) return false;
   if (scales != nullptr && group != kBK) return false;
   if (lda % 8 != 0 || (reinterpret_cast<uintptr_t>(a) & 15) != 0) return false;
   if (K > (1ll << 30) || N > (1ll << 30)) return false;
@@ -404,8 +405,7 @@ size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int split) {
   (void)K;
   if (split <= 1) return 0;
   const int64_t tiles = N / kBN;
-  const size_t sem_bytes = ((tiles * sizeof(unsigned) + 255) / 256) * 256;
-  return sem_bytes + static_cast<size_t>(tiles) * split * M * kBN * sizeof(float);
+  return kCounterBytes + static_cast<size_t>(tiles) * split * M * kBN * sizeof(float);
 }
 
 cudaError_t launch_w4a16_decode(const DecodeArgs& p, cudaStream_t s, const char** why) {

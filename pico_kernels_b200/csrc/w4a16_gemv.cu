@@ -1,0 +1,635 @@
+// W4A16 GEMV for decode shapes (M <= 4) on sm_100a, on the CUDA cores.
+//
+// out[M, N] = A[M, K] @ (q[K, N] * s[K/g, N])  -- gemm_int4.int4_gemm
+// (gemm_int4.py:75-92) with group scales, q unpacked from Wp[K, N/2] in the
+// reference's nibble order (gemm_int4.py:43-50, pack_int4_n at :65-72).
+//
+// At M <= 4 the layer is a stream over the packed weights (K*N/2 bytes) with
+// 2*M*K*N flops: far below one flop per byte, so the tensor cores would only
+// add the dequantized-operand round trip through shared memory. This kernel
+// streams the weights once and does the arithmetic in fp32 on the CUDA cores.
+//
+//  * Units. The weights are cut into units of 128 rows x 256 columns (128 x
+//    128 packed bytes, 16 KB); a "slice" is a 256-column strip, KB units tall.
+//  * Work split, two modes chosen on the host:
+//    - cluster mode (small layers): a thread-block cluster of C CTAs (C a
+//      power of two <= 8) per slice, each CTA a contiguous run of the slice's
+//      units; the C partial columns are summed through distributed shared
+//      memory in rank order. No workspace, no atomics.
+//    - stream-K mode (large layers): units numbered slice-major, CTA c of G
+//      (two per SM when registers allow) takes [U*c/G, U*(c+1)/G). A CTA's
+//      range covers parts of a few slices ("segments"). A segment that is a
+//      whole slice is stored directly; otherwise the CTA writes its partial to
+//      the workspace (slot c + slice, unique per segment) and bumps the
+//      slice's arrival counter with an acq_rel atomic; the last arriver sums
+//      the slice's partials in CTA order, stores, and re-arms the counter.
+//    Both modes sum in a fixed order: results are deterministic per shape.
+//  * Pipeline. Warp 8 (one thread) is the TMA producer: per unit one 2D box
+//    of weights, the unit's group-scale rows and the activation tile
+//    A[0:M, k0:k0+128] into a ring of shared-memory slots, completing one
+//    mbarrier. Before griddepcontrol.wait it only prefetches weights and
+//    scales into L2 (a hint that cannot return stale data), so with
+//    programmatic dependent launch the DRAM fetch overlaps the previous
+//    kernel's tail; every load into shared memory and every global write
+//    comes after the wait.
+//  * Dequant. Warps 0-7 each take 16 consecutive rows of every unit; lane l
+//    owns columns [8l, 8l+8) of the slice, one 32-bit word per row (nibble j
+//    = column 8l+j). A nibble n = q & 15 is placed in the low mantissa bits
+//    of 2^23 with its sign bit flipped, (w & (15 << 4p)) ^ (0x4B000000 |
+//    8 << 4p), which is the float 2^23 + (q + 8) * 16^p exactly; subtracting
+//    2^23 + 8 * 16^p leaves q * 16^p exactly. One LOP3 and half a packed add
+//    per weight, then a packed fp32 FMA with the activation. Each column's
+//    accumulator carries a fixed power of two (16^p), removed exactly when
+//    the group's scale is applied: tot += acc * (s * 16^-p). So every product
+//    a*q is exact and accumulated in fp32, and the group scale multiplies the
+//    fp32 group sum, as in the reference's fp32 dequantize-then-matmul up to
+//    summation order.
+#include "pk_common.cuh"
+
+#include <cstring>
+#include <type_traits>
+
+#include "pk_internal.h"
+
+namespace pk {
+namespace {
+
+constexpr int kRows = 128;              // K rows per unit
+constexpr int kCols = 256;              // output columns per slice
+constexpr int kRowBytes = kCols / 2;    // packed bytes per row of a slice
+constexpr int kWarps = 8;               // dequant/FMA warps
+constexpr int kProducerWarp = kWarps;
+constexpr int kThreads = (kWarps + 1) * 32;
+constexpr int kRowsPerWarp = kRows / kWarps;  // 16
+constexpr int kMaxM = 4;
+constexpr int kMaxCluster = 8;
+constexpr int kMaxScaleRows = 2;        // scale rows per unit (group >= 64)
+
+template <int M>
+struct GemvCfg {
+  // M <= 2: about 100 KB of shared memory and <= 113 registers per thread, so
+  // two CTAs share an SM (the next kernel's, under programmatic launch, or a
+  // second CTA of a stream-K grid); M >= 3 runs one CTA per SM.
+  static constexpr int kStages = M <= 2 ? 5 : 8;
+  static constexpr int kWBytes = kRows * kRowBytes;          // 16384
+  static constexpr int kSBytes = kMaxScaleRows * kCols * 2;  // 1024
+  static constexpr int kABytes = kRows * 2 * M;              // 256 * M
+  static constexpr int kSlotBytes = ((kWBytes + kSBytes + kABytes + 127) / 128) * 128;
+  static constexpr int kRingBytes = kStages * kSlotBytes;
+  static constexpr int kPairOff = kRingBytes;                // per-warp activation pairs
+  static constexpr int kPairBytes = kWarps * kRowsPerWarp * M * 8;
+  static constexpr int kRedOff = kPairOff + kPairBytes;      // cross-warp reduction
+  static constexpr int kRedBytes = kWarps * M * kCols * 4;
+  static constexpr int kBarOff = kRedOff + kRedBytes;
+  static constexpr int kSmemBytes = kBarOff + 2 * kStages * 8 + 16 + 128;
+  static constexpr int kMinBlocks = M <= 2 ? 2 : 1;
+  static constexpr int kCtasPerSm = M <= 2 ? 2 : 1;
+};
+
+// Bit patterns 2^23 | 8 << 4p for p = 0..4. Passed as kernel parameters so
+// that (w & mask) ^ x compiles to one LOP3: an instruction takes at most one
+// 32-bit immediate, and a constant-bank operand is free.
+struct DecodeConsts {
+  uint32_t x[5];
+};
+
+// fp32 pair helpers (packed f32x2 arithmetic, sm_100)
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 unpack2(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// 2^23 + 8 * 16^p: the float a nibble at position p decodes to when q = 0.
+constexpr float kMagic0 = 8388616.0f;   // p = 0
+constexpr float kMagic1 = 8388736.0f;   // p = 1
+constexpr float kMagic2 = 8390656.0f;   // p = 2
+constexpr float kMagic3 = 8421376.0f;   // p = 3
+constexpr float kMagic4 = 8912896.0f;   // p = 4
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) {
+  return __half2float(v);
+}
+
+// Eight 16-bit scales (one uint4) -> four fp32 pairs.
+template <typename T>
+__device__ __forceinline__ void scales8(uint4 raw, uint64_t (&s)[4]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      s[i] = pack2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u));
+    } else {
+      const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+      const float2 f = __half22float2(h);
+      s[i] = pack2(f.x, f.y);
+    }
+  }
+}
+
+// CTA owning unit u under the stream-K split [U*c/G, U*(c+1)/G).
+__device__ __host__ __forceinline__ int64_t unit_owner(int64_t u, int64_t U, int64_t G) {
+  return ((u + 1) * G + U - 1) / U - 1;
+}
+
+__device__ __forceinline__ unsigned atomic_add_acq_rel(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;"
+               : "=r"(old)
+               : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
+struct GemvParams {
+  int N, K, group;
+  int scale_rows;      // group-scale rows per unit in the scale box (1 or 2)
+  int cluster;         // 0: stream-K; else CTAs per slice (cluster size)
+  float scalar_scale;
+  void* out;
+  int out_dtype;
+  int64_t ldo;
+  float* partials;
+  unsigned* sems;
+  int* status;
+};
+
+template <int M, typename T, bool kGrouped>
+__global__ void __launch_bounds__(kThreads, GemvCfg<M>::kMinBlocks)
+    w4a16_gemv_kernel(const __grid_constant__ CUtensorMap tmW,
+                      const __grid_constant__ CUtensorMap tmA,
+                      const __grid_constant__ CUtensorMap tmS, const GemvParams p,
+                      const DecodeConsts dc) {
+  using C = GemvCfg<M>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
+                                             ~static_cast<uintptr_t>(127));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* empty = full + C::kStages;
+  volatile int* last_flag = reinterpret_cast<volatile int*>(empty + C::kStages);
+  float* red = reinterpret_cast<float*>(smem + C::kRedOff);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t NS = (p.N + kCols - 1) / kCols;
+  const int64_t KB = (p.K + kRows - 1) / kRows;
+  const int64_t U = NS * KB;
+  const bool clustered = p.cluster > 0;
+  const int64_t G = gridDim.x;
+  const int64_t cta = blockIdx.x;  // stream-K: CTA index; cluster mode: rank in the cluster
+  int64_t u0, u1;
+  if (clustered) {
+    const int64_t s = blockIdx.y;
+    u0 = s * KB + KB * cta / p.cluster;
+    u1 = s * KB + KB * (cta + 1) / p.cluster;
+  } else {
+    u0 = U * cta / G;
+    u1 = U * (cta + 1) / G;
+  }
+  const int n_units = static_cast<int>(u1 - u0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  // Dependents may start their own prologue (an L2 prefetch of their weights)
+  // now; they wait for this grid before touching anything it writes.
+  griddep_launch_dependents();
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      const uint32_t tx =
+          C::kWBytes + (kGrouped ? p.scale_rows * kCols * 2 : 0) + C::kABytes;
+      tma_prefetch_desc(&tmW);
+      tma_prefetch_desc(&tmA);
+      if constexpr (kGrouped) tma_prefetch_desc(&tmS);
+      const int pre = n_units < 2 * C::kStages ? n_units : 2 * C::kStages;
+      for (int i = 0, s = static_cast<int>(u0 / KB), kb = static_cast<int>(u0 % KB); i < pre;
+           ++i) {
+        tma_prefetch_l2_2d(&tmW, s * kRowBytes, kb * kRows);
+        if constexpr (kGrouped) tma_prefetch_l2_2d(&tmS, s * kCols, kb * kRows / p.group);
+        if (++kb == KB) kb = 0, ++s;
+      }
+      griddep_wait();
+      int issued = 0;
+      bool ok = true;
+      int slice = static_cast<int>(u0 / KB);
+      int kb = static_cast<int>(u0 % KB);
+      for (int i = 0, slot = 0, round = 0; i < n_units; ++i) {
+        if (i >= C::kStages &&
+            !mbar_wait(&empty[slot], (round - 1) & 1, p.status, kSiteGemvProducer)) {
+          ok = false;
+          break;
+        }
+        const int k0 = kb * kRows;
+        uint8_t* base = smem + slot * C::kSlotBytes;
+        mbar_arrive_expect_tx(&full[slot], tx);
+        tma_load_2d(base, &tmW, &full[slot], slice * kRowBytes, k0);
+        if constexpr (kGrouped)
+          tma_load_2d(base + C::kWBytes, &tmS, &full[slot], slice * kCols, k0 / p.group);
+        tma_load_2d(base + C::kWBytes + C::kSBytes, &tmA, &full[slot], k0, 0);
+        issued = i + 1;
+        if (++kb == KB) kb = 0, ++slice;
+        if (++slot == C::kStages) slot = 0, ++round;
+      }
+      if (!ok) {
+        // let copies already issued land before the CTA's shared memory is released
+        const int first = issued > C::kStages ? issued - C::kStages : 0;
+        for (int i = first; i < issued; ++i)
+          mbar_wait(&full[i % C::kStages], (i / C::kStages) & 1, nullptr, 0);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- dequant / FMA warps ----------------
+    griddep_wait();
+    const uint64_t neg[4] = {pack2(-kMagic0, -kMagic1), pack2(-kMagic2, -kMagic3),
+                             pack2(-kMagic4, -kMagic2), pack2(-kMagic3, -kMagic4)};
+    // 16^-p of each column's decode position: columns 0-4 from w, 5-7 from w >> 12.
+    const uint64_t unpos[4] = {pack2(1.0f, 0.0625f), pack2(0.00390625f, 0.000244140625f),
+                               pack2(0.0000152587890625f, 0.00390625f),
+                               pack2(0.000244140625f, 0.0000152587890625f)};
+    uint64_t acc[M][4], tot[M][4], sc[4];
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[m][q] = tot[m][q] = 0ull;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      sc[q] = kGrouped ? 0ull : mul2(pack2(p.scalar_scale, p.scalar_scale), unpos[q]);
+
+    uint64_t* pairs = reinterpret_cast<uint64_t*>(smem + C::kPairOff) + warp * kRowsPerWarp * M;
+    bool failed = false;
+    int cur_group = -1;
+    int slice = static_cast<int>(u0 / KB);
+    int kb = static_cast<int>(u0 % KB);
+    for (int i = 0, slot = 0, round = 0; i < n_units;
+         ++i, slice += (kb + 1 == KB), kb = (kb + 1 == KB ? 0 : kb + 1),
+             slot = (slot + 1 == C::kStages ? 0 : slot + 1), round += (slot == 0)) {
+      const int k0 = kb * kRows;
+      if (!failed && !mbar_wait(&full[slot], round & 1, p.status, kSiteGemvConsumer))
+        failed = true;
+      const uint8_t* base = smem + slot * C::kSlotBytes;
+
+      if constexpr (kGrouped) {
+        const int g = (k0 + warp * kRowsPerWarp) / p.group;  // this warp's 16 rows: one group
+        if (g != cur_group) {
+          if (cur_group >= 0) {
+#pragma unroll
+            for (int m = 0; m < M; ++m)
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                tot[m][q] = fma2(acc[m][q], sc[q], tot[m][q]);
+                acc[m][q] = 0ull;
+              }
+          }
+          const int srow = g - k0 / p.group;
+          uint64_t s[4];
+          scales8<T>(*reinterpret_cast<const uint4*>(base + C::kWBytes + srow * kCols * 2 +
+                                                      lane * 16),
+                     s);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) sc[q] = mul2(s[q], unpos[q]);
+          cur_group = g;
+        }
+      }
+
+      // activations of this warp's 16 rows, as (a, a) pairs
+#pragma unroll
+      for (int e = lane; e < kRowsPerWarp * M; e += 32) {
+        const int m = e / kRowsPerWarp, r = e % kRowsPerWarp;
+        const T* a = reinterpret_cast<const T*>(base + C::kWBytes + C::kSBytes);
+        const float v = to_f32<T>(a[m * kRows + warp * kRowsPerWarp + r]);
+        pairs[r * M + m] = pack2(v, v);
+      }
+      __syncwarp();
+
+      const uint32_t* wrow =
+          reinterpret_cast<const uint32_t*>(base) + warp * kRowsPerWarp * 32 + lane;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t wv[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) wv[r] = wrow[(half * 8 + r) * 32];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const uint32_t w = wv[r];
+          const uint32_t t = w >> 12;
+          const float f0 = __uint_as_float((w & 0xFu) ^ dc.x[0]);
+          const float f1 = __uint_as_float((w & 0xF0u) ^ dc.x[1]);
+          const float f2 = __uint_as_float((w & 0xF00u) ^ dc.x[2]);
+          const float f3 = __uint_as_float((w & 0xF000u) ^ dc.x[3]);
+          const float f4 = __uint_as_float((w & 0xF0000u) ^ dc.x[4]);
+          const float f5 = __uint_as_float((t & 0xF00u) ^ dc.x[2]);
+          const float f6 = __uint_as_float((t & 0xF000u) ^ dc.x[3]);
+          const float f7 = __uint_as_float((t & 0xF0000u) ^ dc.x[4]);
+          const uint64_t d[4] = {add2(pack2(f0, f1), neg[0]), add2(pack2(f2, f3), neg[1]),
+                                 add2(pack2(f4, f5), neg[2]), add2(pack2(f6, f7), neg[3])};
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            const uint64_t av = pairs[(half * 8 + r) * M + m];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[m][q] = fma2(d[q], av, acc[m][q]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+
+      const bool seg_end = (i + 1 == n_units) || (kb + 1 == KB);
+      if (!seg_end) continue;
+
+      // ---- end of a segment: fold the open group, reduce over warps ----
+#pragma unroll
+      for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          tot[m][q] = fma2(acc[m][q], sc[q], tot[m][q]);
+          acc[m][q] = 0ull;
+        }
+      cur_group = -1;
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        float4* dst = reinterpret_cast<float4*>(red + (warp * M + m) * kCols + lane * 8);
+        const float2 a0 = unpack2(tot[m][0]), a1 = unpack2(tot[m][1]);
+        const float2 a2 = unpack2(tot[m][2]), a3 = unpack2(tot[m][3]);
+        dst[0] = make_float4(a0.x, a0.y, a1.x, a1.y);
+        dst[1] = make_float4(a2.x, a2.y, a3.x, a3.y);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tot[m][q] = 0ull;
+      }
+      named_bar_sync(1, kWarps * 32);
+      const int t = threadIdx.x;  // column within the slice
+      float v[M];
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) s += red[(w * M + m) * kCols + t];
+        v[m] = s;
+      }
+      if (clustered) {
+        // stage the CTA's partial for the cluster reduction (thread t alone
+        // reads and writes column t)
+#pragma unroll
+        for (int m = 0; m < M; ++m) red[m * kCols + t] = v[m];
+        break;  // a cluster CTA owns exactly one segment
+      }
+      const int64_t col = static_cast<int64_t>(slice) * kCols + t;
+      auto store = [&](const float* vals) {
+        if (col >= p.N) return;
+        if (p.out_dtype == PK_BF16) {
+          __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out);
+#pragma unroll
+          for (int m = 0; m < M; ++m) o[m * p.ldo + col] = __float2bfloat16_rn(vals[m]);
+        } else {
+          float* o = static_cast<float*>(p.out);
+#pragma unroll
+          for (int m = 0; m < M; ++m) o[m * p.ldo + col] = vals[m];
+        }
+      };
+      const int64_t cfirst = unit_owner(slice * KB, U, G);
+      const int64_t clast = unit_owner(slice * KB + KB - 1, U, G);
+      if (cfirst == clast) {
+        store(v);
+        named_bar_sync(1, kWarps * 32);  // red is rewritten by the next segment
+        continue;
+      }
+      float* mine = p.partials + (cta + slice) * (M * kCols);
+#pragma unroll
+      for (int m = 0; m < M; ++m) __stcg(mine + m * kCols + t, v[m]);
+      named_bar_sync(1, kWarps * 32);
+      if (t == 0) {
+        // release: the CTA's partial (ordered before by the barrier) becomes
+        // visible with the count; acquire: the last arriver sees every partial
+        const unsigned arrived = atomic_add_acq_rel(&p.sems[slice], 1u);
+        *last_flag = arrived == static_cast<unsigned>(clast - cfirst) ? 1 : 0;
+      }
+      named_bar_sync(1, kWarps * 32);
+      if (*last_flag) {
+        float sum[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) sum[m] = 0.0f;
+        for (int64_t c = cfirst; c <= clast; ++c) {
+          const float* src = p.partials + (c + slice) * (M * kCols);
+#pragma unroll
+          for (int m = 0; m < M; ++m) sum[m] += __ldcg(src + m * kCols + t);
+        }
+        store(sum);
+        if (t == 0) p.sems[slice] = 0u;  // re-arm for the next call
+      }
+      named_bar_sync(1, kWarps * 32);
+    }
+  }
+
+  if (clustered) {
+    // Cluster reduction: rank r sums columns [r*per, (r+1)*per) of the C
+    // staged partials in rank order. Every thread of every CTA takes part in
+    // both cluster barriers; the second keeps each CTA's shared memory alive
+    // until its peers have read it.
+    cluster_sync();
+    if (warp < kWarps) {
+      const int cs = p.cluster;
+      const int per = kCols / cs;
+      const int64_t slice = blockIdx.y;
+      const uint32_t red_addr = smem_u32(red);
+      for (int e = threadIdx.x; e < M * per; e += kWarps * 32) {
+        const int m = e / per;
+        const int c = static_cast<int>(cta) * per + e % per;
+        float s = 0.0f;
+        for (int r = 0; r < cs; ++r)
+          s += ld_cluster_f32(cluster_map(red_addr + (m * kCols + c) * 4, static_cast<uint32_t>(r)));
+        const int64_t col = slice * kCols + c;
+        if (col < p.N) {
+          if (p.out_dtype == PK_BF16)
+            static_cast<__nv_bfloat16*>(p.out)[m * p.ldo + col] = __float2bfloat16_rn(s);
+          else
+            static_cast<float*>(p.out)[m * p.ldo + col] = s;
+        }
+      }
+    }
+    cluster_sync();
+  }
+}
+
+CUtensorMapDataType tmap_type16(int dt) {
+  return dt == PK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+// How a call is split over the GPU.
+struct GemvPlan {
+  int cluster;     // > 0: cluster mode with this many CTAs per slice; 0: stream-K
+  int64_t grid_x;  // cluster mode: cluster size; stream-K: CTAs
+  int64_t grid_y;  // cluster mode: slices; stream-K: 1
+};
+
+GemvPlan make_plan(int64_t M, int64_t N, int64_t K) {
+  const int64_t NS = (N + kCols - 1) / kCols;
+  const int64_t KB = (K + kRows - 1) / kRows;
+  const int64_t U = NS * KB;
+  const int64_t sms = num_sms();
+  GemvPlan pl{};
+  if (U <= 8 * sms && NS <= sms) {
+    // small layer: a cluster per slice, the slice's units split between its CTAs
+    int c = 1;
+    while (c * 2 <= kMaxCluster && NS * c * 2 <= sms && c * 2 <= KB) c *= 2;
+    pl.cluster = c;
+    pl.grid_x = c;
+    pl.grid_y = NS;
+  } else {
+    const int64_t cap = (M <= 2 ? 2 : 1) * sms;
+    pl.cluster = 0;
+    pl.grid_x = U < cap ? U : cap;
+    pl.grid_y = 1;
+  }
+  return pl;
+}
+
+}  // namespace
+
+bool gemv_supported(int64_t M, int64_t N, int64_t K, int group, const void* scales, int64_t lda,
+                    const void* a, const void* wp) {
+  if (M < 1 || M > kMaxM) return false;
+  if (N < kCols || N % 32 != 0 || K < kRows) return false;
+  if (N > (1ll << 30) || K > (1ll << 30)) return false;
+  if ((N + kCols - 1) / kCols > kMaxCounters) return false;
+  if (lda % 8 != 0 || (reinterpret_cast<uintptr_t>(a) & 15) != 0) return false;
+  if ((reinterpret_cast<uintptr_t>(wp) & 15) != 0) return false;
+  if (scales != nullptr &&
+      (group <= 0 || group % 64 != 0 || (reinterpret_cast<uintptr_t>(scales) & 15) != 0))
+    return false;
+  return true;
+}
+
+size_t gemv_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  const GemvPlan pl = make_plan(M, N, K);
+  if (pl.cluster > 0) return 0;
+  const int64_t NS = (N + kCols - 1) / kCols;
+  const int64_t KB = (K + kRows - 1) / kRows;
+  const int64_t U = NS * KB;
+  const int64_t G = pl.grid_x;
+  bool split = false;
+  for (int64_t j = 0; j < NS && !split; ++j)
+    split = unit_owner(j * KB, U, G) != unit_owner(j * KB + KB - 1, U, G);
+  if (!split) return 0;
+  return kCounterBytes + static_cast<size_t>(G + NS) * M * kCols * sizeof(float);
+}
+
+cudaError_t launch_w4a16_gemv(const DecodeArgs& a, cudaStream_t s, const char** why) {
+  CUtensorMap tmW, tmA, tmS;
+  const CUtensorMapDataType dt = tmap_type16(a.a_dtype);
+  if (!encode_tmap_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.wp, a.N / 2, a.K, a.N / 2, kRowBytes,
+                      kRows, CU_TENSOR_MAP_SWIZZLE_NONE, why))
+    return cudaErrorInvalidValue;
+  if (!encode_tmap_2d(&tmA, dt, a.a, a.K, a.M, a.lda * 2, kRows, static_cast<uint32_t>(a.M),
+                      CU_TENSOR_MAP_SWIZZLE_NONE, why))
+    return cudaErrorInvalidValue;
+  const bool grouped = a.scales != nullptr;
+  GemvParams p{};
+  p.N = static_cast<int>(a.N);
+  p.K = static_cast<int>(a.K);
+  p.group = grouped ? a.group : kRows;
+  p.scale_rows = (grouped && a.group % kRows != 0) ? 2 : 1;
+  p.scalar_scale = a.scalar_scale;
+  p.out = a.out;
+  p.out_dtype = a.out_dtype;
+  p.ldo = a.ldo;
+  p.partials = a.partials;
+  p.sems = a.sems;
+  p.status = a.status;
+  if (grouped) {
+    const int64_t groups = (a.K + a.group - 1) / a.group;
+    if (!encode_tmap_2d(&tmS, dt, a.scales, a.N, groups, a.N * 2, kCols,
+                        static_cast<uint32_t>(p.scale_rows), CU_TENSOR_MAP_SWIZZLE_NONE, why))
+      return cudaErrorInvalidValue;
+  } else {
+    std::memcpy(&tmS, &tmW, sizeof(tmS));  // unused
+  }
+  const GemvPlan pl = make_plan(a.M, a.N, a.K);
+  p.cluster = pl.cluster;
+  if (pl.cluster == 0 && gemv_workspace_bytes(a.M, a.N, a.K) > 0 &&
+      (a.partials == nullptr || a.sems == nullptr)) {
+    *why = "the split-K GEMV needs a workspace";
+    return cudaErrorInvalidValue;
+  }
+  DecodeConsts dc;
+  dc.x[0] = 0x4B000008u;
+  dc.x[1] = 0x4B000080u;
+  dc.x[2] = 0x4B000800u;
+  dc.x[3] = 0x4B008000u;
+  dc.x[4] = 0x4B080000u;
+
+  auto launch = [&](auto kernel, int smem_bytes) -> cudaError_t {
+    cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(pl.grid_x), static_cast<unsigned>(pl.grid_y), 1);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem_bytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attrs[2];
+    int na = 0;
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+    if (pl.cluster > 1) {
+      attrs[na].id = cudaLaunchAttributeClusterDimension;
+      attrs[na].val.clusterDim.x = pl.cluster;
+      attrs[na].val.clusterDim.y = 1;
+      attrs[na].val.clusterDim.z = 1;
+      ++na;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, kernel, tmW, tmA, tmS, p, dc);
+  };
+  auto by_m = [&](auto tag, auto grouped_tag) -> cudaError_t {
+    using T = decltype(tag);
+    constexpr bool kG = decltype(grouped_tag)::value;
+    switch (a.M) {
+      case 1: return launch(w4a16_gemv_kernel<1, T, kG>, GemvCfg<1>::kSmemBytes);
+      case 2: return launch(w4a16_gemv_kernel<2, T, kG>, GemvCfg<2>::kSmemBytes);
+      case 3: return launch(w4a16_gemv_kernel<3, T, kG>, GemvCfg<3>::kSmemBytes);
+      default: return launch(w4a16_gemv_kernel<4, T, kG>, GemvCfg<4>::kSmemBytes);
+    }
+  };
+  if (a.a_dtype == PK_BF16) {
+    return grouped ? by_m(__nv_bfloat16{}, std::true_type{})
+                   : by_m(__nv_bfloat16{}, std::false_type{});
+  }
+  return grouped ? by_m(__half{}, std::true_type{}) : by_m(__half{}, std::false_type{});
+}
+
+}  // namespace pk
