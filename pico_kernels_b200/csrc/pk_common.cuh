@@ -92,6 +92,36 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
+// As mbar_wait, but each probe lets the hardware suspend the warp for up to
+// `hint_ns` nanoseconds (it resumes as soon as the phase completes), so a
+// waiting warp does not spin and take issue slots from working warps.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar_addr, uint32_t parity,
+                                                   uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int* status,
+                                                int where, uint32_t hint_ns = 20000) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait(a, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait_hint(a, parity, hint_ns)) return true;
+    if (clock64() - t0 > PK_WAIT_CYCLES) {
+      record_error(status, PK_ERR_TIMEOUT, where);
+      return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // programmatic dependent launch and thread-block clusters
 // ---------------------------------------------------------------------------

@@ -9,41 +9,48 @@
 // add the dequantized-operand round trip through shared memory. This kernel
 // streams the weights once and does the arithmetic in fp32 on the CUDA cores.
 //
-//  * Units. The weights are cut into units of 128 rows x 256 columns (128 x
-//    128 packed bytes, 16 KB); a "slice" is a 256-column strip, KB units tall.
+//  * Units. The weights are cut into units of 256 rows x 256 columns (256 x
+//    128 packed bytes, 32 KB); a "slice" is a 256-column strip, KB units tall.
 //  * Work split, two modes chosen on the host:
 //    - cluster mode (small layers): a thread-block cluster of C CTAs (C a
 //      power of two <= 8) per slice, each CTA a contiguous run of the slice's
 //      units; the C partial columns are summed through distributed shared
 //      memory in rank order. No workspace, no atomics.
 //    - stream-K mode (large layers): units numbered slice-major, CTA c of G
-//      (two per SM when registers allow) takes [U*c/G, U*(c+1)/G). A CTA's
-//      range covers parts of a few slices ("segments"). A segment that is a
-//      whole slice is stored directly; otherwise the CTA writes its partial to
-//      the workspace (slot c + slice, unique per segment) and bumps the
-//      slice's arrival counter with an acq_rel atomic; the last arriver sums
-//      the slice's partials in CTA order, stores, and re-arms the counter.
+//      (two per SM when the CTA fits twice) takes [U*c/G, U*(c+1)/G). A
+//      CTA's range covers parts of a few slices ("segments"). A segment that
+//      is a whole slice is stored directly; otherwise the CTA writes its
+//      partial to the workspace (slot c + slice, unique per segment) and bumps
+//      the slice's arrival counter with an acq_rel atomic; the last arriver
+//      sums the slice's partials in CTA order, stores, and re-arms the counter.
 //    Both modes sum in a fixed order: results are deterministic per shape.
 //  * Pipeline. Warp 8 (one thread) is the TMA producer: per unit one 2D box
 //    of weights, the unit's group-scale rows and the activation tile
-//    A[0:M, k0:k0+128] into a ring of shared-memory slots, completing one
+//    A[0:M, k0:k0+256] into a ring of shared-memory slots, completing one
 //    mbarrier. Before griddepcontrol.wait it only prefetches weights and
 //    scales into L2 (a hint that cannot return stale data), so with
 //    programmatic dependent launch the DRAM fetch overlaps the previous
 //    kernel's tail; every load into shared memory and every global write
 //    comes after the wait.
-//  * Dequant. Warps 0-7 each take 16 consecutive rows of every unit; lane l
-//    owns columns [8l, 8l+8) of the slice, one 32-bit word per row (nibble j
-//    = column 8l+j). A nibble n = q & 15 is placed in the low mantissa bits
-//    of 2^23 with its sign bit flipped, (w & (15 << 4p)) ^ (0x4B000000 |
-//    8 << 4p), which is the float 2^23 + (q + 8) * 16^p exactly; subtracting
-//    2^23 + 8 * 16^p leaves q * 16^p exactly. One LOP3 and half a packed add
-//    per weight, then a packed fp32 FMA with the activation. Each column's
-//    accumulator carries a fixed power of two (16^p), removed exactly when
-//    the group's scale is applied: tot += acc * (s * 16^-p). So every product
-//    a*q is exact and accumulated in fp32, and the group scale multiplies the
-//    fp32 group sum, as in the reference's fp32 dequantize-then-matmul up to
-//    summation order.
+//  * Dequant. Warps 0-7 each take 32 consecutive rows of every unit (inside
+//    one scale group); lane l owns columns [8l, 8l+8) of the slice, one
+//    32-bit word per row (nibble j = column 8l+j). Each nibble n = q & 15 is
+//    moved to bit position 4p (p = 2..5: the word itself for nibbles 2-5,
+//    w << 8 for 0-1, w >> 8 for 6-7) and its sign bit flipped with one LOP3,
+//    (src & (15 << 4p)) ^ (8 << 4p). Read as an fp32 bit pattern below 2^24
+//    that is exactly the number (q + 8) * 16^p * 2^-149 (a subnormal, or the
+//    smallest normal binade). The activations are pre-scaled by 2^S, so one
+//    packed FMA per two weights accumulates a' * (q + 8) * 16^p * 2^-149 with
+//    the product exact and one fp32 rounding, as a plain fp32 dot product
+//    would. At the end of each unit the warp removes the +8 offset with the
+//    sum of its scaled activations, A' = sum a': acc + (-8 * 16^p * 2^-149) *
+//    A', multiplies by 2^(149 - S - 4p) (exact) and then by the fp32 group
+//    scale. S is chosen per unit from the largest activation exponent of the
+//    warp's rows, S = clamp(248 - e_max, 30, 127), which keeps every scaled
+//    activation, product and sum in the normal fp32 range for any activation
+//    below 2^98 in magnitude. The result is the reference's fp32
+//    dequantize-then-matmul up to summation order (and one extra rounding of
+//    the offset term).
 #include "pk_common.cuh"
 
 #include <cstring>
@@ -54,43 +61,47 @@
 namespace pk {
 namespace {
 
-constexpr int kRows = 128;              // K rows per unit
+constexpr int kRows = 256;              // K rows per unit
 constexpr int kCols = 256;              // output columns per slice
 constexpr int kRowBytes = kCols / 2;    // packed bytes per row of a slice
 constexpr int kWarps = 8;               // dequant/FMA warps
 constexpr int kProducerWarp = kWarps;
 constexpr int kThreads = (kWarps + 1) * 32;
-constexpr int kRowsPerWarp = kRows / kWarps;  // 16
+constexpr int kRowsPerWarp = kRows / kWarps;  // 32: one row per lane for the activations
 constexpr int kMaxM = 4;
 constexpr int kMaxCluster = 8;
-constexpr int kMaxScaleRows = 2;        // scale rows per unit (group >= 64)
+constexpr int kMaxScaleRows = 4;        // scale rows a unit can touch (group >= 64)
+constexpr int kSmemTwoPerSm = 115712;   // per-CTA limit for two resident CTAs (228 KB SM)
 
 template <int M>
 struct GemvCfg {
-  // M <= 2: about 100 KB of shared memory and <= 113 registers per thread, so
-  // two CTAs share an SM (the next kernel's, under programmatic launch, or a
-  // second CTA of a stream-K grid); M >= 3 runs one CTA per SM.
-  static constexpr int kStages = M <= 2 ? 5 : 8;
-  static constexpr int kWBytes = kRows * kRowBytes;          // 16384
-  static constexpr int kSBytes = kMaxScaleRows * kCols * 2;  // 1024
-  static constexpr int kABytes = kRows * 2 * M;              // 256 * M
+  // M = 1: three slots and ~113 KB, two CTAs per SM; M = 2: two slots, two
+  // CTAs per SM; M >= 3 (registers): one CTA per SM with five slots.
+  static constexpr int kStages = M == 1 ? 3 : (M == 2 ? 2 : 5);
+  static constexpr int kWBytes = kRows * kRowBytes;          // 32768
+  static constexpr int kSBytes = kMaxScaleRows * kCols * 2;  // 2048
+  static constexpr int kABytes = kRows * 2 * M;              // 512 * M
   static constexpr int kSlotBytes = ((kWBytes + kSBytes + kABytes + 127) / 128) * 128;
   static constexpr int kRingBytes = kStages * kSlotBytes;
-  static constexpr int kPairOff = kRingBytes;                // per-warp activation pairs
+  // Per-warp activation pairs (during a unit) and the cross-warp reduction
+  // buffer (at a segment end) share one region: a segment end starts after
+  // every warp's last use of its pairs and ends with a barrier.
   static constexpr int kPairBytes = kWarps * kRowsPerWarp * M * 8;
-  static constexpr int kRedOff = kPairOff + kPairBytes;      // cross-warp reduction
-  static constexpr int kRedBytes = kWarps * M * kCols * 4;
-  static constexpr int kBarOff = kRedOff + kRedBytes;
+  static constexpr int kRedBytes = kWarps * kCols * 4;  // one output row at a time
+  static constexpr int kScratchOff = kRingBytes;
+  static constexpr int kScratchBytes = kPairBytes > kRedBytes ? kPairBytes : kRedBytes;
+  static constexpr int kBarOff = kScratchOff + kScratchBytes;
   static constexpr int kSmemBytes = kBarOff + 2 * kStages * 8 + 16 + 128;
-  static constexpr int kMinBlocks = M <= 2 ? 2 : 1;
   static constexpr int kCtasPerSm = M <= 2 ? 2 : 1;
+  static_assert(kCtasPerSm == 1 || kSmemBytes <= kSmemTwoPerSm, "two CTAs must fit an SM");
 };
 
-// Bit patterns 2^23 | 8 << 4p for p = 0..4. Passed as kernel parameters so
-// that (w & mask) ^ x compiles to one LOP3: an instruction takes at most one
-// 32-bit immediate, and a constant-bank operand is free.
+// Bit patterns 8 << 4p for p = 2..5 (the flipped sign bit of a nibble at
+// position p). Passed as kernel parameters so that (w & mask) ^ x compiles to
+// one LOP3: an instruction takes at most one 32-bit immediate, and a
+// constant-bank operand is free.
 struct DecodeConsts {
-  uint32_t x[5];
+  uint32_t x[4];
 };
 
 // fp32 pair helpers (packed f32x2 arithmetic, sm_100)
@@ -104,11 +115,6 @@ __device__ __forceinline__ float2 unpack2(uint64_t v) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
   return r;
 }
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
 __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
@@ -119,13 +125,6 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
 }
-
-// 2^23 + 8 * 16^p: the float a nibble at position p decodes to when q = 0.
-constexpr float kMagic0 = 8388616.0f;   // p = 0
-constexpr float kMagic1 = 8388736.0f;   // p = 1
-constexpr float kMagic2 = 8390656.0f;   // p = 2
-constexpr float kMagic3 = 8421376.0f;   // p = 3
-constexpr float kMagic4 = 8912896.0f;   // p = 4
 
 template <typename T>
 __device__ __forceinline__ float to_f32(T v);
@@ -154,6 +153,9 @@ __device__ __forceinline__ void scales8(uint4 raw, uint64_t (&s)[4]) {
   }
 }
 
+// 2^e for an unbiased exponent in the normal range.
+__device__ __forceinline__ float exp2i(int e) { return __uint_as_float(static_cast<uint32_t>(e + 127) << 23); }
+
 // CTA owning unit u under the stream-K split [U*c/G, U*(c+1)/G).
 __device__ __host__ __forceinline__ int64_t unit_owner(int64_t u, int64_t U, int64_t G) {
   return ((u + 1) * G + U - 1) / U - 1;
@@ -170,7 +172,8 @@ __device__ __forceinline__ unsigned atomic_add_acq_rel(unsigned* p, unsigned v) 
 
 struct GemvParams {
   int N, K, group;
-  int scale_rows;      // group-scale rows per unit in the scale box (1 or 2)
+  int group_shift;     // log2(group) when group is a power of two, else -1
+  int scale_rows;      // group-scale rows per unit in the scale box
   int cluster;         // 0: stream-K; else CTAs per slice (cluster size)
   float scalar_scale;
   void* out;
@@ -181,8 +184,13 @@ struct GemvParams {
   int* status;
 };
 
+// Index of the scale group holding K row `row` (a shift for power-of-two groups).
+__device__ __forceinline__ int group_of(int row, const GemvParams& p) {
+  return p.group_shift >= 0 ? (row >> p.group_shift) : row / p.group;
+}
+
 template <int M, typename T, bool kGrouped>
-__global__ void __launch_bounds__(kThreads, GemvCfg<M>::kMinBlocks)
+__global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
     w4a16_gemv_kernel(const __grid_constant__ CUtensorMap tmW,
                       const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmS, const GemvParams p,
@@ -194,21 +202,21 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kMinBlocks)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* empty = full + C::kStages;
   volatile int* last_flag = reinterpret_cast<volatile int*>(empty + C::kStages);
-  float* red = reinterpret_cast<float*>(smem + C::kRedOff);
+  float* red = reinterpret_cast<float*>(smem + C::kScratchOff);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t NS = (p.N + kCols - 1) / kCols;
-  const int64_t KB = (p.K + kRows - 1) / kRows;
-  const int64_t U = NS * KB;
+  const int NS = (p.N + kCols - 1) / kCols;
+  const int KB = (p.K + kRows - 1) / kRows;
+  const int64_t U = static_cast<int64_t>(NS) * KB;
   const bool clustered = p.cluster > 0;
   const int64_t G = gridDim.x;
   const int64_t cta = blockIdx.x;  // stream-K: CTA index; cluster mode: rank in the cluster
   int64_t u0, u1;
   if (clustered) {
     const int64_t s = blockIdx.y;
-    u0 = s * KB + KB * cta / p.cluster;
-    u1 = s * KB + KB * (cta + 1) / p.cluster;
+    u0 = s * KB + static_cast<int64_t>(KB) * cta / p.cluster;
+    u1 = s * KB + static_cast<int64_t>(KB) * (cta + 1) / p.cluster;
   } else {
     u0 = U * cta / G;
     u1 = U * (cta + 1) / G;
@@ -238,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kMinBlocks)
       for (int i = 0, s = static_cast<int>(u0 / KB), kb = static_cast<int>(u0 % KB); i < pre;
            ++i) {
         tma_prefetch_l2_2d(&tmW, s * kRowBytes, kb * kRows);
-        if constexpr (kGrouped) tma_prefetch_l2_2d(&tmS, s * kCols, kb * kRows / p.group);
+        if constexpr (kGrouped) tma_prefetch_l2_2d(&tmS, s * kCols, group_of(kb * kRows, p));
         if (++kb == KB) kb = 0, ++s;
       }
       griddep_wait();
@@ -257,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kMinBlocks)
         mbar_arrive_expect_tx(&full[slot], tx);
         tma_load_2d(base, &tmW, &full[slot], slice * kRowBytes, k0);
         if constexpr (kGrouped)
-          tma_load_2d(base + C::kWBytes, &tmS, &full[slot], slice * kCols, k0 / p.group);
+          tma_load_2d(base + C::kWBytes, &tmS, &full[slot], slice * kCols, group_of(k0, p));
         tma_load_2d(base + C::kWBytes + C::kSBytes, &tmA, &full[slot], k0, 0);
         issued = i + 1;
         if (++kb == KB) kb = 0, ++slice;
@@ -274,134 +282,131 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kMinBlocks)
   } else {
     // ---------------- dequant / FMA warps ----------------
     griddep_wait();
-    const uint64_t neg[4] = {pack2(-kMagic0, -kMagic1), pack2(-kMagic2, -kMagic3),
-                             pack2(-kMagic4, -kMagic2), pack2(-kMagic3, -kMagic4)};
-    // 16^-p of each column's decode position: columns 0-4 from w, 5-7 from w >> 12.
-    const uint64_t unpos[4] = {pack2(1.0f, 0.0625f), pack2(0.00390625f, 0.000244140625f),
-                               pack2(0.0000152587890625f, 0.00390625f),
-                               pack2(0.000244140625f, 0.0000152587890625f)};
-    uint64_t acc[M][4], tot[M][4], sc[4];
+    // -8 * 16^p * 2^-149 for the column pairs' positions (2,3) and (4,5): the
+    // same bit patterns as the sign flips, negated
+    const uint64_t off23 = pack2(__uint_as_float(0x80000800u), __uint_as_float(0x80008000u));
+    const uint64_t off45 = pack2(__uint_as_float(0x80080000u), __uint_as_float(0x80800000u));
+    uint64_t acc[M][4], tot[M][4];
 #pragma unroll
     for (int m = 0; m < M; ++m)
 #pragma unroll
       for (int q = 0; q < 4; ++q) acc[m][q] = tot[m][q] = 0ull;
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      sc[q] = kGrouped ? 0ull : mul2(pack2(p.scalar_scale, p.scalar_scale), unpos[q]);
 
-    uint64_t* pairs = reinterpret_cast<uint64_t*>(smem + C::kPairOff) + warp * kRowsPerWarp * M;
+    uint64_t* pairs = reinterpret_cast<uint64_t*>(smem + C::kScratchOff) + warp * kRowsPerWarp * M;
     bool failed = false;
-    int cur_group = -1;
     int slice = static_cast<int>(u0 / KB);
     int kb = static_cast<int>(u0 % KB);
     for (int i = 0, slot = 0, round = 0; i < n_units;
          ++i, slice += (kb + 1 == KB), kb = (kb + 1 == KB ? 0 : kb + 1),
              slot = (slot + 1 == C::kStages ? 0 : slot + 1), round += (slot == 0)) {
       const int k0 = kb * kRows;
-      if (!failed && !mbar_wait(&full[slot], round & 1, p.status, kSiteGemvConsumer))
+      if (!failed && !mbar_wait_sleep(&full[slot], round & 1, p.status, kSiteGemvConsumer))
         failed = true;
       const uint8_t* base = smem + slot * C::kSlotBytes;
 
-      if constexpr (kGrouped) {
-        const int g = (k0 + warp * kRowsPerWarp) / p.group;  // this warp's 16 rows: one group
-        if (g != cur_group) {
-          if (cur_group >= 0) {
+      // Activations: lane l converts row 32*warp + l of every output row m.
+      // S = clamp(248 - e_max, 30, 127) from the largest exponent in the warp.
+      float av[M];
+      uint32_t emax = 0;
+      {
+        const T* a = reinterpret_cast<const T*>(base + C::kWBytes + C::kSBytes);
 #pragma unroll
-            for (int m = 0; m < M; ++m)
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                tot[m][q] = fma2(acc[m][q], sc[q], tot[m][q]);
-                acc[m][q] = 0ull;
-              }
-          }
-          const int srow = g - k0 / p.group;
-          uint64_t s[4];
-          scales8<T>(*reinterpret_cast<const uint4*>(base + C::kWBytes + srow * kCols * 2 +
-                                                      lane * 16),
-                     s);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) sc[q] = mul2(s[q], unpos[q]);
-          cur_group = g;
+        for (int m = 0; m < M; ++m) {
+          av[m] = to_f32<T>(a[m * kRows + warp * kRowsPerWarp + lane]);
+          const uint32_t e = (__float_as_uint(av[m]) >> 23) & 0xFFu;
+          emax = e > emax ? e : emax;
         }
       }
-
-      // activations of this warp's 16 rows, as (a, a) pairs
+      emax = __reduce_max_sync(0xffffffffu, emax);
+      int S = 248 - static_cast<int>(emax);
+      S = S < 30 ? 30 : (S > 127 ? 127 : S);
+      const float two_s = exp2i(S);
+      uint64_t asum[M];
 #pragma unroll
-      for (int e = lane; e < kRowsPerWarp * M; e += 32) {
-        const int m = e / kRowsPerWarp, r = e % kRowsPerWarp;
-        const T* a = reinterpret_cast<const T*>(base + C::kWBytes + C::kSBytes);
-        const float v = to_f32<T>(a[m * kRows + warp * kRowsPerWarp + r]);
-        pairs[r * M + m] = pack2(v, v);
+      for (int m = 0; m < M; ++m) {
+        const float as = av[m] * two_s;
+        pairs[lane * M + m] = pack2(as, as);
+        float t = as;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        asum[m] = pack2(t, t);
+      }
+      // 2^(149 - S - 4p) for the pairs' positions (2,3) and (4,5)
+      const uint64_t pw23 = pack2(exp2i(141 - S), exp2i(137 - S));
+      const uint64_t pw45 = pack2(exp2i(133 - S), exp2i(129 - S));
+      uint64_t sc[4];
+      if constexpr (kGrouped) {
+        const int srow = group_of(k0 + warp * kRowsPerWarp, p) - group_of(k0, p);
+        scales8<T>(*reinterpret_cast<const uint4*>(base + C::kWBytes + srow * kCols * 2 + lane * 16),
+                   sc);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) sc[q] = pack2(p.scalar_scale, p.scalar_scale);
       }
       __syncwarp();
 
       const uint32_t* wrow =
           reinterpret_cast<const uint32_t*>(base) + warp * kRowsPerWarp * 32 + lane;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
+      for (int b = 0; b < kRowsPerWarp / 8; ++b) {
         uint32_t wv[8];
 #pragma unroll
-        for (int r = 0; r < 8; ++r) wv[r] = wrow[(half * 8 + r) * 32];
+        for (int r = 0; r < 8; ++r) wv[r] = wrow[(b * 8 + r) * 32];
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
           const uint32_t w = wv[r];
-          const uint32_t t = w >> 12;
-          const float f0 = __uint_as_float((w & 0xFu) ^ dc.x[0]);
-          const float f1 = __uint_as_float((w & 0xF0u) ^ dc.x[1]);
-          const float f2 = __uint_as_float((w & 0xF00u) ^ dc.x[2]);
-          const float f3 = __uint_as_float((w & 0xF000u) ^ dc.x[3]);
-          const float f4 = __uint_as_float((w & 0xF0000u) ^ dc.x[4]);
-          const float f5 = __uint_as_float((t & 0xF00u) ^ dc.x[2]);
-          const float f6 = __uint_as_float((t & 0xF000u) ^ dc.x[3]);
-          const float f7 = __uint_as_float((t & 0xF0000u) ^ dc.x[4]);
-          const uint64_t d[4] = {add2(pack2(f0, f1), neg[0]), add2(pack2(f2, f3), neg[1]),
-                                 add2(pack2(f4, f5), neg[2]), add2(pack2(f6, f7), neg[3])};
+          const uint32_t lo = w << 8, hi = w >> 8;
+          uint64_t d[4];
+          d[0] = pack2(__uint_as_float((lo & 0xF00u) ^ dc.x[0]), __uint_as_float((lo & 0xF000u) ^ dc.x[1]));
+          d[1] = pack2(__uint_as_float((w & 0xF00u) ^ dc.x[0]), __uint_as_float((w & 0xF000u) ^ dc.x[1]));
+          d[2] = pack2(__uint_as_float((w & 0xF0000u) ^ dc.x[2]), __uint_as_float((w & 0xF00000u) ^ dc.x[3]));
+          d[3] = pack2(__uint_as_float((hi & 0xF0000u) ^ dc.x[2]), __uint_as_float((hi & 0xF00000u) ^ dc.x[3]));
 #pragma unroll
           for (int m = 0; m < M; ++m) {
-            const uint64_t av = pairs[(half * 8 + r) * M + m];
+            const uint64_t a2 = pairs[(b * 8 + r) * M + m];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) acc[m][q] = fma2(d[q], av, acc[m][q]);
+            for (int q = 0; q < 4; ++q) acc[m][q] = fma2(d[q], a2, acc[m][q]);
           }
         }
       }
+      // fold the unit: remove the +8 offset, undo 2^S * 16^p, apply the scale
+#pragma unroll
+      for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint64_t c = fma2(q < 2 ? off23 : off45, asum[m], acc[m][q]);
+          tot[m][q] = fma2(mul2(c, q < 2 ? pw23 : pw45), sc[q], tot[m][q]);
+          acc[m][q] = 0ull;
+        }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
 
       const bool seg_end = (i + 1 == n_units) || (kb + 1 == KB);
       if (!seg_end) continue;
 
-      // ---- end of a segment: fold the open group, reduce over warps ----
-#pragma unroll
-      for (int m = 0; m < M; ++m)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          tot[m][q] = fma2(acc[m][q], sc[q], tot[m][q]);
-          acc[m][q] = 0ull;
-        }
-      cur_group = -1;
+      // ---- end of a segment: reduce over warps, one output row at a time ----
+      named_bar_sync(1, kWarps * 32);  // every warp is done with its pairs
+      const int t = threadIdx.x;       // column within the slice
+      float v[M];
 #pragma unroll
       for (int m = 0; m < M; ++m) {
-        float4* dst = reinterpret_cast<float4*>(red + (warp * M + m) * kCols + lane * 8);
+        float4* dst = reinterpret_cast<float4*>(red + warp * kCols + lane * 8);
         const float2 a0 = unpack2(tot[m][0]), a1 = unpack2(tot[m][1]);
         const float2 a2 = unpack2(tot[m][2]), a3 = unpack2(tot[m][3]);
         dst[0] = make_float4(a0.x, a0.y, a1.x, a1.y);
         dst[1] = make_float4(a2.x, a2.y, a3.x, a3.y);
 #pragma unroll
         for (int q = 0; q < 4; ++q) tot[m][q] = 0ull;
-      }
-      named_bar_sync(1, kWarps * 32);
-      const int t = threadIdx.x;  // column within the slice
-      float v[M];
-#pragma unroll
-      for (int m = 0; m < M; ++m) {
+        named_bar_sync(1, kWarps * 32);
         float s = 0.0f;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) s += red[(w * M + m) * kCols + t];
+        for (int w = 0; w < kWarps; ++w) s += red[w * kCols + t];
         v[m] = s;
+        named_bar_sync(1, kWarps * 32);
       }
       if (clustered) {
         // stage the CTA's partial for the cluster reduction (thread t alone
-        // reads and writes column t)
+        // writes column t of each row)
 #pragma unroll
         for (int m = 0; m < M; ++m) red[m * kCols + t] = v[m];
         break;  // a cluster CTA owns exactly one segment
@@ -419,11 +424,10 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kMinBlocks)
           for (int m = 0; m < M; ++m) o[m * p.ldo + col] = vals[m];
         }
       };
-      const int64_t cfirst = unit_owner(slice * KB, U, G);
-      const int64_t clast = unit_owner(slice * KB + KB - 1, U, G);
+      const int64_t cfirst = unit_owner(static_cast<int64_t>(slice) * KB, U, G);
+      const int64_t clast = unit_owner(static_cast<int64_t>(slice) * KB + KB - 1, U, G);
       if (cfirst == clast) {
         store(v);
-        named_bar_sync(1, kWarps * 32);  // red is rewritten by the next segment
         continue;
       }
       float* mine = p.partials + (cta + slice) * (M * kCols);
@@ -449,7 +453,7 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kMinBlocks)
         store(sum);
         if (t == 0) p.sems[slice] = 0u;  // re-arm for the next call
       }
-      named_bar_sync(1, kWarps * 32);
+      named_bar_sync(1, kWarps * 32);  // last_flag is rewritten by the next segment
     }
   }
 
@@ -500,7 +504,7 @@ GemvPlan make_plan(int64_t M, int64_t N, int64_t K) {
   const int64_t U = NS * KB;
   const int64_t sms = num_sms();
   GemvPlan pl{};
-  if (U <= 8 * sms && NS <= sms) {
+  if (U <= 4 * sms && NS <= sms) {
     // small layer: a cluster per slice, the slice's units split between its CTAs
     int c = 1;
     while (c * 2 <= kMaxCluster && NS * c * 2 <= sms && c * 2 <= KB) c *= 2;
@@ -514,6 +518,12 @@ GemvPlan make_plan(int64_t M, int64_t N, int64_t K) {
     pl.grid_y = 1;
   }
   return pl;
+}
+
+int scale_rows_for(int group) {
+  // group-scale rows a 256-row unit can touch
+  const int span = (kRows + group - 1) / group + (kRows % group != 0 ? 1 : 0);
+  return span < kMaxScaleRows ? span : kMaxScaleRows;
 }
 
 }  // namespace
@@ -560,7 +570,10 @@ cudaError_t launch_w4a16_gemv(const DecodeArgs& a, cudaStream_t s, const char** 
   p.N = static_cast<int>(a.N);
   p.K = static_cast<int>(a.K);
   p.group = grouped ? a.group : kRows;
-  p.scale_rows = (grouped && a.group % kRows != 0) ? 2 : 1;
+  p.scale_rows = grouped ? scale_rows_for(a.group) : 1;
+  p.group_shift = -1;
+  for (int sh = 0; sh < 31; ++sh)
+    if ((1 << sh) == p.group) p.group_shift = sh;
   p.scalar_scale = a.scalar_scale;
   p.out = a.out;
   p.out_dtype = a.out_dtype;
@@ -583,12 +596,7 @@ cudaError_t launch_w4a16_gemv(const DecodeArgs& a, cudaStream_t s, const char** 
     *why = "the split-K GEMV needs a workspace";
     return cudaErrorInvalidValue;
   }
-  DecodeConsts dc;
-  dc.x[0] = 0x4B000008u;
-  dc.x[1] = 0x4B000080u;
-  dc.x[2] = 0x4B000800u;
-  dc.x[3] = 0x4B008000u;
-  dc.x[4] = 0x4B080000u;
+  const DecodeConsts dc{{0x800u, 0x8000u, 0x80000u, 0x800000u}};
 
   auto launch = [&](auto kernel, int smem_bytes) -> cudaError_t {
     cudaError_t e =

@@ -56,7 +56,7 @@ def test_gemv_4096(M, dt):
     (1, 1024, 4224, 192),    # groups straddle the 128-row units
     (1, 256, 163840, 128),   # stream-K: one slice split over every CTA (fan-in ~300)
     (2, 65536, 256, 128),    # stream-K: CTA ranges span several slices
-    (1, 8192, 128, 64),      # one unit per slice: clusters of one CTA, no reduction
+    (1, 8192, 256, 64),      # one unit per slice: clusters of one CTA, no reduction
 ])
 def test_gemv_shapes(M, N, K, group):
     a, packed, scales, ref = make_case(M, N, K, group=group, seed=N + K)
