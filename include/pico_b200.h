@@ -116,9 +116,10 @@ PK_API size_t pk_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int split
  * 1 = no split, > 1 = split the K reduction over that many CTAs (decode
  * shapes), reduced deterministically in split order through `workspace`
  * (pk_w4a16_workspace_size bytes, zero-filled once before its first use; the
- * kernel leaves it ready for the next call). With split_k = 0 and M <= 4 the
- * CUDA-core GEMV runs, a stream-K split whose partials also go through the
- * workspace; without one it falls back to the tensor-core decode kernel.
+ * kernel leaves it ready for the next call). With split_k = 0 at M = 1 (and
+ * at M = 2 for layers of 16 MB or more) a CUDA-core GEMV runs instead; for
+ * large layers it splits K over the SMs and reduces through the workspace,
+ * and without one it falls back to the tensor-core decode kernel.
  * A workspace may serve calls of different shapes and of pk_gemm_splitk in
  * turn (arrival counters sit in its first 64 KB, partials after them), but
  * calls sharing one workspace must not overlap on the GPU.

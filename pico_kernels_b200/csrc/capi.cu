@@ -212,7 +212,8 @@ size_t pk_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int split_k) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const void* aligned = reinterpret_cast<const void*>(16);
   size_t bytes = 0;
-  if (split_k == 0 && gemv_supported(M, N, K, 128, aligned, 8, aligned, aligned))
+  if (split_k == 0 && gemv_preferred(M, N, K) &&
+      gemv_supported(M, N, K, 128, aligned, 8, aligned, aligned))
     bytes = gemv_workspace_bytes(M, N, K);
   if (decode_supported(M, N, K, 128, nullptr, 8, aligned)) {
     const int split = split_k > 0 ? split_k : decode_pick_split(M, N, K);
@@ -238,8 +239,10 @@ int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t* wp, co
   if (split_k < 0) return fail(PK_ERR_SHAPE, "split_k must be >= 0");
   cudaStream_t s = as_stream(stream);
 
-  // M <= 4 with the automatic split: the CUDA-core GEMV (a weight stream).
-  if (split_k == 0 && gemv_supported(M, N, K, group_size, scales, lda, a, wp)) {
+  // Decode shapes where it is faster, with the automatic split: the CUDA-core
+  // GEMV (a weight stream).
+  if (split_k == 0 && gemv_preferred(M, N, K) &&
+      gemv_supported(M, N, K, group_size, scales, lda, a, wp)) {
     const size_t need = gemv_workspace_bytes(M, N, K);
     bool have_ws = need == 0;
     if (need > 0 && workspace != nullptr) {

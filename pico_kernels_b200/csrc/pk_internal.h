@@ -90,7 +90,8 @@ int decode_pick_split(int64_t M, int64_t N, int64_t K);
 size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int split);
 cudaError_t launch_w4a16_decode(const DecodeArgs& args, cudaStream_t s, const char** why);
 
-// ---- w4a16_gemv.cu (M <= 4 on the CUDA cores; stream-K over SMs) -------
+// ---- w4a16_gemv.cu (M <= 2 on the CUDA cores; cluster or stream-K split) -
+bool gemv_preferred(int64_t M, int64_t N, int64_t K);  // faster than the decode kernel here
 bool gemv_supported(int64_t M, int64_t N, int64_t K, int group, const void* scales, int64_t lda,
                     const void* a, const void* wp);
 size_t gemv_workspace_bytes(int64_t M, int64_t N, int64_t K);  // 0: no split-K fixup needed

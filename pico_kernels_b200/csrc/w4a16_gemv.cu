@@ -1,10 +1,10 @@
-// W4A16 GEMV for decode shapes (M <= 4) on sm_100a, on the CUDA cores.
+// W4A16 GEMV for decode shapes (M <= 2) on sm_100a, on the CUDA cores.
 //
 // out[M, N] = A[M, K] @ (q[K, N] * s[K/g, N])  -- gemm_int4.int4_gemm
 // (gemm_int4.py:75-92) with group scales, q unpacked from Wp[K, N/2] in the
 // reference's nibble order (gemm_int4.py:43-50, pack_int4_n at :65-72).
 //
-// At M <= 4 the layer is a stream over the packed weights (K*N/2 bytes) with
+// At M <= 2 the layer is a stream over the packed weights (K*N/2 bytes) with
 // 2*M*K*N flops: far below one flop per byte, so the tensor cores would only
 // add the dequantized-operand round trip through shared memory. This kernel
 // streams the weights once and does the arithmetic in fp32 on the CUDA cores.
@@ -68,16 +68,17 @@ constexpr int kWarps = 8;               // dequant/FMA warps
 constexpr int kProducerWarp = kWarps;
 constexpr int kThreads = (kWarps + 1) * 32;
 constexpr int kRowsPerWarp = kRows / kWarps;  // 32: one row per lane for the activations
-constexpr int kMaxM = 4;
+constexpr int kMaxM = 2;
 constexpr int kMaxCluster = 8;
 constexpr int kMaxScaleRows = 4;        // scale rows a unit can touch (group >= 64)
 constexpr int kSmemTwoPerSm = 115712;   // per-CTA limit for two resident CTAs (228 KB SM)
 
 template <int M>
 struct GemvCfg {
-  // M = 1: three slots and ~113 KB, two CTAs per SM; M = 2: two slots, two
-  // CTAs per SM; M >= 3 (registers): one CTA per SM with five slots.
-  static constexpr int kStages = M == 1 ? 3 : (M == 2 ? 2 : 5);
+  // M = 1: three slots and ~113 KB; M = 2: two slots. Either way two CTAs
+  // share an SM (a stream-K grid's pair, or this grid and the next under
+  // programmatic launch).
+  static constexpr int kStages = M == 1 ? 3 : 2;
   static constexpr int kWBytes = kRows * kRowBytes;          // 32768
   static constexpr int kSBytes = kMaxScaleRows * kCols * 2;  // 2048
   static constexpr int kABytes = kRows * 2 * M;              // 512 * M
@@ -92,8 +93,8 @@ struct GemvCfg {
   static constexpr int kScratchBytes = kPairBytes > kRedBytes ? kPairBytes : kRedBytes;
   static constexpr int kBarOff = kScratchOff + kScratchBytes;
   static constexpr int kSmemBytes = kBarOff + 2 * kStages * 8 + 16 + 128;
-  static constexpr int kCtasPerSm = M <= 2 ? 2 : 1;
-  static_assert(kCtasPerSm == 1 || kSmemBytes <= kSmemTwoPerSm, "two CTAs must fit an SM");
+  static constexpr int kCtasPerSm = 2;
+  static_assert(kSmemBytes <= kSmemTwoPerSm, "two CTAs must fit an SM");
 };
 
 // Bit patterns 8 << 4p for p = 2..5 (the flipped sign bit of a nibble at
@@ -512,7 +513,7 @@ GemvPlan make_plan(int64_t M, int64_t N, int64_t K) {
     pl.grid_x = c;
     pl.grid_y = NS;
   } else {
-    const int64_t cap = (M <= 2 ? 2 : 1) * sms;
+    const int64_t cap = 2 * sms;
     pl.cluster = 0;
     pl.grid_x = U < cap ? U : cap;
     pl.grid_y = 1;
@@ -527,6 +528,16 @@ int scale_rows_for(int group) {
 }
 
 }  // namespace
+
+bool gemv_preferred(int64_t M, int64_t N, int64_t K) {
+  // Measured on B200 against the tensor-core decode kernel: at M = 1 the GEMV
+  // is faster at every size (4096 x 4096: 7.8 vs 8.4 us; Llama-70B up_proj:
+  // 35 vs 66 us); at M = 2 only for layers of 16 MB or more (4096 x 4096:
+  // 10.1 vs 8.5 us; up_proj: 46 vs 66 us); from M = 3 on the CUDA-core FMAs
+  // cost more than the tensor core's wasted columns.
+  if (M == 1) return true;
+  return M == 2 && K * (N / 2) >= (16ll << 20);
+}
 
 bool gemv_supported(int64_t M, int64_t N, int64_t K, int group, const void* scales, int64_t lda,
                     const void* a, const void* wp) {
@@ -626,12 +637,8 @@ cudaError_t launch_w4a16_gemv(const DecodeArgs& a, cudaStream_t s, const char** 
   auto by_m = [&](auto tag, auto grouped_tag) -> cudaError_t {
     using T = decltype(tag);
     constexpr bool kG = decltype(grouped_tag)::value;
-    switch (a.M) {
-      case 1: return launch(w4a16_gemv_kernel<1, T, kG>, GemvCfg<1>::kSmemBytes);
-      case 2: return launch(w4a16_gemv_kernel<2, T, kG>, GemvCfg<2>::kSmemBytes);
-      case 3: return launch(w4a16_gemv_kernel<3, T, kG>, GemvCfg<3>::kSmemBytes);
-      default: return launch(w4a16_gemv_kernel<4, T, kG>, GemvCfg<4>::kSmemBytes);
-    }
+    if (a.M == 1) return launch(w4a16_gemv_kernel<1, T, kG>, GemvCfg<1>::kSmemBytes);
+    return launch(w4a16_gemv_kernel<2, T, kG>, GemvCfg<2>::kSmemBytes);
   };
   if (a.a_dtype == PK_BF16) {
     return grouped ? by_m(__nv_bfloat16{}, std::true_type{})
