@@ -119,7 +119,10 @@ PK_API size_t pk_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int split
  * kernel leaves it ready for the next call). With split_k = 0 at M = 1 (and
  * at M = 2 for layers of 16 MB or more) a CUDA-core GEMV runs instead; for
  * large layers it splits K over the SMs and reduces through the workspace,
- * and without one it falls back to the tensor-core decode kernel.
+ * and without one it falls back to the tensor-core decode kernel. From
+ * M = 1024 the weights are dequantized once into the workspace (16-bit
+ * B[K, N] after the counters, pk_w4a16_workspace_size bytes) and the dense
+ * tensor-core GEMM runs on it; without that workspace the fused kernel runs.
  * A workspace may serve calls of different shapes and of pk_gemm_splitk in
  * turn (arrival counters sit in its first 64 KB, partials after them), but
  * calls sharing one workspace must not overlap on the GPU.

@@ -39,6 +39,11 @@ bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* bas
 
 int num_sms();  // SM count of the current device (cached)
 
+// W4A16 with large M: dequantize the weights once into a 16-bit workspace
+// B[K, N] (prefill_workspace_bytes) and run the dense tensor-core GEMM.
+bool prefill_dequant_once(int64_t M, int64_t N, int64_t K);
+size_t prefill_workspace_bytes(int64_t N, int64_t K);
+
 // Split-K workspaces. Every kernel that reduces through a caller's workspace
 // keeps its arrival counters in the first kCounterBytes and its fp32 partials
 // after them. Counters are zero between calls (each call re-arms the ones it
@@ -63,6 +68,9 @@ cudaError_t launch_unpack_int4(const uint8_t* p, int64_t K, int64_t N, int8_t* q
                                cudaStream_t s);
 cudaError_t launch_fp8_quantize(const void* x, int dtype, int64_t n, float scale, uint8_t* y,
                                 cudaStream_t s);
+// B[K, N] (dtype) = q * s rounded to dtype, or q when scales == nullptr (N % 32 == 0)
+cudaError_t launch_dequant_int4(const uint8_t* wp, const void* scales, int group, int dtype,
+                                int64_t K, int64_t N, void* out, cudaStream_t s);
 
 // ---- w4a16_decode.cu -----------------------------------------------------
 struct DecodeArgs {

@@ -142,4 +142,9 @@ def test_workspace_shared_across_kernels():
         b = torch.randn(512, 2048, device="cuda", dtype=torch.bfloat16)
         c = pk.triton_gemm_splitk(x, b, split_k=4)
         assert torch.allclose(c, x.float() @ b.float(), atol=1e-2, rtol=1e-3)
+        # large-M W4A16: its dequantized weights go after the counter region
+        a3, p3, s3, ref3 = make_case(1024, 512, 1024, seed=53)
+        y3 = pk.int4_gemm(a3, p3, s3)
+        rel3 = np.linalg.norm(y3.cpu().numpy() - ref3) / np.linalg.norm(ref3)
+        assert rel3 < 5e-3
     assert pk.device_status() == (0, 0)

@@ -126,3 +126,37 @@ def test_errors_are_reference_compatible():
         pk.int4_gemm(a, wp, 1.0)
     with pytest.raises(TypeError):
         pk.int4_gemm(a.float(), torch.zeros(256, 64, dtype=torch.uint8, device="cuda"), 1.0)
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_prefill_dequant_once_matches_fused(dt):
+    """M >= 1024 with a workspace: the weights are dequantized once into the
+    workspace (q*s rounded to A's dtype, the fused kernel's operand) and the
+    dense tcgen05 GEMM runs; without a workspace the fused kernel runs. Same
+    operand values and tile order, so the two agree to fp32 summation order."""
+    from pico_kernels_b200 import _lib as L
+    lib = L.load()
+    M, N, K = 1024, 1024, 2048
+    a, w, ref = make_case(M, N, K, dt, seed=13)
+    packed, scales = pk.quantize_int4_grouped(w.cuda(), 128)
+    a = a.cuda()
+    assert lib.pk_w4a16_workspace_size(M, N, K, 0) >= K * N * 2
+    y_once = pk.int4_gemm(a, packed, scales)                      # workspace given
+    check(y_once, ref, dt, "dequant once")
+    y_fused = torch.empty(M, N, device="cuda")
+    rc = lib.pk_w4a16_gemm(L.ptr(a), L.dtype_code(dt), K, L.ptr(packed), L.ptr(scales), 1.0, 128,
+                           M, N, K, L.ptr(y_fused), L.dtype_code(torch.float32), N, 0, None, 0,
+                           torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, L.last_error()
+    rel = (torch.norm(y_once - y_fused) / torch.norm(y_fused)).item()
+    assert rel < 1e-6, rel
+
+
+def test_prefill_dequant_once_per_tensor_scale():
+    torch.manual_seed(1)
+    a = torch.randn(1024, 512, device="cuda", dtype=torch.float16)
+    w = torch.randn(512, 256, device="cuda", dtype=torch.float16)
+    w_q, scale = pk.quantize_int4(w)
+    c = pk.int4_gemm(a, pk.pack_int4_n(w_q), scale)
+    ref = a.float() @ (w_q.float() * scale)
+    assert (torch.norm(c - ref) / torch.norm(ref)).item() < 1e-5
