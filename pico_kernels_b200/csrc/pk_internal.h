@@ -68,7 +68,7 @@ cudaError_t launch_unpack_int4(const uint8_t* p, int64_t K, int64_t N, int8_t* q
                                cudaStream_t s);
 cudaError_t launch_fp8_quantize(const void* x, int dtype, int64_t n, float scale, uint8_t* y,
                                 cudaStream_t s);
-// B[K, N] (dtype) = q * s rounded to dtype, or q when scales == nullptr (N % 32 == 0)
+// B[K, N] (dtype) = q * s rounded to dtype, or q when scales == nullptr (N % 8 == 0)
 cudaError_t launch_dequant_int4(const uint8_t* wp, const void* scales, int group, int dtype,
                                 int64_t K, int64_t N, void* out, cudaStream_t s);
 

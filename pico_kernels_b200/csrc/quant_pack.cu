@@ -255,49 +255,31 @@ __global__ void fp8_quantize_kernel(const T* __restrict__ x, int64_t n, float sc
 }
 
 // Dequantize packed int4 weights once into a 16-bit row-major B[K, N] for the
-// dense tensor-core GEMM of large-M calls: B[k, n] = round_T(q[k, n] * s[k/g, n])
-// (the value the fused W4A16 kernel feeds its MMA), or q exactly when there are
-// no group scales. One thread per 32 weights of a row: a 16-byte packed load,
-// the row's 32 scales (L2-resident), four 16-byte stores.
+// dense tensor-core GEMM of large-M calls: B[k, n] = q[k, n] * s[k/g, n] rounded
+// to T by the same packed instructions the fused W4A16 kernel uses for its MMA
+// operand (dequant8), or q exactly when there are no group scales. One thread
+// per 8 columns of a row, so a warp's loads (128 B packed, 512 B scales) and its
+// 512 B store are each one contiguous access.
 template <typename T, bool kGrouped>
 __global__ void __launch_bounds__(256)
     dequant_int4_kernel(const uint8_t* __restrict__ wp, const T* __restrict__ scales, int group,
                         int64_t K, int64_t N, T* __restrict__ out) {
-  const int64_t chunks_per_row = N / 32;
-  const int64_t total = K * chunks_per_row;
-  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < total;
-       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t k = c / chunks_per_row;
-    const int64_t n0 = (c - k * chunks_per_row) * 32;
-    const uint4 raw = ldg_stream_v4(wp + k * (N / 2) + n0 / 2);
-    const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
-    const T* srow = kGrouped ? scales + (k / group) * N + n0 : nullptr;
-    uint4 o[4];
-    uint32_t* ov = reinterpret_cast<uint32_t*>(o);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float sc[8];
-      if constexpr (kGrouped) {
-        const uint4 sraw = *reinterpret_cast<const uint4*>(srow + 8 * i);
-        const T* sv = reinterpret_cast<const T*>(&sraw);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) sc[j] = to_f32<T>(sv[j]);
-      }
-#pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        // nibble j of the word is column n0 + 8i + j (low nibble = even column)
-        const int q0 = static_cast<int>(words[i] << (28 - 4 * j)) >> 28;
-        const int q1 = static_cast<int>(words[i] << (24 - 4 * j)) >> 28;
-        const float v0 = kGrouped ? static_cast<float>(q0) * sc[j] : static_cast<float>(q0);
-        const float v1 = kGrouped ? static_cast<float>(q1) * sc[j + 1] : static_cast<float>(q1);
-        const T t0 = from_f32<T>(v0), t1 = from_f32<T>(v1);
-        ov[4 * i + j / 2] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&t0)) |
-                            (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&t1)) << 16);
-      }
+  // Blocks stride over rows, threads over a row's 8-column items: no integer
+  // division in the loop (a 64-bit one per item made the pass issue-bound).
+  const int items = static_cast<int>(N / 8);
+  for (int64_t k = blockIdx.x; k < K; k += gridDim.x) {
+    const uint32_t* wrow = reinterpret_cast<const uint32_t*>(wp + k * (N / 2));
+    const uint4* srow =
+        kGrouped ? reinterpret_cast<const uint4*>(scales + (k / group) * N) : nullptr;
+    uint4* orow = reinterpret_cast<uint4*>(out + k * N);
+    for (int i = threadIdx.x; i < items; i += blockDim.x) {
+      const uint32_t w = __ldg(wrow + i);
+      uint4 sc = make_uint4(0u, 0u, 0u, 0u);
+      if constexpr (kGrouped) sc = __ldg(srow + i);
+      uint32_t o[4];
+      dequant8<T, kGrouped>(w, sc.x, sc.y, sc.z, sc.w, o);
+      orow[i] = make_uint4(o[0], o[1], o[2], o[3]);
     }
-    uint4* dst = reinterpret_cast<uint4*>(out + k * N + n0);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) dst[i] = o[i];
   }
 }
 
@@ -449,9 +431,10 @@ cudaError_t launch_fp8_quantize(const void* x, int dtype, int64_t n, float scale
 
 cudaError_t launch_dequant_int4(const uint8_t* wp, const void* scales, int group, int dtype,
                                 int64_t K, int64_t N, void* out, cudaStream_t s) {
-  if (N % 32 != 0) return cudaErrorInvalidValue;
+  if (N % 8 != 0) return cudaErrorInvalidValue;
   const int threads = 256;
-  const int grid = grid_for(K * (N / 32), threads);
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
+  const int grid = static_cast<int>(K < cap ? K : cap);
   const bool g = scales != nullptr;
   if (dtype == PK_BF16) {
     auto sp = static_cast<const __nv_bfloat16*>(scales);
