@@ -154,6 +154,43 @@ PK_API int pk_w4a16_gemm_noalloc(const void* a, int a_dtype, int64_t lda, const 
                                  int split_k, void* stream);
 
 /* ---------------------------------------------------------------------- */
+/* N-sharded W4A16 layer with the output exchange fused into the GEMV      */
+/* ---------------------------------------------------------------------- */
+
+/* Peer memory for the fused exchange. pk_shared_alloc: cudaMalloc'd, zeroed
+ * device memory that peers can map; pk_ipc_get_handle writes its 64-byte CUDA
+ * IPC handle; pk_ipc_open maps a peer's handle into this process (lazy peer
+ * access over NVLink); pk_ipc_close / pk_shared_free release them. No
+ * counterpart in the reference (it has no multi-GPU path). */
+PK_API int pk_shared_alloc(size_t bytes, void** ptr);
+PK_API int pk_shared_free(void* ptr);
+PK_API int pk_ipc_get_handle(const void* ptr, void* handle64);
+PK_API int pk_ipc_open(const void* handle64, void** ptr);
+PK_API int pk_ipc_close(void* ptr);
+
+/* One rank's slice of an N-sharded W4A16 layer, y[M, N_full] = A @ dequant(W),
+ * where this rank holds columns [n_offset, n_offset + N) (Wp [K, N/2],
+ * scales [K/g, N]). The GEMV writes its columns straight into every rank's
+ * output buffer peer_out[r] (fp32 or bf16 [M, ldo] with ldo >= N_full, mapped
+ * with pk_ipc_open), then its last CTA adds 1 to every peer's 32-bit flag
+ * peer_flag[r] (release, system scope) and waits, at most ~2 s, until its own
+ * flag reaches epoch * (world - 1): on return every rank's columns are in
+ * peer_out[rank]. All ranks call it in the same order with the same epoch
+ * (1, 2, 3, ...); a buffer must not be rewritten by the next call before its
+ * reader is done (alternate two buffers). Needs a workspace of
+ * pk_w4a16_workspace_size bytes (at least 64 KB). Covers the GEMV's shapes
+ * (M = 1, and M = 2 on slices of 16 MB or more; world <= 8); returns
+ * PK_ERR_UNSUPPORTED otherwise, so the caller can exchange with NCCL instead.
+ * Replaces the all-gather that gemm_int4.int4_gemm's callers would need on a
+ * sharded layer (no counterpart in the reference). */
+PK_API int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t* wp,
+                                 const void* scales, float scalar_scale, int group_size, int64_t M,
+                                 int64_t N, int64_t K, int out_dtype, int64_t ldo, int64_t n_offset,
+                                 int world, int rank, const uint64_t* peer_out,
+                                 const uint64_t* peer_flag, uint32_t epoch, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------- */
 /* fp8 (e4m3) GEMM                                                         */
 /* ---------------------------------------------------------------------- */
 

@@ -65,6 +65,14 @@ SIGNATURES = {
     "pk_fp8_gemm": (_int, [_vp, _vp, _i64, _i64, _i64, _f32, _vp, _int, _vp]),
     "pk_gemm_splitk_workspace_size": (_sz, [_i64, _i64, _i64, _int]),
     "pk_gemm_splitk": (_int, [_vp, _vp, _int, _i64, _i64, _i64, _int, _vp, _vp, _sz, _vp]),
+    "pk_shared_alloc": (_int, [_sz, _c.POINTER(_vp)]),
+    "pk_shared_free": (_int, [_vp]),
+    "pk_ipc_get_handle": (_int, [_vp, _vp]),
+    "pk_ipc_open": (_int, [_vp, _c.POINTER(_vp)]),
+    "pk_ipc_close": (_int, [_vp]),
+    "pk_w4a16_gemm_sharded": (_int, [_vp, _int, _i64, _vp, _vp, _f32, _int, _i64, _i64, _i64,
+                                     _int, _i64, _i64, _int, _int, _vp, _vp, _c.c_uint32, _vp,
+                                     _sz, _vp]),
 }
 
 _lib = None

@@ -518,4 +518,112 @@ int pk_gemm_splitk(const void* a, const void* b, int dtype, int64_t M, int64_t N
   return PK_OK;
 }
 
+int pk_shared_alloc(size_t bytes, void** ptr) {
+  if (ptr == nullptr || bytes == 0) return fail(PK_ERR_SHAPE, "need a size and an output pointer");
+  *ptr = nullptr;
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "shared buffer allocation");
+  e = cudaMemset(*ptr, 0, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "shared buffer clear");
+  ok();
+  return PK_OK;
+}
+
+int pk_shared_free(void* ptr) {
+  cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "shared buffer free");
+  ok();
+  return PK_OK;
+}
+
+int pk_ipc_get_handle(const void* ptr, void* handle64) {
+  if (ptr == nullptr || handle64 == nullptr) return fail(PK_ERR_SHAPE, "null pointer");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e != cudaSuccess) return cuda_fail(e, "IPC handle");
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  std::memcpy(handle64, &h, sizeof(h));
+  ok();
+  return PK_OK;
+}
+
+int pk_ipc_open(const void* handle64, void** ptr) {
+  if (handle64 == nullptr || ptr == nullptr) return fail(PK_ERR_SHAPE, "null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle64, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "IPC open");
+  ok();
+  return PK_OK;
+}
+
+int pk_ipc_close(void* ptr) {
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "IPC close");
+  ok();
+  return PK_OK;
+}
+
+int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t* wp,
+                          const void* scales, float scalar_scale, int group_size, int64_t M,
+                          int64_t N, int64_t K, int out_dtype, int64_t ldo, int64_t n_offset,
+                          int world, int rank, const uint64_t* peer_out,
+                          const uint64_t* peer_flag, uint32_t epoch, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  if (!a || !wp || !peer_out || !peer_flag) return fail(PK_ERR_SHAPE, "null pointer");
+  if (M <= 0 || N <= 0 || K <= 0 || (N % 2) != 0) return fail(PK_ERR_SHAPE, "bad shape");
+  if (world < 1 || world > 8 || rank < 0 || rank >= world)
+    return fail(PK_ERR_SHAPE, "need 1 <= world <= 8 and 0 <= rank < world");
+  if (n_offset < 0 || ldo < n_offset + N) return fail(PK_ERR_SHAPE, "ldo too small for the slice");
+  if (!is16(a_dtype)) return fail(PK_ERR_DTYPE, "A must be f16 or bf16");
+  if (out_dtype != PK_F32 && out_dtype != PK_BF16)
+    return fail(PK_ERR_DTYPE, "output must be f32 or bf16");
+  if (!(gemv_preferred(M, N, K) && gemv_supported(M, N, K, group_size, scales, lda, a, wp)))
+    return fail(PK_ERR_UNSUPPORTED, "the fused exchange covers the GEMV's shapes only");
+  size_t need = gemv_workspace_bytes(M, N, K);
+  if (need < kCounterBytes) need = kCounterBytes;
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(PK_ERR_WORKSPACE, "the sharded GEMV needs %zu workspace bytes, got %zu", need,
+                workspace_bytes);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(PK_ERR_ALIGN, "workspace must be 256-byte aligned");
+  for (int r = 0; r < world; ++r)
+    if (peer_out[r] == 0 || peer_flag[r] == 0 || (peer_flag[r] & 3) != 0)
+      return fail(PK_ERR_SHAPE, "peer %d: missing output or misaligned flag", r);
+  DecodeArgs p{};
+  p.a = a;
+  p.lda = lda;
+  p.wp = wp;
+  p.scales = scales;
+  p.group = group_size;
+  p.scalar_scale = scales ? 1.0f : scalar_scale;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.out = reinterpret_cast<void*>(peer_out[rank]);
+  p.out_dtype = out_dtype;
+  p.ldo = ldo;
+  p.a_dtype = a_dtype;
+  p.split = 1;
+  p.status = device_status_ptr();
+  p.sems = ws_counters(workspace);
+  p.partials = ws_partials(workspace);
+  GemvShard sh{};
+  sh.n_offset = n_offset;
+  sh.world = world;
+  sh.rank = rank;
+  for (int r = 0; r < world; ++r) {
+    sh.peer_out[r] = peer_out[r];
+    sh.peer_flag[r] = peer_flag[r];
+  }
+  sh.epoch = epoch;
+  sh.done = ws_counters(workspace) + (kMaxCounters - 1);
+  const char* why = "";
+  cudaError_t e = launch_w4a16_gemv(p, as_stream(stream), &why, &sh);
+  if (e == cudaErrorInvalidValue && why[0] != '\0') return fail(PK_ERR_ALIGN, "%s", why);
+  if (e != cudaSuccess) return cuda_fail(e, "sharded w4a16 gemv launch");
+  ok();
+  return PK_OK;
+}
+
 }  // extern "C"

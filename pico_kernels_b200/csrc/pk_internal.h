@@ -29,6 +29,7 @@ enum WaitSite : int {
   kSiteGemmDequant = 204,
   kSiteGemvProducer = 301,
   kSiteGemvConsumer = 302,
+  kSiteGemvPeers = 303,
 };
 
 // Host-side tensor map encoding (cuTensorMapEncodeTiled via the runtime's
@@ -103,7 +104,18 @@ bool gemv_preferred(int64_t M, int64_t N, int64_t K);  // faster than the decode
 bool gemv_supported(int64_t M, int64_t N, int64_t K, int group, const void* scales, int64_t lda,
                     const void* a, const void* wp);
 size_t gemv_workspace_bytes(int64_t M, int64_t N, int64_t K);  // 0: no split-K fixup needed
-cudaError_t launch_w4a16_gemv(const DecodeArgs& args, cudaStream_t s, const char** why);
+// Output exchange of an N-sharded layer: the GEMV writes its columns
+// [n_offset, n_offset + N) into every rank's buffer, then flags each peer.
+struct GemvShard {
+  int64_t n_offset;
+  int world, rank;
+  uint64_t peer_out[8];
+  uint64_t peer_flag[8];
+  uint32_t epoch;
+  unsigned* done;  // zeroed completion counter (workspace)
+};
+cudaError_t launch_w4a16_gemv(const DecodeArgs& args, cudaStream_t s, const char** why,
+                              const GemvShard* shard = nullptr);
 
 // ---- gemm_tc.cu (persistent tcgen05 GEMM: fp8, dense split-K, W4A16 prefill)
 struct GemmArgs {

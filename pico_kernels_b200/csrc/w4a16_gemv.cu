@@ -171,19 +171,68 @@ __device__ __forceinline__ unsigned atomic_add_acq_rel(unsigned* p, unsigned v) 
   return old;
 }
 
+constexpr int kMaxPeers = 8;
+
 struct GemvParams {
   int N, K, group;
   int group_shift;     // log2(group) when group is a power of two, else -1
   int scale_rows;      // group-scale rows per unit in the scale box
   int cluster;         // 0: stream-K; else CTAs per slice (cluster size)
   float scalar_scale;
-  void* out;
   int out_dtype;
   int64_t ldo;
+  int64_t n_offset;    // column of this slice in the output rows
+  int world, rank;     // output copies (1: just peer_out[0])
+  uint64_t peer_out[kMaxPeers];   // output buffers, peer_out[rank] is this GPU's
+  uint64_t peer_flag[kMaxPeers];  // arrival flags (sharded exchange)
+  uint32_t epoch;
+  unsigned* done;      // CTA completion counter (sharded exchange), zero between calls
   float* partials;
   unsigned* sems;
   int* status;
 };
+
+// Write column `col` of output row m into every copy of the output.
+__device__ __forceinline__ void store_col(const GemvParams& p, int m, int64_t col, float v) {
+  const int64_t idx = m * p.ldo + p.n_offset + col;
+  for (int r = 0; r < p.world; ++r) {
+    if (p.out_dtype == PK_BF16)
+      reinterpret_cast<__nv_bfloat16*>(p.peer_out[r])[idx] = __float2bfloat16_rn(v);
+    else
+      reinterpret_cast<float*>(p.peer_out[r])[idx] = v;
+  }
+}
+
+// After every CTA's stores: the last CTA raises each peer's flag (release,
+// system scope) and waits, bounded, for all peers' contributions to this
+// GPU's copy.
+__device__ __forceinline__ void sharded_finish(const GemvParams& p) {
+  __threadfence_system();  // this thread's peer stores before the CTA's arrival
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  const unsigned total = gridDim.x * gridDim.y;
+  unsigned prev;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p.done) : "memory");
+  if (prev != total - 1) return;
+  *p.done = 0u;  // re-arm; the next call starts after this grid completes
+  for (int r = 0; r < p.world; ++r) {
+    if (r == p.rank) continue;
+    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.peer_flag[r]) : "memory");
+  }
+  const uint32_t target = p.epoch * static_cast<uint32_t>(p.world - 1);
+  const unsigned* own = reinterpret_cast<const unsigned*>(p.peer_flag[p.rank]);
+  const long long t0 = clock64();
+  while (true) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(own) : "memory");
+    if (static_cast<int>(v - target) >= 0) break;
+    if (clock64() - t0 > PK_WAIT_CYCLES) {
+      record_error(p.status, PK_ERR_TIMEOUT, kSiteGemvPeers);
+      break;
+    }
+    __nanosleep(100);
+  }
+}
 
 // Index of the scale group holding K row `row` (a shift for power-of-two groups).
 __device__ __forceinline__ int group_of(int row, const GemvParams& p) {
@@ -415,15 +464,8 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
       const int64_t col = static_cast<int64_t>(slice) * kCols + t;
       auto store = [&](const float* vals) {
         if (col >= p.N) return;
-        if (p.out_dtype == PK_BF16) {
-          __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out);
 #pragma unroll
-          for (int m = 0; m < M; ++m) o[m * p.ldo + col] = __float2bfloat16_rn(vals[m]);
-        } else {
-          float* o = static_cast<float*>(p.out);
-#pragma unroll
-          for (int m = 0; m < M; ++m) o[m * p.ldo + col] = vals[m];
-        }
+        for (int m = 0; m < M; ++m) store_col(p, m, col, vals[m]);
       };
       const int64_t cfirst = unit_owner(static_cast<int64_t>(slice) * KB, U, G);
       const int64_t clast = unit_owner(static_cast<int64_t>(slice) * KB + KB - 1, U, G);
@@ -476,16 +518,12 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
         for (int r = 0; r < cs; ++r)
           s += ld_cluster_f32(cluster_map(red_addr + (m * kCols + c) * 4, static_cast<uint32_t>(r)));
         const int64_t col = slice * kCols + c;
-        if (col < p.N) {
-          if (p.out_dtype == PK_BF16)
-            static_cast<__nv_bfloat16*>(p.out)[m * p.ldo + col] = __float2bfloat16_rn(s);
-          else
-            static_cast<float*>(p.out)[m * p.ldo + col] = s;
-        }
+        if (col < p.N) store_col(p, m, col, s);
       }
     }
     cluster_sync();
   }
+  if (p.world > 1) sharded_finish(p);
 }
 
 CUtensorMapDataType tmap_type16(int dt) {
@@ -544,7 +582,7 @@ bool gemv_supported(int64_t M, int64_t N, int64_t K, int group, const void* scal
   if (M < 1 || M > kMaxM) return false;
   if (N < kCols || N % 32 != 0 || K < kRows) return false;
   if (N > (1ll << 30) || K > (1ll << 30)) return false;
-  if ((N + kCols - 1) / kCols > kMaxCounters) return false;
+  if ((N + kCols - 1) / kCols >= kMaxCounters) return false;  // the last counter: sharded calls
   if (lda % 8 != 0 || (reinterpret_cast<uintptr_t>(a) & 15) != 0) return false;
   if ((reinterpret_cast<uintptr_t>(wp) & 15) != 0) return false;
   if (scales != nullptr &&
@@ -567,7 +605,8 @@ size_t gemv_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   return kCounterBytes + static_cast<size_t>(G + NS) * M * kCols * sizeof(float);
 }
 
-cudaError_t launch_w4a16_gemv(const DecodeArgs& a, cudaStream_t s, const char** why) {
+cudaError_t launch_w4a16_gemv(const DecodeArgs& a, cudaStream_t s, const char** why,
+                              const GemvShard* shard) {
   CUtensorMap tmW, tmA, tmS;
   const CUtensorMapDataType dt = tmap_type16(a.a_dtype);
   if (!encode_tmap_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.wp, a.N / 2, a.K, a.N / 2, kRowBytes,
@@ -586,9 +625,27 @@ cudaError_t launch_w4a16_gemv(const DecodeArgs& a, cudaStream_t s, const char** 
   for (int sh = 0; sh < 31; ++sh)
     if ((1 << sh) == p.group) p.group_shift = sh;
   p.scalar_scale = a.scalar_scale;
-  p.out = a.out;
   p.out_dtype = a.out_dtype;
   p.ldo = a.ldo;
+  p.world = 1;
+  p.rank = 0;
+  p.n_offset = 0;
+  p.peer_out[0] = reinterpret_cast<uint64_t>(a.out);
+  if (shard != nullptr) {
+    if (shard->world < 1 || shard->world > kMaxPeers || shard->done == nullptr) {
+      *why = "sharded GEMV: 1 <= world <= 8 and a workspace are required";
+      return cudaErrorInvalidValue;
+    }
+    p.world = shard->world;
+    p.rank = shard->rank;
+    p.n_offset = shard->n_offset;
+    for (int r = 0; r < shard->world; ++r) {
+      p.peer_out[r] = shard->peer_out[r];
+      p.peer_flag[r] = shard->peer_flag[r];
+    }
+    p.epoch = shard->epoch;
+    p.done = shard->done;
+  }
   p.partials = a.partials;
   p.sems = a.sems;
   p.status = a.status;

@@ -60,6 +60,19 @@ def _worker(rank, world, port, q):
         n0, n1 = sharded.shard_columns(1024, world, rank)
         y = sharded.sharded_fp8_gemm(a8, sa, b8[:, n0:n1].contiguous(), sb, world)
         ok.append(bool(torch.equal(y, full)))
+        # fused exchange: the GEMV writes every rank's output over NVLink
+        ex = sharded.PeerExchange(max_m=2, n_full=8192)
+        try:
+            for it, (M, K) in enumerate(((1, 4096), (1, 2048), (1, 4096))):
+                a, packed, scales = _layer(M, 8192, K, dev)
+                a = a + it  # a different input on every call
+                full = pk.int4_gemm(a, packed, scales)
+                p_r, s_r = sharded.shard_int4(packed, scales, world, rank)
+                y = sharded.sharded_int4_gemm(a, p_r, s_r, 128, world, exchange=ex)
+                rel = (torch.norm(y - full) / torch.norm(full)).item()
+                ok.append(rel < 1e-5 and pk.device_status() == (0, 0))
+        finally:
+            ex.close()
         q.put((rank, ok))
     finally:
         dist.destroy_process_group()
