@@ -261,6 +261,20 @@ class Workload:
         self.ws_bytes = (self.lib.pk_w4a16_workspace_size(M, self.NL, K, split_k)
                          if self.kind == "w4a16" else 0)
         self.ws = _lib.workspace(device, self.ws_bytes, tag="bench")
+        # M = 1 sharded layers: the GEMV writes every rank's output itself
+        self.exchange = None
+        if self.sharded and self.world > 1 and self.kind == "w4a16" and split_k == 0:
+            from pico_kernels_b200 import sharded
+            if M == 1:  # the GEMV's shape (pk_w4a16_gemm_sharded covers it)
+                self.exchange = sharded.PeerExchange(max_m=M, n_full=N, dtype=self.out_dtype)
+                ex = self.exchange
+                self.ex_ws_bytes = max(self.lib.pk_w4a16_workspace_size(M, self.NL, K, 0), 1 << 16)
+                self.ex_ws = _lib.workspace(device, self.ex_ws_bytes, tag="exchange")
+                import ctypes
+                self.ex_outs = [(ctypes.c_uint64 * self.world)(*[b + par * ex.buf_bytes for b in ex.bases])
+                                for par in (0, 1)]
+                self.ex_flags = (ctypes.c_uint64 * self.world)(*[b + ex.flag_off for b in ex.bases])
+                self.ex_calls = 0
         torch.cuda.synchronize()
 
     def gemm(self, i: int) -> torch.Tensor:
@@ -285,7 +299,23 @@ class Workload:
             self.full.copy_(self.gather.view(self.world, self.M, self.NL).permute(1, 0, 2)
                             .reshape(self.M, self.N))
 
+    def fused_step(self, i: int) -> None:
+        import ctypes
+        lib, L, M, K, NL = self.lib, self._lib, self.M, self.K, self.NL
+        a, packed, scales = self.sets[i]
+        self.ex_calls += 1
+        outs = self.ex_outs[self.ex_calls & 1]
+        st = lib.pk_w4a16_gemm_sharded(
+            a.data_ptr(), L.PK_BF16, K, packed.data_ptr(), scales.data_ptr(), 1.0, 128, M, NL, K,
+            self.out_code, self.N, self.rank * NL, self.world, self.rank, ctypes.addressof(outs),
+            ctypes.addressof(self.ex_flags), L.ptr(self.ex_ws), self.ex_ws_bytes,
+            torch.cuda.current_stream().cuda_stream)
+        L.check(st, self.name + " (fused exchange)")
+
     def step(self, i: int) -> None:
+        if self.exchange is not None:
+            self.fused_step(i)
+            return
         out = self.gemm(i)
         if self.sharded and self.world > 1:
             self.all_gather(out)
@@ -321,7 +351,8 @@ class Workload:
             def fn(i):
                 _, packed, scales = self.sets[i % self.n_sets]
                 a_dev.copy_(a_host, non_blocking=True)
-                y = sharded.sharded_int4_gemm(a_dev, packed, scales, 128, world)
+                y = sharded.sharded_int4_gemm(a_dev, packed, scales, 128, world,
+                                              exchange=self.exchange)
                 y_host.copy_(y, non_blocking=True)
             return fn, M * K * 2, M * N * 4
         a8_host = torch.empty((M, K), dtype=torch.uint8).pin_memory()
@@ -433,6 +464,11 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
         gemm_ms_local = gemm_ms * args.steps / nb
         breakdown = {"gemm_us": round(gemm_ms / nb * 1e3, 3),
                      "allgather_us": round(gath_ms / nb * 1e3, 3), "steps": nb}
+        if work.exchange is not None:
+            breakdown["step"] = ("one kernel per rank: the GEMV stores its columns into every "
+                                 "rank's output over NVLink and ends with a flag barrier; "
+                                 "gemm_us / allgather_us time the unfused local GEMV and an "
+                                 "NCCL all-gather of its output for comparison")
         del g_gemm, g_gath
 
     # end to end through the public API, host buffers in and out every step
@@ -450,6 +486,8 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(dist, e0.elapsed_time(e1))
     del warm, timed  # graphs holding NCCL calls go before the process group
+    if work.exchange is not None:
+        work.exchange.close()  # collective: every rank unmaps its peers
     torch.cuda.synchronize()
 
     if rank != 0:
@@ -494,8 +532,14 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
                        "output": "bf16 (rescaled in the epilogue)",
                        "cast": "excluded from the timed region (gemm_fp8.py:144)"})
     if work.sharded:
-        par = (f"N sharded over {world} GPUs ({work.NL} columns each), NCCL all-gather of the output"
-               if world > 1 else "single GPU (unsharded)")
+        if world == 1:
+            par = "single GPU (unsharded)"
+        elif work.exchange is not None:
+            par = (f"N sharded over {world} GPUs ({work.NL} columns each), output exchanged inside "
+                   "the GEMV (NVLink peer stores + flag barrier)")
+        else:
+            par = f"N sharded over {world} GPUs ({work.NL} columns each), NCCL all-gather of the output"
+    
     else:
         par = f"replicas x{world}" if world > 1 else "single GPU"
     wl_cfg.update({

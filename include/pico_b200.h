@@ -172,12 +172,15 @@ PK_API int pk_ipc_close(void* ptr);
  * where this rank holds columns [n_offset, n_offset + N) (Wp [K, N/2],
  * scales [K/g, N]). The GEMV writes its columns straight into every rank's
  * output buffer peer_out[r] (fp32 or bf16 [M, ldo] with ldo >= N_full, mapped
- * with pk_ipc_open), then its last CTA adds 1 to every peer's 32-bit flag
+ * with pk_ipc_open), then its last CTA adds 1 to every peer's arrival count
  * peer_flag[r] (release, system scope) and waits, at most ~2 s, until its own
- * flag reaches epoch * (world - 1): on return every rank's columns are in
- * peer_out[rank]. All ranks call it in the same order with the same epoch
- * (1, 2, 3, ...); a buffer must not be rewritten by the next call before its
- * reader is done (alternate two buffers). Needs a workspace of
+ * count reaches the next multiple of world - 1: on return every rank's
+ * columns are in peer_out[rank]. Each peer_flag[r] is 8 zero-initialised,
+ * 8-byte aligned bytes in rank r's memory (the count, then rank r's own
+ * expected count, advanced by the kernel, so CUDA graph replays stay in
+ * step). All ranks call it in the same order; a buffer must not be
+ * rewritten by the next call before its reader is done (alternate two
+ * buffers). Needs a workspace of
  * pk_w4a16_workspace_size bytes (at least 64 KB). Covers the GEMV's shapes
  * (M = 1, and M = 2 on slices of 16 MB or more; world <= 8); returns
  * PK_ERR_UNSUPPORTED otherwise, so the caller can exchange with NCCL instead.
@@ -187,7 +190,7 @@ PK_API int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const 
                                  const void* scales, float scalar_scale, int group_size, int64_t M,
                                  int64_t N, int64_t K, int out_dtype, int64_t ldo, int64_t n_offset,
                                  int world, int rank, const uint64_t* peer_out,
-                                 const uint64_t* peer_flag, uint32_t epoch, void* workspace,
+                                 const uint64_t* peer_flag, void* workspace,
                                  size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------- */

@@ -71,8 +71,7 @@ SIGNATURES = {
     "pk_ipc_open": (_int, [_vp, _c.POINTER(_vp)]),
     "pk_ipc_close": (_int, [_vp]),
     "pk_w4a16_gemm_sharded": (_int, [_vp, _int, _i64, _vp, _vp, _f32, _int, _i64, _i64, _i64,
-                                     _int, _i64, _i64, _int, _int, _vp, _vp, _c.c_uint32, _vp,
-                                     _sz, _vp]),
+                                     _int, _i64, _i64, _int, _int, _vp, _vp, _vp, _sz, _vp]),
 }
 
 _lib = None

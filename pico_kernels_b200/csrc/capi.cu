@@ -568,8 +568,8 @@ int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t
                           const void* scales, float scalar_scale, int group_size, int64_t M,
                           int64_t N, int64_t K, int out_dtype, int64_t ldo, int64_t n_offset,
                           int world, int rank, const uint64_t* peer_out,
-                          const uint64_t* peer_flag, uint32_t epoch, void* workspace,
-                          size_t workspace_bytes, void* stream) {
+                          const uint64_t* peer_flag, void* workspace, size_t workspace_bytes,
+                          void* stream) {
   if (!a || !wp || !peer_out || !peer_flag) return fail(PK_ERR_SHAPE, "null pointer");
   if (M <= 0 || N <= 0 || K <= 0 || (N % 2) != 0) return fail(PK_ERR_SHAPE, "bad shape");
   if (world < 1 || world > 8 || rank < 0 || rank >= world)
@@ -588,7 +588,7 @@ int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
     return fail(PK_ERR_ALIGN, "workspace must be 256-byte aligned");
   for (int r = 0; r < world; ++r)
-    if (peer_out[r] == 0 || peer_flag[r] == 0 || (peer_flag[r] & 3) != 0)
+    if (peer_out[r] == 0 || peer_flag[r] == 0 || (peer_flag[r] & 7) != 0)
       return fail(PK_ERR_SHAPE, "peer %d: missing output or misaligned flag", r);
   DecodeArgs p{};
   p.a = a;
@@ -616,7 +616,6 @@ int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t
     sh.peer_out[r] = peer_out[r];
     sh.peer_flag[r] = peer_flag[r];
   }
-  sh.epoch = epoch;
   sh.done = ws_counters(workspace) + (kMaxCounters - 1);
   const char* why = "";
   cudaError_t e = launch_w4a16_gemv(p, as_stream(stream), &why, &sh);

@@ -110,8 +110,7 @@ struct GemvShard {
   int64_t n_offset;
   int world, rank;
   uint64_t peer_out[8];
-  uint64_t peer_flag[8];
-  uint32_t epoch;
+  uint64_t peer_flag[8];  // 8 bytes each: arrival count, then (own only) expected count
   unsigned* done;  // zeroed completion counter (workspace)
 };
 cudaError_t launch_w4a16_gemv(const DecodeArgs& args, cudaStream_t s, const char** why,

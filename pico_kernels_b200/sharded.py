@@ -122,7 +122,7 @@ class PeerExchange:
             hbuf = ctypes.create_string_buffer(h, 64)
             _lib.check(self.lib.pk_ipc_open(ctypes.addressof(hbuf), ctypes.byref(peer)), "IPC open")
             self.bases.append(peer.value)
-        self.epoch = 0
+        self.calls = 0  # selects the buffer: calls alternate between the two
         self.device = torch.device("cuda", torch.cuda.current_device())
 
     def output(self, parity: int, m: int) -> torch.Tensor:
@@ -145,8 +145,8 @@ class PeerExchange:
             return None
         ws_bytes = max(self.lib.pk_w4a16_workspace_size(M, n_local, K, 0), 1 << 16)
         ws = _lib.workspace(a.device, ws_bytes, tag="sharded")
-        self.epoch += 1
-        parity = self.epoch & 1
+        self.calls += 1
+        parity = self.calls & 1
         outs = (ctypes.c_uint64 * self.world)(*[b + parity * self.buf_bytes for b in self.bases])
         flags = (ctypes.c_uint64 * self.world)(*[b + self.flag_off for b in self.bases])
         outs_p, flags_p = ctypes.addressof(outs), ctypes.addressof(flags)
@@ -154,10 +154,10 @@ class PeerExchange:
         rc = self.lib.pk_w4a16_gemm_sharded(
             a.data_ptr(), _lib.dtype_code(a.dtype), a.stride(0), packed_shard.data_ptr(),
             scales.data_ptr(), 1.0, group_size, M, n_local, K, _lib.dtype_code(self.dtype),
-            self.n_full, self.rank * n_local, self.world, self.rank, outs_p, flags_p, self.epoch,
+            self.n_full, self.rank * n_local, self.world, self.rank, outs_p, flags_p,
             ws.data_ptr(), ws.numel(), _lib.stream_of(a))
         if rc == _lib.PK_ERR_UNSUPPORTED:
-            self.epoch -= 1
+            self.calls -= 1
             return None
         _lib.check(rc, "sharded int4_gemm")
         return self.output(parity, M)
