@@ -11,19 +11,16 @@
 //
 //  * Units. The weights are cut into units of 256 rows x 256 columns (256 x
 //    128 packed bytes, 32 KB); a "slice" is a 256-column strip, KB units tall.
-//  * Work split, two modes chosen on the host:
-//    - cluster mode (small layers): a thread-block cluster of C CTAs (C a
-//      power of two <= 8) per slice, each CTA a contiguous run of the slice's
-//      units; the C partial columns are summed through distributed shared
-//      memory in rank order. No workspace, no atomics.
-//    - stream-K mode (large layers): units numbered slice-major, CTA c of G
-//      (two per SM when the CTA fits twice) takes [U*c/G, U*(c+1)/G). A
-//      CTA's range covers parts of a few slices ("segments"). A segment that
-//      is a whole slice is stored directly; otherwise the CTA writes its
-//      partial to the workspace (slot c + slice, unique per segment) and bumps
-//      the slice's arrival counter with an acq_rel atomic; the last arriver
-//      sums the slice's partials in CTA order, stores, and re-arms the counter.
-//    Both modes sum in a fixed order: results are deterministic per shape.
+//  * Work split (stream-K): units numbered slice-major, CTA c of G (two per
+//    SM) takes [U*c/G, U*(c+1)/G). A CTA's range covers parts of a few slices
+//    ("segments"). A segment that is a whole slice is stored directly;
+//    otherwise the CTA writes its partial to the workspace (slot c + slice,
+//    unique per segment) and bumps the slice's arrival counter with an
+//    acq_rel atomic; the last arriver sums the slice's partials in CTA order,
+//    stores, and re-arms the counter. Fixed summation order: deterministic
+//    for a given SM count. (A variant with one 8-CTA cluster per slice and a
+//    distributed-shared-memory reduction measured slower even at 4096^2:
+//    8.1 vs 7.6 us, half the CTAs per SM.)
 //  * Pipeline. Warp 8 (one thread) is the TMA producer: per unit one 2D box
 //    of weights, the unit's group-scale rows and the activation tile
 //    A[0:M, k0:k0+256] into a ring of shared-memory slots, completing one
@@ -69,15 +66,13 @@ constexpr int kProducerWarp = kWarps;
 constexpr int kThreads = (kWarps + 1) * 32;
 constexpr int kRowsPerWarp = kRows / kWarps;  // 32: one row per lane for the activations
 constexpr int kMaxM = 2;
-constexpr int kMaxCluster = 8;
 constexpr int kMaxScaleRows = 4;        // scale rows a unit can touch (group >= 64)
 constexpr int kSmemTwoPerSm = 115712;   // per-CTA limit for two resident CTAs (228 KB SM)
 
 template <int M>
 struct GemvCfg {
   // M = 1: three slots and ~113 KB; M = 2: two slots. Either way two CTAs
-  // share an SM (a stream-K grid's pair, or this grid and the next under
-  // programmatic launch).
+  // of the grid share an SM.
   static constexpr int kStages = M == 1 ? 3 : 2;
   static constexpr int kWBytes = kRows * kRowBytes;          // 32768
   static constexpr int kSBytes = kMaxScaleRows * kCols * 2;  // 2048
@@ -177,7 +172,6 @@ struct GemvParams {
   int N, K, group;
   int group_shift;     // log2(group) when group is a power of two, else -1
   int scale_rows;      // group-scale rows per unit in the scale box
-  int cluster;         // 0: stream-K; else CTAs per slice (cluster size)
   float scalar_scale;
   int out_dtype;
   int64_t ldo;
@@ -213,7 +207,7 @@ __device__ __forceinline__ void sharded_finish(const GemvParams& p, bool stored)
   const bool any = __syncthreads_or(stored) != 0;
   if (threadIdx.x != 0) return;
   if (any) __threadfence_system();
-  const unsigned total = gridDim.x * gridDim.y;
+  const unsigned total = gridDim.x;
   unsigned prev;
   asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p.done) : "memory");
   if (prev != total - 1) return;
@@ -266,18 +260,10 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
   const int NS = (p.N + kCols - 1) / kCols;
   const int KB = (p.K + kRows - 1) / kRows;
   const int64_t U = static_cast<int64_t>(NS) * KB;
-  const bool clustered = p.cluster > 0;
   const int64_t G = gridDim.x;
-  const int64_t cta = blockIdx.x;  // stream-K: CTA index; cluster mode: rank in the cluster
-  int64_t u0, u1;
-  if (clustered) {
-    const int64_t s = blockIdx.y;
-    u0 = s * KB + static_cast<int64_t>(KB) * cta / p.cluster;
-    u1 = s * KB + static_cast<int64_t>(KB) * (cta + 1) / p.cluster;
-  } else {
-    u0 = U * cta / G;
-    u1 = U * (cta + 1) / G;
-  }
+  const int64_t cta = blockIdx.x;
+  const int64_t u0 = U * cta / G;
+  const int64_t u1 = U * (cta + 1) / G;
   const int n_units = static_cast<int>(u1 - u0);
   bool stored = false;  // this thread wrote output (sharded exchange: fence before arriving)
 
@@ -462,13 +448,6 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
         v[m] = s;
         named_bar_sync(1, kWarps * 32);
       }
-      if (clustered) {
-        // stage the CTA's partial for the cluster reduction (thread t alone
-        // writes column t of each row)
-#pragma unroll
-        for (int m = 0; m < M; ++m) red[m * kCols + t] = v[m];
-        break;  // a cluster CTA owns exactly one segment
-      }
       const int64_t col = static_cast<int64_t>(slice) * kCols + t;
       auto store = [&](const float* vals) {
         if (col >= p.N) return;
@@ -509,32 +488,6 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
     }
   }
 
-  if (clustered) {
-    // Cluster reduction: rank r sums columns [r*per, (r+1)*per) of the C
-    // staged partials in rank order. Every thread of every CTA takes part in
-    // both cluster barriers; the second keeps each CTA's shared memory alive
-    // until its peers have read it.
-    cluster_sync();
-    if (warp < kWarps) {
-      const int cs = p.cluster;
-      const int per = kCols / cs;
-      const int64_t slice = blockIdx.y;
-      const uint32_t red_addr = smem_u32(red);
-      for (int e = threadIdx.x; e < M * per; e += kWarps * 32) {
-        const int m = e / per;
-        const int c = static_cast<int>(cta) * per + e % per;
-        float s = 0.0f;
-        for (int r = 0; r < cs; ++r)
-          s += ld_cluster_f32(cluster_map(red_addr + (m * kCols + c) * 4, static_cast<uint32_t>(r)));
-        const int64_t col = slice * kCols + c;
-        if (col < p.N) {
-          store_col(p, m, col, s);
-          stored = true;
-        }
-      }
-    }
-    cluster_sync();
-  }
   if (p.world > 1) sharded_finish(p, stored);
 }
 
@@ -542,33 +495,11 @@ CUtensorMapDataType tmap_type16(int dt) {
   return dt == PK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 }
 
-// How a call is split over the GPU.
-struct GemvPlan {
-  int cluster;     // > 0: cluster mode with this many CTAs per slice; 0: stream-K
-  int64_t grid_x;  // cluster mode: cluster size; stream-K: CTAs
-  int64_t grid_y;  // cluster mode: slices; stream-K: 1
-};
-
-GemvPlan make_plan(int64_t M, int64_t N, int64_t K) {
-  const int64_t NS = (N + kCols - 1) / kCols;
-  const int64_t KB = (K + kRows - 1) / kRows;
-  const int64_t U = NS * KB;
-  const int64_t sms = num_sms();
-  GemvPlan pl{};
-  if (U <= 4 * sms && NS <= sms) {
-    // small layer: a cluster per slice, the slice's units split between its CTAs
-    int c = 1;
-    while (c * 2 <= kMaxCluster && NS * c * 2 <= sms && c * 2 <= KB) c *= 2;
-    pl.cluster = c;
-    pl.grid_x = c;
-    pl.grid_y = NS;
-  } else {
-    const int64_t cap = 2 * sms;
-    pl.cluster = 0;
-    pl.grid_x = U < cap ? U : cap;
-    pl.grid_y = 1;
-  }
-  return pl;
+// Stream-K grid: two CTAs per SM, at most one CTA per unit.
+int64_t gemv_grid(int64_t N, int64_t K) {
+  const int64_t U = ((N + kCols - 1) / kCols) * ((K + kRows - 1) / kRows);
+  const int64_t cap = 2 * static_cast<int64_t>(num_sms());
+  return U < cap ? U : cap;
 }
 
 int scale_rows_for(int group) {
@@ -604,12 +535,10 @@ bool gemv_supported(int64_t M, int64_t N, int64_t K, int group, const void* scal
 }
 
 size_t gemv_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-  const GemvPlan pl = make_plan(M, N, K);
-  if (pl.cluster > 0) return 0;
   const int64_t NS = (N + kCols - 1) / kCols;
   const int64_t KB = (K + kRows - 1) / kRows;
   const int64_t U = NS * KB;
-  const int64_t G = pl.grid_x;
+  const int64_t G = gemv_grid(N, K);
   bool split = false;
   for (int64_t j = 0; j < NS && !split; ++j)
     split = unit_owner(j * KB, U, G) != unit_owner(j * KB + KB - 1, U, G);
@@ -668,10 +597,8 @@ cudaError_t launch_w4a16_gemv(const DecodeArgs& a, cudaStream_t s, const char** 
   } else {
     std::memcpy(&tmS, &tmW, sizeof(tmS));  // unused
   }
-  const GemvPlan pl = make_plan(a.M, a.N, a.K);
-  p.cluster = pl.cluster;
-  if (pl.cluster == 0 && gemv_workspace_bytes(a.M, a.N, a.K) > 0 &&
-      (a.partials == nullptr || a.sems == nullptr)) {
+  const int64_t G = gemv_grid(a.N, a.K);
+  if (gemv_workspace_bytes(a.M, a.N, a.K) > 0 && (a.partials == nullptr || a.sems == nullptr)) {
     *why = "the split-K GEMV needs a workspace";
     return cudaErrorInvalidValue;
   }
@@ -682,24 +609,15 @@ cudaError_t launch_w4a16_gemv(const DecodeArgs& a, cudaStream_t s, const char** 
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(pl.grid_x), static_cast<unsigned>(pl.grid_y), 1);
+    cfg.gridDim = dim3(static_cast<unsigned>(G), 1, 1);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem_bytes;
     cfg.stream = s;
-    cudaLaunchAttribute attrs[2];
-    int na = 0;
-    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attrs[na].val.programmaticStreamSerializationAllowed = 1;
-    ++na;
-    if (pl.cluster > 1) {
-      attrs[na].id = cudaLaunchAttributeClusterDimension;
-      attrs[na].val.clusterDim.x = pl.cluster;
-      attrs[na].val.clusterDim.y = 1;
-      attrs[na].val.clusterDim.z = 1;
-      ++na;
-    }
-    cfg.attrs = attrs;
-    cfg.numAttrs = na;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, tmW, tmA, tmS, p, dc);
   };
   auto by_m = [&](auto tag, auto grouped_tag) -> cudaError_t {

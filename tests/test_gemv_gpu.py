@@ -52,13 +52,13 @@ def test_gemv_decode(M, N, dt):
 @pytest.mark.parametrize("M,N,K,group", [
     (1, 4128, 4096, 128),    # last 256-column slice ragged (32 columns)
     (1, 1024, 4160, 64),     # K not a multiple of 128, group 64 (four scale rows per unit)
-    (2, 8192, 4160, 64),     # M = 2, cluster mode
+    (2, 8192, 4160, 64),     # M = 2
     (1, 2048, 4100, 128),    # K not a multiple of the 256-row unit
     (1, 512, 8192, 256),     # group 256
     (1, 1024, 4224, 192),    # groups straddle the 256-row units
     (1, 256, 163840, 128),   # stream-K: one slice split over every CTA (fan-in ~300)
     (2, 65536, 512, 128),    # stream-K, M = 2: CTA ranges span several slices
-    (1, 8192, 256, 64),      # one unit per slice: clusters of one CTA, no reduction
+    (1, 8192, 256, 64),      # one unit per slice: every segment a whole slice, no reduction
 ])
 def test_gemv_shapes(M, N, K, group):
     a, packed, scales, ref = make_case(M, N, K, group=group, seed=N + K)
