@@ -8,10 +8,13 @@
 // overlaps the main loop of the next.
 //
 // Used by three entry points:
-//   * fp8 (e4m3 x e4m3, kind::f8f6f4, K = 32 per MMA), 128 x 256 tiles,
-//     epilogue x out_scale -- gemm_fp8.fp8_gemm_kernel (gemm_fp8.py:38-86);
-//   * dense fp16/bf16 (kind::f16), 128 x 256 tiles, optional deterministic
-//     split-K -- gemm_splitk.gemm_splitk_kernel (gemm_splitk.py:26-64);
+//   * fp8 (e4m3 x e4m3, kind::f8f6f4, K = 32 per MMA), epilogue x out_scale
+//     -- gemm_fp8.fp8_gemm_kernel (gemm_fp8.py:38-86);
+//   * dense fp16/bf16 (kind::f16), optional deterministic split-K --
+//     gemm_splitk.gemm_splitk_kernel (gemm_splitk.py:26-64);
+//     both on 256 x 256 tiles computed by a CTA pair (gemm_pair_kernel,
+//     cta_group::2) when the tiles make more than one wave, else (and for
+//     split-K) on one-CTA 128 x 256 tiles;
 //   * W4A16 prefill: 128 x 256 tiles; B is produced in shared memory by
 //     dequant warps from the packed int4 weights and group scales (q * s
 //     rounded to A's dtype) -- gemm_int4.int4_gemm_kernel (gemm_int4.py:21-55).
@@ -122,6 +125,45 @@ __device__ __forceinline__ void store8(void* out, int out_dtype, int64_t idx, co
       reinterpret_cast<float4*>(o)[1] = make_float4(v[4], v[5], v[6], v[7]);
     } else {
       for (int i = 0; i < valid; ++i) o[i] = v[i];
+    }
+  }
+}
+
+// Sum `parts` fp32 partial rows of kBN columns (`stride` floats apart) in part
+// order starting from zero, scale, and store the valid columns of output row
+// `out_row`. 64 columns at a time, with all 16 loads of a part in flight: a
+// loop of one 8-column load per step would pay an L2 round trip per step.
+template <int kBN>
+__device__ __forceinline__ void sum_parts_row(const float* base, int64_t stride, int parts,
+                                              float scale, void* out, int out_dtype,
+                                              int64_t out_row, int col0, int N) {
+#pragma unroll 1
+  for (int c0 = 0; c0 < kBN; c0 += 64) {
+    if (col0 + c0 >= N) break;
+    float v[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = 0.0f;
+#pragma unroll 1
+    for (int j = 0; j < parts; ++j) {
+      const float4* src = reinterpret_cast<const float4*>(base + j * stride + c0);
+      float4 x[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[i] = __ldcg(src + i);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        v[4 * i] += x[i].x;
+        v[4 * i + 1] += x[i].y;
+        v[4 * i + 2] += x[i].z;
+        v[4 * i + 3] += x[i].w;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 64; i += 8) {
+      float w[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) w[e] = v[i + e] * scale;
+      const int col = col0 + c0 + i;
+      if (col < N) store8(out, out_dtype, out_row + col, w, col + 8 <= N, min(8, N - col));
     }
   }
 }
@@ -331,22 +373,9 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
             const int64_t row = static_cast<int64_t>(tm) * BM + row_in_tile;
             const float* base = p.partials + static_cast<int64_t>(tile_id) * p.split * (BM * BN) +
                                 row_in_tile * BN;
-#pragma unroll 1
-            for (int c = 0; c < BN / 8 && row < p.M; ++c) {
-              float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-              for (int j = 0; j < p.split; ++j) {
-                const float4 x0 = __ldcg(reinterpret_cast<const float4*>(base + j * (BM * BN) + c * 8));
-                const float4 x1 =
-                    __ldcg(reinterpret_cast<const float4*>(base + j * (BM * BN) + c * 8 + 4));
-                v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
-                v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
-              }
-#pragma unroll
-              for (int e = 0; e < 8; ++e) v[e] *= p.out_scale;
-              const int col = col0 + c * 8;
-              if (col < p.N)
-                store8(p.out, p.out_dtype, row * p.ldc + col, v, col + 8 <= p.N, min(8, p.N - col));
-            }
+            if (row < p.M)
+              sum_parts_row<BN>(base, BM * BN, p.split, p.out_scale, p.out, p.out_dtype,
+                                row * p.ldc, col0, p.N);
           }
           named_bar_sync(1, kEpiWarps * 32);
           if (tid == kEpiWarp0 * 32) p.sems[tile_id] = 0u;  // re-arm
@@ -453,6 +482,196 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
   if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
 }
 
+// ---------------------------------------------------------------------------
+// Pair tiles (dense fp16/bf16 and fp8, no split): a cluster of two CTAs
+// computes a 256 x 256 tile with cta_group::2 MMAs (M = 256, N = 256). CTA r
+// stages rows [128 r, 128 r + 128) of the A tile and columns
+// [128 r, 128 r + 128) of the B tile; the MMA issued by CTA 0 reads both
+// halves and writes rows 128 r .. of D into CTA r's TMEM. Per SM and k-step
+// that is 32 KB of operands for the FLOPs a one-CTA 128 x 256 tile needs
+// 48 KB for, and the smaller stages allow a deeper ring.
+//
+// Both CTAs' TMA loads signal CTA 0's `full` barrier (CTA 0 expects the bytes
+// of both halves); the MMA completion is multicast to the `empty` and
+// `acc_full` barriers of both CTAs; both CTAs' epilogue warps arrive on CTA
+// 0's `acc_empty`.
+// ---------------------------------------------------------------------------
+template <int kKind>
+struct PairCfg {
+  static constexpr int kElem = kKind == kF16 ? 2 : 1;
+  static constexpr int kBK = 128 / kElem;
+  static constexpr int kMmaK = kKind == kF16 ? 16 : 32;
+  static constexpr int kKSteps = kBK / kMmaK;
+  static constexpr int kBM = 256, kBN = 256;            // pair tile
+  static constexpr int kHalfM = 128, kHalfN = 128;      // per CTA
+  static constexpr int kATile = kHalfM * 128;           // 16 KB
+  static constexpr int kBTile = kBK * kHalfN * kElem;   // 16 KB
+  static constexpr int kBAtomN = 128 / kElem;
+  static constexpr int kBBoxes = kHalfN / kBAtomN;      // 2 (16-bit) / 1 (fp8)
+  static constexpr int kBLBO = kBK * 128;
+  static constexpr int kBStepBytes = (kMmaK / 8) * 1024;
+  static constexpr int kStages = 6;
+  static constexpr int kStageBytes = kATile + kBTile;
+  static constexpr int kBarOff = kStages * kStageBytes;
+  static constexpr int kSmem = kBarOff + 256 + 1024;
+  static constexpr int kThreads = kDeqWarp0 * 32;       // TMA, MMA, 4 epilogue warps
+  static constexpr int kAccCols = kBN;
+  static constexpr uint32_t kIdesc = make_idesc(kKind == kF16 ? 1u : 0u, false, true, 256, kBN);
+  static constexpr uint32_t kIdescF16 = make_idesc(0u, false, true, 256, kBN);
+  static_assert(2 * kAccCols <= 512, "two accumulator sets fit TMEM");
+  static_assert(kSmem <= 227 * 1024, "shared memory");
+};
+
+template <int kKind>
+__global__ void __launch_bounds__(PairCfg<kKind>::kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB, const Params p) {
+  using C = PairCfg<kKind>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int k_tiles = (p.K + C::kBK - 1) / C::kBK;
+  const int num_units = p.num_m * p.num_n;
+
+  if (warp == kTmaWarp && lane == 0) {
+    for (int i = 0; i < C::kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 2 * kEpiWarps);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == kMmaWarp) tmem_alloc_pair(tmem_holder, 512);
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers exist before either signals the other
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  griddep_wait();
+
+  bool fail = false;
+  if (warp == kTmaWarp) {
+    // ------------------------------- producer -------------------------------
+    if (lane == 0) {
+      const uint32_t full0 = cluster_map(smem_u32(&full[0]), 0);
+      int it = 0;
+      for (int u = pair; u < num_units && !fail; u += npairs) {
+        int tm, tn, ks;
+        tile_coords(u, p, tm, tn, ks);
+        const int row = tm * C::kBM + static_cast<int>(rank) * C::kHalfM;
+        const int col = tn * C::kBN + static_cast<int>(rank) * C::kHalfN;
+        for (int kt = 0; kt < k_tiles && !fail; ++kt, ++it) {
+          const int st = it % C::kStages;
+          if (it >= C::kStages)
+            fail = !mbar_wait(&empty[st], ((it / C::kStages) - 1) & 1, p.status, kSiteGemmProducer);
+          if (fail) break;
+          uint8_t* base = smem + st * C::kStageBytes;
+          const uint32_t bar = full0 + st * 8;
+          if (rank == 0) mbar_arrive_expect_tx(&full[st], 2 * C::kStageBytes);
+          const int k0 = kt * C::kBK;
+          tma_load_2d_pair(base, &tmA, bar, k0, row);
+#pragma unroll
+          for (int b = 0; b < C::kBBoxes; ++b)
+            tma_load_2d_pair(base + C::kATile + b * C::kBLBO, &tmB, bar, col + b * C::kBAtomN, k0);
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ----------------------- MMA issuer (CTA 0 only) ------------------------
+    if (rank == 0 && lane == 0) {
+      int it = 0, local = 0;
+      for (int u = pair; u < num_units && !fail; u += npairs, ++local) {
+        const int ab = local & 1;
+        if (local >= 2)
+          fail = !mbar_wait_cluster(&acc_empty[ab], ((local >> 1) - 1) & 1, p.status, kSiteGemmMma);
+        if (fail) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + ab * C::kAccCols;
+        for (int kt = 0; kt < k_tiles && !fail; ++kt, ++it) {
+          const int st = it % C::kStages;
+          fail = !mbar_wait(&full[st], (it / C::kStages) & 1, p.status, kSiteGemmMma);
+          if (fail) break;
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + st * C::kStageBytes);
+          const uint32_t b_base = a_base + C::kATile;
+#pragma unroll
+          for (int s = 0; s < C::kKSteps; ++s) {
+            const uint64_t ad = make_smem_desc(a_base + s * 32, 16, 1024);
+            const uint64_t bd = make_smem_desc(b_base + s * C::kBStepBytes, C::kBLBO, 1024);
+            const uint32_t acc = (kt > 0 || s > 0) ? 1u : 0u;
+            if (kKind == kF8)
+              umma_f8_pair(d_tmem, ad, bd, C::kIdesc, acc);
+            else if (p.a_is_f16)
+              umma_f16_pair(d_tmem, ad, bd, C::kIdescF16, acc);
+            else
+              umma_f16_pair(d_tmem, ad, bd, C::kIdesc, acc);
+          }
+          umma_commit_pair(&empty[st]);
+        }
+        if (fail) break;
+        umma_commit_pair(&acc_full[ab]);
+      }
+    }
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kEpiWarps) {
+    // ----------------------- epilogue (both CTAs) ---------------------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const uint32_t acc_empty0 = cluster_map(smem_u32(&acc_empty[0]), 0);
+    int local = 0;
+    for (int u = pair; u < num_units && !fail; u += npairs, ++local) {
+      int tm, tn, ks;
+      tile_coords(u, p, tm, tn, ks);
+      const int ab = local & 1;
+      fail = !mbar_wait(&acc_full[ab], (local >> 1) & 1, p.status, kSiteGemmEpilogue);
+      if (fail) break;
+      tc_fence_after();
+      const int64_t row =
+          static_cast<int64_t>(tm) * C::kBM + static_cast<int>(rank) * C::kHalfM + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + ab * C::kAccCols;
+      const int col0 = tn * C::kBN;
+#pragma unroll 1
+      for (int c = 0; c < C::kBN / 32; ++c) {
+        uint32_t raw[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, raw);
+        tmem_ld_wait();
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(raw[i + e]) * p.out_scale;
+            const int col = col0 + c * 32 + i;
+            if (col < p.N)
+              store8(p.out, p.out_dtype, row * p.ldc + col, v, col + 8 <= p.N, min(8, p.N - col));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty0 + ab * 8);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the other may still touch its memory
+  tc_fence_after();
+  if (warp == kMmaWarp) tmem_dealloc_pair(tmem, 512);
+}
+
 CUtensorMapDataType elem_tmap(int dt) {
   switch (dt) {
     case PK_BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -514,6 +733,83 @@ cudaError_t launch_typed(const GemmArgs& g, cudaStream_t s, const char** why) {
   return cudaGetLastError();
 }
 
+// Pairs of CTAs that can be resident at once for the pair kernel (one CTA per
+// SM): the persistent grid is twice this, capped by the tile count.
+template <int kKind>
+int pair_slots(cudaStream_t s) {
+  static int cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return num_sms() / 2;
+  if (cached[dev] > 0) return cached[dev];
+  using C = PairCfg<kKind>;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.gridDim = dim3(num_sms(), 1, 1);
+  cfg.blockDim = dim3(C::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = s;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<kKind>, &cfg) != cudaSuccess ||
+      clusters <= 0) {
+    cudaGetLastError();
+    clusters = num_sms() / 2;
+  }
+  cached[dev] = clusters;
+  return clusters;
+}
+
+template <int kKind>
+cudaError_t launch_pair(const GemmArgs& g, cudaStream_t s, const char** why) {
+  using C = PairCfg<kKind>;
+  CUtensorMap tmA, tmB;
+  if (!encode_tmap_2d(&tmA, elem_tmap(g.a_dtype), g.a, g.K, g.M, g.lda * C::kElem, C::kBK,
+                      C::kHalfM, CU_TENSOR_MAP_SWIZZLE_128B, why))
+    return cudaErrorInvalidValue;
+  if (!encode_tmap_2d(&tmB, elem_tmap(g.a_dtype), g.b, g.N, g.K, g.ldb * C::kElem, C::kBAtomN,
+                      C::kBK, CU_TENSOR_MAP_SWIZZLE_128B, why))
+    return cudaErrorInvalidValue;
+  Params p{};
+  p.M = static_cast<int>(g.M);
+  p.N = static_cast<int>(g.N);
+  p.K = static_cast<int>(g.K);
+  p.split = 1;
+  p.num_m = static_cast<int>((g.M + C::kBM - 1) / C::kBM);
+  p.num_n = static_cast<int>((g.N + C::kBN - 1) / C::kBN);
+  p.out_dtype = g.out_dtype;
+  p.ldc = g.ldc;
+  p.out_scale = g.out_scale;
+  p.out = g.out;
+  p.group = 1;
+  p.a_is_f16 = g.a_dtype == PK_F16;
+  p.status = g.status;
+  auto kernel = gemm_pair_kernel<kKind>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  if (e != cudaSuccess) return e;
+  const int units = p.num_m * p.num_n;
+  const int slots = pair_slots<kKind>(s);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attrs[2];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = 2;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(2 * (units < slots ? units : slots), 1, 1);
+  cfg.blockDim = dim3(C::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = s;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, p);
+}
+
 // dense split-K tiles (the only configuration that uses the workspace)
 using DenseCfg = Cfg<kF16, false>;
 
@@ -531,6 +827,16 @@ size_t gemm_splitk_workspace_bytes(int64_t M, int64_t N, int split) {
 }
 
 cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t s, const char** why) {
+  // Pair tiles for dense / fp8 products without split-K that have rows for both
+  // halves of a pair, unless the pair tiles make at most one wave: then
+  // one-CTA tiles keep at least as many SMs busy and start sooner (fp8
+  // 2048^3: 14.7 us on one-CTA tiles, 15.7 us on pairs).
+  if (g.kind != GemmArgs::kW4A16 && g.split <= 1 && g.M > 128) {
+    const bool f8 = g.kind == GemmArgs::kFp8;
+    const int64_t tiles = ((g.M + 255) / 256) * ((g.N + 255) / 256);
+    if (tiles > (f8 ? pair_slots<kF8>(s) : pair_slots<kF16>(s)))
+      return f8 ? launch_pair<kF8>(g, s, why) : launch_pair<kF16>(g, s, why);
+  }
   if (g.kind == GemmArgs::kFp8) return launch_typed<kF8, false>(g, s, why);
   if (g.kind == GemmArgs::kW4A16) return launch_typed<kF16, true>(g, s, why);
   return launch_typed<kF16, false>(g, s, why);

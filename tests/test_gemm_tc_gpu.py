@@ -131,6 +131,43 @@ def test_dense_gemm_matches_torch(shape):
         assert torch.allclose(c, a.float() @ b.float(), atol=1e-2, rtol=1e-2)
 
 
+# ---------------------------------------------------------- CTA-pair tiles
+@pytest.mark.parametrize("M,N,K", [
+    (4096, 4096, 4096),   # 256 pair tiles over the resident pairs: 3.5 waves
+    (3000, 2000, 1040),   # ragged M and N edges inside pair tiles (96 tiles)
+    (2048, 2048, 2048),   # one wave of pair tiles: one-CTA tiles instead
+])
+def test_fp8_pair_tiles(M, N, K):
+    """fp8 on 256 x 256 CTA-pair tiles (cta_group::2) matches the exact
+    product (e4m3 products are exact in fp32: only summation order differs)
+    and is bitwise reproducible."""
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    a8, sa = gemm_fp8.quantize(torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16))
+    b8, sb = gemm_fp8.quantize(torch.randn(K, N, device="cuda", generator=g).to(torch.bfloat16))
+    y = gemm_fp8.fp8_gemm_precast(a8, sa, b8, sb)
+    assert torch.equal(y, gemm_fp8.fp8_gemm_precast(a8, sa, b8, sb))
+    ref = (a8.float() @ b8.float()) / (sa * sb)
+    assert (torch.norm(y - ref) / torch.norm(ref)).item() < 1e-5
+    yb = gemm_fp8.fp8_gemm_precast(a8, sa, b8, sb, out_dtype=torch.bfloat16)
+    assert torch.equal(yb, y.to(torch.bfloat16))
+    assert pk.device_status() == (0, 0)
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 4096), (3000, 2000, 1000), (200, 4104, 264)])
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_dense_pair_tiles(M, N, K, dt):
+    """Dense 16-bit GEMM on CTA-pair tiles (and, for the last shape, one wave
+    of one-CTA tiles) against the fp32 product: bf16/fp16 products are exact
+    in fp32, so only summation order differs."""
+    torch.manual_seed(M + K)
+    a = torch.randn(M, K, device="cuda", dtype=dt)
+    b = torch.randn(K, N, device="cuda", dtype=dt)
+    c = gemm_splitk.triton_gemm(a, b)
+    ref = a.float() @ b.float()
+    assert (torch.norm(c - ref) / torch.norm(ref)).item() < 1e-5
+    assert torch.equal(c, gemm_splitk.triton_gemm(a, b))
+
+
 # ------------------------------------------------------------ W4A16 prefill
 def _w4a16_case(M, N, K, seed=0, dt=torch.bfloat16):
     g = torch.Generator().manual_seed(seed)
