@@ -50,6 +50,10 @@ WORKLOADS = {
     "fp8_2048": dict(kind="fp8", M=2048, N=2048, K=2048),
     "fp8_4096": dict(kind="fp8", M=4096, N=4096, K=4096),
     "fp8_8192": dict(kind="fp8", M=8192, N=8192, K=8192),
+    # dense bf16 GEMM, fp32 out (gemm.py:103, the comparison partner of the
+    # split-K kernel): metric TFLOP/s
+    "dense_bf16_4096": dict(kind="dense", M=4096, N=4096, K=4096),
+    "dense_bf16_8192": dict(kind="dense", M=8192, N=8192, K=8192),
     # Llama-70B MLP layers sharded along N over the ranks, output all-gathered
     # with NCCL; strong scaling: the layer is fixed, ranks split it
     "llama70b_up_m1": dict(kind="w4a16", M=1, N=28672, K=8192, sharded=True),
@@ -223,6 +227,8 @@ class Workload:
         n0 = self.rank * self.NL
         if self.kind == "w4a16":
             per_set = K * self.NL // 2 + (K // 128) * self.NL * 2 + M * K * 2
+        elif self.kind == "dense":
+            per_set = (M * K + K * self.NL) * 2
         else:
             per_set = M * K + K * self.NL
         self.n_sets = max(2, int(2 * L2_BYTES // per_set) + 1)
@@ -241,6 +247,10 @@ class Workload:
                     scales = scales[:, n0:n0 + self.NL].contiguous()
                 a = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
                 self.sets.append((a, packed, scales))
+            elif self.kind == "dense":
+                a = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
+                b = torch.randn(K, N, device=device, generator=g).to(torch.bfloat16)
+                self.sets.append((a, b))
             else:
                 a8, sa = gemm_fp8.quantize(torch.randn(M, K, device=device, generator=g).to(torch.bfloat16))
                 b8, sb = gemm_fp8.quantize(torch.randn(K, N, device=device, generator=g).to(torch.bfloat16))
@@ -249,8 +259,8 @@ class Workload:
                 self.sets.append((a8, b8, 1.0 / (sa * sb)))
         torch.cuda.empty_cache()
         # fp8 layers write bf16 (configs[3]: "bf16 output rescaled in the epilogue")
-        self.out_dtype = torch.float32 if self.kind == "w4a16" else torch.bfloat16
-        self.out_code = _lib.PK_F32 if self.kind == "w4a16" else _lib.PK_BF16
+        self.out_dtype = torch.bfloat16 if self.kind == "fp8" else torch.float32
+        self.out_code = _lib.PK_BF16 if self.kind == "fp8" else _lib.PK_F32
         # decode outputs are tiny: one per set; large outputs share one buffer
         n_out = self.n_sets if self.hbm else 1
         self.outs = [torch.empty((M, self.NL), dtype=self.out_dtype, device=device)
@@ -286,6 +296,10 @@ class Workload:
             st = lib.pk_w4a16_gemm(a.data_ptr(), L.PK_BF16, K, packed.data_ptr(), scales.data_ptr(),
                                    1.0, 128, M, NL, K, out.data_ptr(), self.out_code, NL,
                                    self.split_k, L.ptr(self.ws), self.ws_bytes, stream)
+        elif self.kind == "dense":
+            a, b = self.sets[i]
+            st = lib.pk_gemm_splitk(a.data_ptr(), b.data_ptr(), L.PK_BF16, M, NL, K, 1,
+                                    out.data_ptr(), None, 0, stream)
         else:
             a8, b8, out_scale = self.sets[i]
             st = lib.pk_fp8_gemm(a8.data_ptr(), b8.data_ptr(), M, NL, K, out_scale, out.data_ptr(),
@@ -331,6 +345,8 @@ class Workload:
         M, N, K = self.M, self.N, self.K
         if self.kind == "w4a16":
             return K * N // 2 + (K // 128) * N * 2 + M * K * 2 + M * N * 4
+        if self.kind == "dense":
+            return (M * K + K * N) * 2 + M * N * 4
         return M * K + K * N + M * N * 2
 
     def flops_per_step(self) -> int:
@@ -354,6 +370,17 @@ class Workload:
                 y = sharded.sharded_int4_gemm(a_dev, packed, scales, 128, world,
                                               exchange=self.exchange)
                 y_host.copy_(y, non_blocking=True)
+            return fn, M * K * 2, M * N * 4
+        if self.kind == "dense":
+            from pico_kernels_b200 import gemm
+            a_host = torch.empty((M, K), dtype=torch.bfloat16).pin_memory()
+            a_host.copy_(self.sets[0][0])
+            a_dev = torch.empty((M, K), dtype=torch.bfloat16, device=self.device)
+
+            def fn(i):
+                _, b = self.sets[i % self.n_sets]
+                a_dev.copy_(a_host, non_blocking=True)
+                y_host.copy_(gemm.triton_gemm(a_dev, b), non_blocking=True)
             return fn, M * K * 2, M * N * 4
         a8_host = torch.empty((M, K), dtype=torch.uint8).pin_memory()
         a8_host.copy_(self.sets[0][0].view(torch.uint8))
@@ -527,6 +554,8 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
         wl_cfg.update({"group_size": 128, "weights": "int4 packed [K, N/2] + bf16 scales [K/128, N]",
                        "activations": "bf16", "output": "fp32",
                        "split_k": args.split_k if args.split_k > 0 else "auto"})
+    elif work.kind == "dense":
+        wl_cfg.update({"inputs": "bf16 [M,K] x bf16 [K,N]", "output": "fp32"})
     else:
         wl_cfg.update({"inputs": "e4m3 [M,K] x e4m3 [K,N], per-tensor scales",
                        "output": "bf16 (rescaled in the epilogue)",
@@ -559,7 +588,7 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
         "higher_is_better": True,
         "scaling": "strong" if work.sharded else "weak",
         "vs_baseline": None,
-        "dtype": "bf16" if work.kind == "w4a16" else "e4m3",
+        "dtype": "e4m3" if work.kind == "fp8" else "bf16",
         "data": "synthetic (seeded N(0,0.02) weights quantized on device, N(0,1) activations)",
         "config": wl_cfg,
         "roofline": {
@@ -600,7 +629,8 @@ def cpu_baseline(wl: dict, budget_s: float = 10.0) -> dict:
     """Time the reference's CPU path on a bounded sample of the workload.
 
     W4A16: unpack + dequantize + fp32 matmul (tests/test_gemm_int4.py:26);
-    fp8: (a8.float()/sa) @ (b8.float()/sb) (gemm_fp8.py:132). Large GEMMs are
+    fp8: (a8.float()/sa) @ (b8.float()/sb) (gemm_fp8.py:132); dense: fp32
+    matmul of the bf16 inputs (gemm.py:134-142). Large GEMMs are
     sampled by output rows; the rate is scaled to the full step's unit.
     """
     from oracle import quant_ref as o
@@ -619,6 +649,15 @@ def cpu_baseline(wl: dict, budget_s: float = 10.0) -> dict:
 
         def per_rows(wd):  # fp32 matmul of `rows` activation rows
             return a @ wd
+    elif wl["kind"] == "dense":
+        a = o.round_to_bf16(rng.standard_normal((rows, K), dtype=np.float32))
+        b = o.round_to_bf16(rng.standard_normal((K, N), dtype=np.float32))
+
+        def once():
+            return b
+
+        def per_rows(bd):  # gemm.py:134-142 checks against a.float() @ b.float()
+            return a @ bd
     else:
         a8, sa = o.fp8_quantize(rng.standard_normal((rows, K), dtype=np.float32), "bf16")
         b8, sb = o.fp8_quantize(rng.standard_normal((K, N), dtype=np.float32), "bf16")
@@ -643,6 +682,7 @@ def cpu_baseline(wl: dict, budget_s: float = 10.0) -> dict:
         el = tc - t0
         if el >= budget_s and n >= 2:
             break
+    prep = {"w4a16": "weight dequant", "fp8": "B e4m3 -> f32", "dense": "no weight prep"}[wl["kind"]]
     # one full step = one dequant + the matmul over all M rows
     sec_per_step = t_once / n + (t_rows / n) * (M / rows)
     hbm = is_hbm_bound(wl)
@@ -652,7 +692,7 @@ def cpu_baseline(wl: dict, budget_s: float = 10.0) -> dict:
     else:
         value, unit = 2 * M * N * K / sec_per_step / 1e12, "TFLOP/s"
     return {"value": round(value, 6), "unit": unit, "cores": _cpu_threads(), "kind": "port",
-            "sample": f"{n} repetitions of (weight dequant + matmul of {rows} of {M} rows), "
+            "sample": f"{n} repetitions of ({prep} + matmul of {rows} of {M} rows), "
                       f"M={M} N={N} K={K}, {el:.1f} s, scaled to all rows; numpy restatement "
                       f"of the reference's torch CPU path",
             "ms_per_step": round(sec_per_step * 1e3, 3)}

@@ -209,6 +209,23 @@ PK_API int pk_fp8_quantize(const void* x, int dtype, int64_t n, float scale, uin
 PK_API int pk_fp8_gemm(const uint8_t* a8, const uint8_t* b8, int64_t M, int64_t N, int64_t K,
                 float out_scale, void* out, int out_dtype, void* stream);
 
+/* gemm_fp8.quantize (gemm_fp8.py:89-95) without the host sync of its .item():
+ * amax[0] = max|x| and scale[0] = 448 / amax (1 when x is all zero, where the
+ * reference's division raises) are computed and left in DEVICE memory, and
+ * x8 = e4m3(dtype(x * scale)) as pk_fp8_quantize would write it with that
+ * scale. amax and scale are distinct device floats. Stream-ordered; graph
+ * capturable. */
+PK_API int pk_fp8_quantize_device(const void* x, int dtype, int64_t n, uint8_t* x8, float* amax,
+                           float* scale, void* stream);
+
+/* pk_fp8_gemm with the per-tensor scales read from DEVICE memory (as
+ * pk_fp8_quantize_device leaves them): out = (A8 @ B8) / (a_scale[0] *
+ * b_scale[0]), the reciprocal formed in double and rounded to fp32 as
+ * gemm_fp8.py:106 forms out_scale on the host. */
+PK_API int pk_fp8_gemm_scaled(const uint8_t* a8, const uint8_t* b8, int64_t M, int64_t N, int64_t K,
+                       const float* a_scale, const float* b_scale, void* out, int out_dtype,
+                       void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* Dense split-K GEMM                                                      */
 /* ---------------------------------------------------------------------- */

@@ -425,8 +425,13 @@ int pk_fp8_quantize(const void* x, int dtype, int64_t n, float scale, uint8_t* x
   return PK_OK;
 }
 
-int pk_fp8_gemm(const uint8_t* a8, const uint8_t* b8, int64_t M, int64_t N, int64_t K,
-                float out_scale, void* out, int out_dtype, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int fp8_gemm_impl(const uint8_t* a8, const uint8_t* b8, int64_t M, int64_t N, int64_t K,
+                  float out_scale, const float* a_scale, const float* b_scale, void* out,
+                  int out_dtype, void* stream) {
   if (!a8 || !b8 || !out) return fail(PK_ERR_SHAPE, "null pointer");
   if (M <= 0 || N <= 0 || K <= 0) return fail(PK_ERR_SHAPE, "need M, N, K > 0");
   if ((K % 16) != 0 || (N % 16) != 0)
@@ -452,11 +457,41 @@ int pk_fp8_gemm(const uint8_t* a8, const uint8_t* b8, int64_t M, int64_t N, int6
   g.out_dtype = out_dtype;
   g.ldc = N;
   g.out_scale = out_scale;
+  g.scale_a = a_scale;
+  g.scale_b = b_scale;
   g.status = device_status_ptr();
   const char* why = "";
   cudaError_t e = launch_gemm_tc(g, as_stream(stream), &why);
   if (e == cudaErrorInvalidValue && why[0] != '\0') return fail(PK_ERR_ALIGN, "%s", why);
   if (e != cudaSuccess) return cuda_fail(e, "fp8 GEMM launch");
+  ok();
+  return PK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pk_fp8_gemm(const uint8_t* a8, const uint8_t* b8, int64_t M, int64_t N, int64_t K,
+                float out_scale, void* out, int out_dtype, void* stream) {
+  return fp8_gemm_impl(a8, b8, M, N, K, out_scale, nullptr, nullptr, out, out_dtype, stream);
+}
+
+int pk_fp8_gemm_scaled(const uint8_t* a8, const uint8_t* b8, int64_t M, int64_t N, int64_t K,
+                       const float* a_scale, const float* b_scale, void* out, int out_dtype,
+                       void* stream) {
+  if (!a_scale || !b_scale) return fail(PK_ERR_SHAPE, "null scale pointer");
+  return fp8_gemm_impl(a8, b8, M, N, K, 1.0f, a_scale, b_scale, out, out_dtype, stream);
+}
+
+int pk_fp8_quantize_device(const void* x, int dtype, int64_t n, uint8_t* x8, float* amax,
+                           float* scale, void* stream) {
+  if (!x || !x8 || !amax || !scale || n <= 0) return fail(PK_ERR_SHAPE, "need a non-empty input");
+  if (amax == scale) return fail(PK_ERR_SHAPE, "amax and scale must be different floats");
+  if (dtype != PK_F16 && dtype != PK_BF16 && dtype != PK_F32)
+    return fail(PK_ERR_DTYPE, "fp8 quantize input must be f16, bf16 or f32");
+  cudaError_t e = launch_fp8_quantize_device(x, dtype, n, amax, scale, x8, as_stream(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fp8 device quantize launch");
   ok();
   return PK_OK;
 }

@@ -87,7 +87,18 @@ struct Params {
   int grouped;           // int4: 1 = group scales in the dequant, 0 = scalar out_scale
   int a_is_f16;          // 16-bit kinds: A dtype is fp16 (else bf16)
   int* status;
+  const float* scale_a;  // fp8 with device scales: out_scale = 1 / (*scale_a * *scale_b)
+  const float* scale_b;
 };
+
+// The epilogue multiplier: the host's out_scale, or, for scales that live on
+// the device (written by the previous kernel; read after griddepcontrol.wait),
+// 1 / (scale_a * scale_b) formed in double as the reference forms it on the
+// host (gemm_fp8.py:106) and rounded once to fp32.
+__device__ __forceinline__ float epilogue_scale(const Params& p) {
+  if (p.scale_a == nullptr) return p.out_scale;
+  return static_cast<float>(1.0 / (static_cast<double>(*p.scale_a) * static_cast<double>(*p.scale_b)));
+}
 
 __device__ __forceinline__ void tile_coords(int t, const Params& p, int& tm, int& tn, int& ks) {
   ks = t % p.split;
@@ -304,6 +315,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
     // ------------------------------- epilogue -------------------------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_sub = q * 32 + lane;
+    const float out_scale = epilogue_scale(p);
     int local = 0;
     for (int u = blockIdx.x; u < num_units && !fail; u += gridDim.x, ++local) {
       int tm, tn, ks;
@@ -344,7 +356,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
               // emits; column e of the chunk sits at position (e%4)*2 + e/4.
 #pragma unroll
               for (int e = 0; e < 8; ++e)
-                v[e] = __uint_as_float(raw[i + (kInt4 ? ((e & 3) * 2 + (e >> 2)) : e)]) * p.out_scale;
+                v[e] = __uint_as_float(raw[i + (kInt4 ? ((e & 3) * 2 + (e >> 2)) : e)]) * out_scale;
               const int col = col0 + c * 32 + i;
               if (col < p.N)
                 store8(p.out, p.out_dtype, row * p.ldc + col, v, col + 8 <= p.N, min(8, p.N - col));
@@ -374,7 +386,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
             const float* base = p.partials + static_cast<int64_t>(tile_id) * p.split * (BM * BN) +
                                 row_in_tile * BN;
             if (row < p.M)
-              sum_parts_row<BN>(base, BM * BN, p.split, p.out_scale, p.out, p.out_dtype,
+              sum_parts_row<BN>(base, BM * BN, p.split, out_scale, p.out, p.out_dtype,
                                 row * p.ldc, col0, p.N);
           }
           named_bar_sync(1, kEpiWarps * 32);
@@ -629,6 +641,7 @@ __global__ void __launch_bounds__(PairCfg<kKind>::kThreads, 1)
     // ----------------------- epilogue (both CTAs) ---------------------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t acc_empty0 = cluster_map(smem_u32(&acc_empty[0]), 0);
+    const float out_scale = epilogue_scale(p);
     int local = 0;
     for (int u = pair; u < num_units && !fail; u += npairs, ++local) {
       int tm, tn, ks;
@@ -652,7 +665,7 @@ __global__ void __launch_bounds__(PairCfg<kKind>::kThreads, 1)
           for (int i = 0; i < 32; i += 8) {
             float v[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(raw[i + e]) * p.out_scale;
+            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(raw[i + e]) * out_scale;
             const int col = col0 + c * 32 + i;
             if (col < p.N)
               store8(p.out, p.out_dtype, row * p.ldc + col, v, col + 8 <= p.N, min(8, p.N - col));
@@ -717,6 +730,8 @@ cudaError_t launch_typed(const GemmArgs& g, cudaStream_t s, const char** why) {
   p.out_dtype = g.out_dtype;
   p.ldc = g.ldc;
   p.out_scale = g.out_scale;
+  p.scale_a = g.scale_a;
+  p.scale_b = g.scale_b;
   p.out = g.out;
   p.partials = g.partials;
   p.sems = g.sems;
@@ -784,6 +799,8 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t s, const char** why) {
   p.out_dtype = g.out_dtype;
   p.ldc = g.ldc;
   p.out_scale = g.out_scale;
+  p.scale_a = g.scale_a;
+  p.scale_b = g.scale_b;
   p.out = g.out;
   p.group = 1;
   p.a_is_f16 = g.a_dtype == PK_F16;

@@ -67,6 +67,10 @@ cudaError_t launch_quant_int4_tensor(const void* w, int dtype, int64_t n, float 
 cudaError_t launch_pack_int4(const int8_t* q, int64_t K, int64_t N, uint8_t* p, cudaStream_t s);
 cudaError_t launch_unpack_int4(const uint8_t* p, int64_t K, int64_t N, int8_t* q,
                                cudaStream_t s);
+// absmax into amax, then the cast with scale = 448 / amax computed on the
+// device and stored to `scale` (gemm_fp8.quantize without the host sync)
+cudaError_t launch_fp8_quantize_device(const void* x, int dtype, int64_t n, float* amax,
+                                       float* scale, uint8_t* y, cudaStream_t s);
 cudaError_t launch_fp8_quantize(const void* x, int dtype, int64_t n, float scale, uint8_t* y,
                                 cudaStream_t s);
 // B[K, N] (dtype) = q * s rounded to dtype, or q when scales == nullptr (N % 8 == 0)
@@ -132,6 +136,8 @@ struct GemmArgs {
   int out_dtype;        // PK_F32 / PK_BF16
   int64_t ldc;
   float out_scale;
+  const float* scale_a;  // fp8: device scales of A and B; when set, the epilogue
+  const float* scale_b;  // multiplies by 1 / (scale_a * scale_b) instead of out_scale
   float* partials;      // split-K workspace
   unsigned* sems;
   int* status;

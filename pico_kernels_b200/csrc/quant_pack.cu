@@ -254,6 +254,55 @@ __global__ void fp8_quantize_kernel(const T* __restrict__ x, int64_t n, float sc
   }
 }
 
+// gemm_fp8.py:89-95 without the host round trip: scale = E4M3_MAX / amax is
+// computed here from the absmax the previous kernel left in device memory
+// (fp32 division, correctly rounded: the same float as the reference's
+// double quotient rounded to fp32), then (x * scale) in x's dtype, RNE to
+// e4m3. Block 0 stores the scale for the GEMM epilogue. An all-zero input
+// (where the reference's division raises) gets scale 1. Eight elements per
+// thread: one 16-byte load of 16-bit inputs (two of fp32), one 8-byte store.
+constexpr float kE4m3Max = 448.0f;
+
+template <typename T>
+__global__ void fp8_quantize_dev_kernel(const T* __restrict__ x, int64_t n,
+                                        const float* __restrict__ amax, float* __restrict__ scale_out,
+                                        uint8_t* __restrict__ y) {
+  const float m = *amax;
+  const float scale = m > 0.0f ? kE4m3Max / m : 1.0f;
+  if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(y) & 7) == 0;
+  const int64_t n8 = vec ? n / 8 : 0;
+  for (int64_t i = tid; i < n8; i += stride) {
+    float v[8];
+    if constexpr (sizeof(T) == 2) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(x) + i);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) v[c] = to_f32<T>(e[c]);
+    } else {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(x) + 2 * i);
+      const float4 b = __ldg(reinterpret_cast<const float4*>(x) + 2 * i + 1);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint32_t b8 = __nv_cvt_float_to_fp8(round_through<T>(v[c] * scale), __NV_NOSAT,
+                                                __NV_E4M3);
+      w[c >> 2] |= b8 << (8 * (c & 3));
+    }
+    reinterpret_cast<uint2*>(y)[i] = make_uint2(w[0], w[1]);
+  }
+  for (int64_t i = n8 * 8 + tid; i < n; i += stride) {
+    const float v = round_through<T>(to_f32<T>(x[i]) * scale);
+    y[i] = static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_NOSAT, __NV_E4M3));
+  }
+}
+
 // Dequantize packed int4 weights once into a 16-bit row-major B[K, N] for the
 // dense tensor-core GEMM of large-M calls: B[k, n] = q[k, n] * s[k/g, n] rounded
 // to T by the same packed instructions the fused W4A16 kernel uses for its MMA
@@ -405,6 +454,30 @@ cudaError_t launch_unpack_int4(const uint8_t* p, int64_t K, int64_t N, int8_t* q
                                cudaStream_t s) {
   const int64_t nb = K * N / 2;
   unpack_int4_kernel<<<static_cast<unsigned>((nb + 255) / 256), 256, 0, s>>>(p, nb, q);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fp8_quantize_device(const void* x, int dtype, int64_t n, float* amax,
+                                       float* scale, uint8_t* y, cudaStream_t s) {
+  cudaError_t e = launch_absmax(x, dtype, n, amax, s);
+  if (e != cudaSuccess) return e;
+  const int threads = 256;
+  const int grid = grid_for(n / 8 + 1, threads);
+  switch (dtype) {
+    case PK_F16:
+      fp8_quantize_dev_kernel<__half>
+          <<<grid, threads, 0, s>>>(static_cast<const __half*>(x), n, amax, scale, y);
+      break;
+    case PK_BF16:
+      fp8_quantize_dev_kernel<__nv_bfloat16>
+          <<<grid, threads, 0, s>>>(static_cast<const __nv_bfloat16*>(x), n, amax, scale, y);
+      break;
+    case PK_F32:
+      fp8_quantize_dev_kernel<float>
+          <<<grid, threads, 0, s>>>(static_cast<const float*>(x), n, amax, scale, y);
+      break;
+    default: return cudaErrorInvalidValue;
+  }
   return cudaGetLastError();
 }
 

@@ -19,6 +19,7 @@ def header_functions():
 def test_header_declares_the_boundary():
     names = header_functions()
     for must in ("pk_quant_int4_group", "pk_pack_int4_n", "pk_w4a16_gemm", "pk_fp8_gemm",
+                 "pk_fp8_quantize_device", "pk_fp8_gemm_scaled",
                  "pk_gemm_splitk", "pk_w4a16_workspace_size", "pk_last_error_string"):
         assert must in names
 
@@ -46,6 +47,12 @@ def test_host_only_calls_work_without_gpu():
         _lib.check(st, "pack")
     with pytest.raises(AssertionError):  # the reference's error type still catches it
         _lib.check(st, "pack")
+    # device-scale fp8 entries validate their pointers on the host too
+    assert lib.pk_fp8_quantize_device(None, _lib.PK_BF16, 16, None, None, None, None) == \
+        _lib.PK_ERR_SHAPE
+    assert lib.pk_fp8_quantize_device(8, _lib.PK_BF16, 16, 8, 64, 64, None) == _lib.PK_ERR_SHAPE
+    assert lib.pk_fp8_gemm_scaled(16, 16, 16, 16, 16, None, None, 16, _lib.PK_F32, None) == \
+        _lib.PK_ERR_SHAPE
 
 
 def test_workspace_size_is_host_only():
