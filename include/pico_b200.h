@@ -193,6 +193,22 @@ PK_API int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const 
                                  const uint64_t* peer_flag, void* workspace,
                                  size_t workspace_bytes, void* stream);
 
+/* GPTQ producer of packed int4 weights: the loop of quantize.gptq_layer
+ * (quantize.py:71-115, act_order=False) run on the GPU, emitting codes and
+ * scales in the W4A16 layout instead of fake-quant floats. wt[K, N] fp32
+ * (K = input features, N = outputs: the layer's weight transposed) is the
+ * working copy and is overwritten; h_inv[K, K] fp32 is the inverse of the
+ * damped Hessian (quantize.py:88-93). Scales are per group of group_size
+ * (<= 128) consecutive input features and output, taken from the group's
+ * error-updated weights when the walk reaches it (max|w| clamped at 1e-12,
+ * / 7), stored rounded to scale_dtype as [ceil(K/group), N]; codes
+ * clamp(round(w / scale), -7, 7) packed as pk_pack_int4_n into packed[K,
+ * N/2]. err_scratch holds group_size * N floats. Updates are applied in the
+ * reference's order with separately rounded products and differences. */
+PK_API int pk_gptq_int4(float* wt, const float* h_inv, int64_t K, int64_t N, int group_size,
+                 uint8_t* packed, void* scales, int scale_dtype, float* err_scratch,
+                 void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* fp8 (e4m3) GEMM                                                         */
 /* ---------------------------------------------------------------------- */

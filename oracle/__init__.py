@@ -6,10 +6,10 @@ This package is the checker, never the product: only ``tests/``,
 never calls into it and fails loudly when its extension is missing.
 
 Parity is pinned: ``tests/golden/make_golden.py`` ran the reference's own
-functions (``quantize.quantize_col``, ``gemm_int4.quantize_int4``,
-``gemm_int4.pack_int4_n``, ``gemm_fp8.quantize``) on seeded inputs and
-committed their outputs; ``tests/test_oracle_golden.py`` checks this oracle
-against them bit for bit.
+functions (``quantize.quantize_col``, ``quantize.gptq_layer``,
+``gemm_int4.quantize_int4``, ``gemm_int4.pack_int4_n``, ``gemm_fp8.quantize``)
+on seeded inputs and committed their outputs; ``tests/test_oracle_golden.py``
+checks this oracle against them bit for bit.
 """
 
 from .quant_ref import *  # noqa: F401,F403

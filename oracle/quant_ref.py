@@ -27,6 +27,7 @@ __all__ = [
     "quantize_int4_per_tensor", "pack_int4_n", "unpack_int4_n",
     "dequant_weight", "w4a16_reference", "int4_gemm_per_tensor_reference",
     "fp8_quantize", "fp8_gemm_reference", "dense_gemm_reference",
+    "gptq_inverse_hessian_inputs", "gptq_fake_quant_columns", "gptq_int4_codes",
 ]
 
 # gemm_fp8.py:24 -- float(torch.finfo(torch.float8_e4m3fn).max)
@@ -267,3 +268,81 @@ def fp8_gemm_reference(a8_bits: np.ndarray, a_scale: float, b8_bits: np.ndarray,
 def dense_gemm_reference(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     """``a.float() @ b.float()`` (tests/test_gemm_splitk.py:24)."""
     return np.asarray(a, dtype=np.float32) @ np.asarray(b, dtype=np.float32)
+
+
+# ---------------------------------------------------------------------------
+# GPTQ (quantize.py:71-115) with act_order=False, given the inverse Hessian
+# ---------------------------------------------------------------------------
+def gptq_inverse_hessian_inputs(x: np.ndarray, damp: float = 0.01):
+    """``H = X^T X / n + damp * mean(diag) * I`` (quantize.py:88-92), fp32.
+
+    The reference inverts this with ``torch.linalg.inv`` (quantize.py:93); the
+    inverse is taken as an input by the functions below, so that a restatement
+    fed the reference's own inverse reproduces its loop bit for bit."""
+    xf = np.asarray(x, dtype=np.float32)
+    n, d = xf.shape
+    h = (xf.T @ xf) / np.float32(n)
+    mean = np.float32(np.diag(h).mean())
+    return h + np.float32(damp) * mean * np.eye(d, dtype=np.float32)
+
+
+def gptq_fake_quant_columns(w: np.ndarray, h_inv: np.ndarray, bits: int,
+                            group_size: int | None = None) -> np.ndarray:
+    """``gptq_layer(w, x, bits, act_order=False, group_size)`` (quantize.py:71-115).
+
+    Walks the input columns j of ``w[out, in]`` in order (quantize.py:99):
+    ``q = quantize_col(w[:, j])`` with its groups along the OUTPUT rows
+    (quantize.py:100), ``err = w[:, j] - q``, ratio ``h_inv[j, j+1:] /
+    h_inv[j, j]`` and ``w[:, j+1:] -= outer(err, ratio)`` (quantize.py:101-104),
+    each product and difference rounded to fp32 on its own."""
+    wq = np.array(w, dtype=np.float32, copy=True)
+    h_inv = np.asarray(h_inv, dtype=np.float32)
+    if bits >= 16:
+        return wq
+    d = wq.shape[1]
+    for j in range(d):
+        col = wq[:, j].copy()
+        q = quantize_col_fake(col, bits, group_size)
+        err = (col - q).astype(np.float32)
+        ratio = (h_inv[j, j + 1:] / h_inv[j, j]).astype(np.float32)
+        wq[:, j + 1:] = wq[:, j + 1:] - np.outer(err, ratio).astype(np.float32)
+        wq[:, j] = q
+    return wq
+
+
+def gptq_int4_codes(w: np.ndarray, h_inv: np.ndarray, group_size: int = 128):
+    """The packed-weight form of the same loop: codes and scales in the W4A16
+    GEMM's layout ``B[K = in, N = out]`` with groups along K.
+
+    The column walk, error and update are quantize.py:99-104 as in
+    ``gptq_fake_quant_columns``; the only change is the scale, which must be
+    shared by ``group_size`` consecutive input features to be applied after
+    the GEMM's K reduction: at the first input feature of each group, per
+    output row ``n``, ``scale = max|w[n, group]|.clamp_min(1e-12) / 7`` over
+    that group's CURRENT (error-updated) weights (quantize.py:58 applied along
+    K); each column then uses ``q = clamp(round(w / scale), -7, 7)`` and
+    ``q * scale`` (quantize.py:59). With ``h_inv = I`` there is no error
+    feedback and this is ``group_quant_codes(w.T, group_size)``.
+    Returns ``(codes int8[in, out], scales float32[ceil(in/g), out])``."""
+    wq = np.array(w, dtype=np.float32, copy=True)       # [out, in]
+    h_inv = np.asarray(h_inv, dtype=np.float32)
+    out_dim, d = wq.shape
+    qmax = np.float32(7)
+    G = (d + group_size - 1) // group_size
+    scales = np.empty((G, out_dim), dtype=np.float32)
+    codes = np.empty((d, out_dim), dtype=np.int8)
+    s = None
+    for j in range(d):
+        if j % group_size == 0:
+            blk = wq[:, j:min(j + group_size, d)]
+            s = np.maximum(np.abs(blk).max(axis=1), np.float32(1e-12)) / qmax
+            scales[j // group_size] = s
+        col = wq[:, j].copy()
+        qi = np.clip(np.rint(col / s), -qmax, qmax)
+        q = (qi * s).astype(np.float32)
+        codes[j] = qi.astype(np.int8)
+        err = (col - q).astype(np.float32)
+        ratio = (h_inv[j, j + 1:] / h_inv[j, j]).astype(np.float32)
+        wq[:, j + 1:] = wq[:, j + 1:] - np.outer(err, ratio).astype(np.float32)
+        wq[:, j] = q
+    return codes, scales

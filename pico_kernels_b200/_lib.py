@@ -64,6 +64,7 @@ SIGNATURES = {
     "pk_fp8_quantize": (_int, [_vp, _int, _i64, _f32, _vp, _vp]),
     "pk_fp8_gemm": (_int, [_vp, _vp, _i64, _i64, _i64, _f32, _vp, _int, _vp]),
     "pk_fp8_quantize_device": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp]),
+    "pk_gptq_int4": (_int, [_vp, _vp, _i64, _i64, _int, _vp, _vp, _int, _vp, _vp]),
     "pk_fp8_gemm_scaled": (_int, [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _int, _vp]),
     "pk_gemm_splitk_workspace_size": (_sz, [_i64, _i64, _i64, _int]),
     "pk_gemm_splitk": (_int, [_vp, _vp, _int, _i64, _i64, _i64, _int, _vp, _vp, _sz, _vp]),

@@ -484,6 +484,24 @@ int pk_fp8_gemm_scaled(const uint8_t* a8, const uint8_t* b8, int64_t M, int64_t 
   return fp8_gemm_impl(a8, b8, M, N, K, 1.0f, a_scale, b_scale, out, out_dtype, stream);
 }
 
+int pk_gptq_int4(float* wt, const float* h_inv, int64_t K, int64_t N, int group_size,
+                 uint8_t* packed, void* scales, int scale_dtype, float* err_scratch,
+                 void* stream) {
+  if (!wt || !h_inv || !packed || !scales || !err_scratch)
+    return fail(PK_ERR_SHAPE, "null pointer");
+  if (K <= 0 || N <= 0 || (N % 2) != 0) return fail(PK_ERR_SHAPE, "need K > 0 and an even N > 0");
+  if (group_size < 1 || group_size > gptq_max_group())
+    return fail(PK_ERR_SHAPE, "group_size must be in [1, %d] (got %d)", gptq_max_group(),
+                group_size);
+  if (scale_dtype != PK_F32 && scale_dtype != PK_F16 && scale_dtype != PK_BF16)
+    return fail(PK_ERR_DTYPE, "scales must be f32, f16 or bf16");
+  cudaError_t e = launch_gptq_int4(wt, h_inv, K, N, group_size, packed, scales, scale_dtype,
+                                   err_scratch, as_stream(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gptq launch");
+  ok();
+  return PK_OK;
+}
+
 int pk_fp8_quantize_device(const void* x, int dtype, int64_t n, uint8_t* x8, float* amax,
                            float* scale, void* stream) {
   if (!x || !x8 || !amax || !scale || n <= 0) return fail(PK_ERR_SHAPE, "need a non-empty input");

@@ -67,6 +67,12 @@ cudaError_t launch_quant_int4_tensor(const void* w, int dtype, int64_t n, float 
 cudaError_t launch_pack_int4(const int8_t* q, int64_t K, int64_t N, uint8_t* p, cudaStream_t s);
 cudaError_t launch_unpack_int4(const uint8_t* p, int64_t K, int64_t N, int8_t* q,
                                cudaStream_t s);
+// ---- gptq.cu (GPTQ producer of packed int4 weights) ----------------------
+int gptq_max_group();
+cudaError_t launch_gptq_int4(float* wt, const float* h_inv, int64_t K, int64_t N, int group,
+                             uint8_t* packed, void* scales, int scale_dtype, float* err,
+                             cudaStream_t s);
+
 // absmax into amax, then the cast with scale = 448 / amax computed on the
 // device and stored to `scale` (gemm_fp8.quantize without the host sync)
 cudaError_t launch_fp8_quantize_device(const void* x, int dtype, int64_t n, float* amax,

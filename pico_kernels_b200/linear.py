@@ -62,11 +62,15 @@ class W4A16Linear(nn.Module):
 
     @classmethod
     def from_linear(cls, linear: nn.Linear, group_size: int = 128,
-                    dtype: torch.dtype | None = None) -> "W4A16Linear":
+                    dtype: torch.dtype | None = None, calib: torch.Tensor | None = None,
+                    damp: float = 0.01) -> "W4A16Linear":
         """Quantize ``linear.weight`` (on a CUDA device) into a new layer.
 
-        ``dtype`` (activations and stored scales) defaults to the weight's
-        dtype when that is fp16/bf16, else bf16. The bias is kept in fp32.
+        Round-to-nearest per group by default; with calibration inputs
+        ``calib[..., in]`` (this layer's inputs) the GPTQ producer
+        (``gptq.gptq_quantize_int4``) chooses the codes. ``dtype``
+        (activations and stored scales) defaults to the weight's dtype when
+        that is fp16/bf16, else bf16. The bias is kept in fp32.
         """
         w = linear.weight.detach()
         _lib.require_cuda(w)
@@ -76,7 +80,12 @@ class W4A16Linear(nn.Module):
                     group_size, dtype, w.device)
         # group absmax from the weights as stored (fp32 kept exact), scales rounded
         # to the activation dtype as the GEMM reads them
-        packed, scales = quantize_int4_grouped(w.t(), group_size, scale_dtype=dtype)
+        if calib is not None:
+            from .gptq import gptq_quantize_int4
+            packed, scales = gptq_quantize_int4(w, calib, group_size=group_size, damp=damp,
+                                                scale_dtype=dtype)
+        else:
+            packed, scales = quantize_int4_grouped(w.t(), group_size, scale_dtype=dtype)
         layer.w_packed.copy_(packed)
         layer.scales.copy_(scales)
         if linear.bias is not None:
@@ -109,23 +118,48 @@ class W4A16Linear(nn.Module):
                 f"bias={self.bias is not None}, group_size={self.group_size}, int4")
 
 
+def _capture_inputs(model: nn.Module, module: nn.Module, calib) -> torch.Tensor:
+    """Inputs ``module`` sees when ``model`` runs on ``calib`` (a tensor or a
+    tuple of positional arguments), flattened to ``[rows, in]``
+    (quantize.py:132-157)."""
+    seen: list[torch.Tensor] = []
+
+    def hook(_m, args):
+        seen.append(args[0].detach())
+
+    handle = module.register_forward_pre_hook(hook)
+    try:
+        with torch.no_grad():
+            model(*calib) if isinstance(calib, tuple) else model(calib)
+    finally:
+        handle.remove()
+    return torch.cat([t.reshape(-1, t.shape[-1]) for t in seen], dim=0)
+
+
 def quantize_linear_layers(model: nn.Module, group_size: int = 128,
                            select: Callable[[str, nn.Linear], bool] | None = None,
-                           dtype: torch.dtype | None = None) -> nn.Module:
+                           dtype: torch.dtype | None = None, calib=None,
+                           damp: float = 0.01) -> nn.Module:
     """Replace ``nn.Linear`` children in place with ``W4A16Linear``.
 
     ``select(name, module)`` picks the layers (default: every ``nn.Linear``
     with an even ``out_features``); quantize.py:124-129 picks those under
     ``transformer.h``, which ``select=lambda n, m: n.startswith("transformer.h")``
-    reproduces. Returns ``model``.
+    reproduces. With ``calib`` (the model's input: a tensor or a tuple of
+    arguments) each layer is GPTQ-quantized from the inputs it sees when the
+    model, with the layers before it already quantized, runs on ``calib``
+    (the sequential re-capture of quantize.py:160-184); without it, per-group
+    round-to-nearest. Returns ``model``.
     """
-    targets = [(name, mod) for name, mod in model.named_modules()
+    targets = [name for name, mod in model.named_modules()
                if isinstance(mod, nn.Linear) and mod.out_features % 2 == 0
                and (select is None or select(name, mod))]
-    for name, mod in targets:
+    for name in targets:
         parent = model
         *path, leaf = name.split(".")
         for p in path:
             parent = getattr(parent, p)
-        setattr(parent, leaf, W4A16Linear.from_linear(mod, group_size, dtype))
+        mod = getattr(parent, leaf)
+        x = _capture_inputs(model, mod, calib) if calib is not None else None
+        setattr(parent, leaf, W4A16Linear.from_linear(mod, group_size, dtype, calib=x, damp=damp))
     return model

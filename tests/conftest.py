@@ -25,3 +25,9 @@ def golden():
 def config1():
     with np.load(GOLDEN / "config1.npz") as z:
         return {k: z[k] for k in z.files}
+
+
+@pytest.fixture(scope="session")
+def gptq_golden():
+    with np.load(GOLDEN / "gptq_small.npz") as z:
+        return {k: z[k] for k in z.files}

@@ -7,7 +7,9 @@ Run in a container where the reference checkout is available:
 It imports ``quantize.quantize_col``, ``gemm_int4.quantize_int4``,
 ``gemm_int4.pack_int4_n`` and ``gemm_fp8.quantize`` from that checkout and
 runs them on CPU torch tensors (the Triton kernels are never launched), then
-writes ``golden_small.npz`` and ``config1.npz`` beside this script. The GPU box
+writes ``golden_small.npz``, ``config1.npz`` and ``gptq_small.npz`` beside
+this script (``quantize.gptq_layer`` with act_order=False, the inverse Hessian
+it builds, and its fake-quant output). The GPU box
 has no reference checkout: the tests only read the committed ``.npz`` files.
 
 Derived quantities:
@@ -190,6 +192,33 @@ def make_config1(ref: Path) -> dict[str, np.ndarray]:
     }
 
 
+def make_gptq(ref: Path) -> dict[str, np.ndarray]:
+    """``quantize.gptq_layer`` (quantize.py:71-115) with act_order=False on CPU,
+    plus the inverse Hessian built with the reference's own expressions
+    (quantize.py:88-93), which the restatement takes as an input."""
+    sys.path.insert(0, str(ref))
+    import quantize  # noqa: E402
+
+    out: dict[str, np.ndarray] = {}
+    torch.manual_seed(21)
+    for (o_dim, i_dim, n, gs) in ((32, 64, 256, None), (48, 40, 128, 8), (16, 96, 512, 16)):
+        w = torch.randn(o_dim, i_dim) * 0.02
+        x = torch.randn(n, i_dim) * torch.linspace(0.2, 3.0, i_dim)  # uneven feature energy
+        xf = x.float()
+        H = (xf.t() @ xf) / n
+        diag_mean = torch.diag(H).clone().mean()
+        H = H + 0.01 * diag_mean * torch.eye(i_dim)
+        h_inv = torch.linalg.inv(H)
+        wq = quantize.gptq_layer(w, x, 4, damp=0.01, act_order=False, group_size=gs)
+        key = f"gptq/o{o_dim}_i{i_dim}_g{gs or 0}"
+        out[f"{key}/w"] = _np(w)
+        out[f"{key}/x"] = _np(x)
+        out[f"{key}/h_inv"] = _np(h_inv)
+        out[f"{key}/group"] = np.array(gs or 0)
+        out[f"{key}/wq"] = _np(wq)
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
@@ -198,6 +227,7 @@ def main() -> None:
     small = make_small(args.reference)
     np.savez_compressed(HERE / "golden_small.npz", **small)
     np.savez_compressed(HERE / "config1.npz", **make_config1(args.reference))
+    np.savez_compressed(HERE / "gptq_small.npz", **make_gptq(args.reference))
     print("wrote", HERE / "golden_small.npz", len(small), "arrays")
 
 

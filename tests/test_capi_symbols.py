@@ -53,6 +53,9 @@ def test_host_only_calls_work_without_gpu():
     assert lib.pk_fp8_quantize_device(8, _lib.PK_BF16, 16, 8, 64, 64, None) == _lib.PK_ERR_SHAPE
     assert lib.pk_fp8_gemm_scaled(16, 16, 16, 16, 16, None, None, 16, _lib.PK_F32, None) == \
         _lib.PK_ERR_SHAPE
+    # GPTQ producer: odd N and oversized groups are rejected on the host
+    assert lib.pk_gptq_int4(16, 16, 64, 33, 16, 16, 16, _lib.PK_F32, 16, None) == _lib.PK_ERR_SHAPE
+    assert lib.pk_gptq_int4(16, 16, 64, 32, 256, 16, 16, _lib.PK_F32, 16, None) == _lib.PK_ERR_SHAPE
 
 
 def test_workspace_size_is_host_only():

@@ -126,3 +126,48 @@ def test_e4m3_encoder_matches_torch(seed):
     x = x[x.abs() < 464]
     ref = x.to(torch.float8_e4m3fn).view(torch.uint8).numpy()
     assert np.array_equal(o.f32_to_e4m3_bits(x.numpy()), ref)
+
+
+def _gptq_keys(g):
+    return sorted({k.rsplit("/", 1)[0] for k in g if k.startswith("gptq/")})
+
+
+def test_gptq_loop_matches_reference(gptq_golden):
+    """quantize.gptq_layer (act_order=False) reproduced bit for bit from the
+    reference's own inverse Hessian: quantize.py:99-104."""
+    keys = _gptq_keys(gptq_golden)
+    assert len(keys) == 3
+    for key in keys:
+        gs = int(gptq_golden[f"{key}/group"]) or None
+        wq = o.gptq_fake_quant_columns(gptq_golden[f"{key}/w"], gptq_golden[f"{key}/h_inv"], 4, gs)
+        assert np.array_equal(wq.view(np.uint32), gptq_golden[f"{key}/wq"].view(np.uint32)), key
+
+
+def test_gptq_hessian_restatement_is_close(gptq_golden):
+    """The damped Hessian (quantize.py:88-92) in numpy matches torch's to fp32
+    summation order; the GPU producer and the tests use the inverse as given."""
+    for key in _gptq_keys(gptq_golden):
+        h = o.gptq_inverse_hessian_inputs(gptq_golden[f"{key}/x"], 0.01)
+        hi = np.linalg.inv(h.astype(np.float64))
+        ref = gptq_golden[f"{key}/h_inv"].astype(np.float64)
+        assert np.abs(hi - ref).max() <= 1e-4 * np.abs(ref).max(), key
+
+
+def test_gptq_packed_form_reduces_to_rtn_without_feedback():
+    """With an identity inverse Hessian the packed GPTQ form is the RTN group
+    quantizer (group_quant_codes) exactly; with a real one it lowers the
+    calibration error below RTN's (the point of quantize.py:1-17)."""
+    rng = np.random.default_rng(3)
+    w = (rng.standard_normal((24, 64)) * 0.02).astype(np.float32)
+    codes, scales = o.gptq_int4_codes(w, np.eye(64, dtype=np.float32), 16)
+    c2, s2 = o.group_quant_codes(w.T, 16)
+    assert np.array_equal(codes, c2) and np.array_equal(scales, s2)
+    x = (rng.standard_normal((512, 64)) * np.linspace(0.2, 3.0, 64)).astype(np.float32)
+    x[:, 1:] += 0.7 * x[:, :-1]  # correlated features
+    h_inv = np.linalg.inv(o.gptq_inverse_hessian_inputs(x, 0.01).astype(np.float64)).astype(np.float32)
+    codes, scales = o.gptq_int4_codes(w, h_inv, 16)
+    wq_gptq = (codes.astype(np.float32) * np.repeat(scales, 16, axis=0)).T
+    wq_rtn = (c2.astype(np.float32) * np.repeat(s2, 16, axis=0)).T
+    err_g = np.linalg.norm(x @ (wq_gptq - w).T)
+    err_r = np.linalg.norm(x @ (wq_rtn - w).T)
+    assert err_g < 0.9 * err_r, (err_g, err_r)
