@@ -476,10 +476,26 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
         float sum[M];
 #pragma unroll
         for (int m = 0; m < M; ++m) sum[m] = 0.0f;
-        for (int64_t c = cfirst; c <= clast; ++c) {
-          const float* src = p.partials + (c + slice) * (M * kCols);
+        // A batch of partials' loads in flight before the adds, which stay in
+        // CTA order (a loop of load-then-add pays one L2 round trip per CTA).
+        constexpr int kBatch = 16 / M;
+        for (int64_t c0 = cfirst; c0 <= clast; c0 += kBatch) {
+          float x[kBatch][M];
 #pragma unroll
-          for (int m = 0; m < M; ++m) sum[m] += __ldcg(src + m * kCols + t);
+          for (int j = 0; j < kBatch; ++j) {
+            if (c0 + j <= clast) {
+              const float* src = p.partials + (c0 + j + slice) * (M * kCols);
+#pragma unroll
+              for (int m = 0; m < M; ++m) x[j][m] = __ldcg(src + m * kCols + t);
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < kBatch; ++j) {
+            if (c0 + j <= clast) {
+#pragma unroll
+              for (int m = 0; m < M; ++m) sum[m] += x[j][m];
+            }
+          }
         }
         store(sum);
         if (t == 0) p.sems[slice] = 0u;  // re-arm for the next call
