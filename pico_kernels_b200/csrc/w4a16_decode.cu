@@ -35,7 +35,6 @@ constexpr int kMmaWarp = 5;
 constexpr int kDeqWarp0 = 6;
 constexpr int kDeqWarps = 8;
 constexpr int kThreads = (kDeqWarp0 + kDeqWarps) * 32;  // 448
-constexpr int kDeqThreads = kDeqWarps * 32;
 
 constexpr int kBN = 128;      // output columns per CTA (MMA M)
 constexpr int kBK = 128;      // K rows per stage = one quantization group
@@ -291,9 +290,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int lo = (ks * total) / split, hi = ((ks + 1) * total) / split;
       const uint32_t red_addr = smem_u32(red);
       for (int e = lo + tid; e < hi; e += kEpiWarps * 32) {
+        // every CTA's value in flight before the adds (split order kept)
+        float x[kMaxClusterSplit];
+#pragma unroll
+        for (int j = 0; j < kMaxClusterSplit; ++j)
+          if (j < split) x[j] = ld_cluster_f32(cluster_map(red_addr + e * 4, static_cast<uint32_t>(j)));
         float sum = 0.0f;
-        for (int j = 0; j < split; ++j)
-          sum += ld_cluster_f32(cluster_map(red_addr + e * 4, static_cast<uint32_t>(j)));
+#pragma unroll
+        for (int j = 0; j < kMaxClusterSplit; ++j)
+          if (j < split) sum += x[j];
         const int m = e / kBN, l = e % kBN;
         store_out(out, out_dtype, m * ldo + static_cast<int64_t>(tile) * kBN + l,
                   sum * scalar_scale);
@@ -321,9 +326,21 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int m = 0; m < kMmaN; ++m) {
         if (m < M) {
+          // eight partials' loads in flight before the adds (split order kept)
           float sum = 0.0f;
-          for (int j = 0; j < split; ++j)
-            sum += (j == ks) ? acc[m] : __ldcg(tp + (static_cast<int64_t>(j) * M + m) * kBN + nl);
+          for (int j0 = 0; j0 < split; j0 += 8) {
+            float x[8];
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+              const int j = j0 + jj;
+              if (j < split)
+                x[jj] = (j == ks) ? acc[m]
+                                  : __ldcg(tp + (static_cast<int64_t>(j) * M + m) * kBN + nl);
+            }
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj)
+              if (j0 + jj < split) sum += x[jj];
+          }
           store_out(out, out_dtype, m * ldo + n, sum * scalar_scale);
         }
       }
