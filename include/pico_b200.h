@@ -119,7 +119,9 @@ PK_API size_t pk_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int split
  * kernel leaves it ready for the next call). With split_k = 0 at M = 1 (and
  * at M = 2 for layers of 16 MB or more) a CUDA-core GEMV runs instead; for
  * large layers it splits K over the SMs and reduces through the workspace,
- * and without one it falls back to the tensor-core decode kernel. From
+ * and without one it falls back to the tensor-core decode kernel, which
+ * serves the other shapes up to M = 32 (N and K multiples of 128, group 128
+ * or a scalar scale); larger M runs the tcgen05 prefill kernel. From
  * M = 1024 the weights are dequantized once into the workspace (16-bit
  * B[K, N] after the counters, pk_w4a16_workspace_size bytes) and the dense
  * tensor-core GEMM runs on it; without that workspace the fused kernel runs.
@@ -139,7 +141,7 @@ PK_API int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t*
  * cudaMalloc: a runtime that plans all device memory itself and forbids
  * libraries from allocating, or a latency-critical decode loop that cannot
  * afford cudaMalloc's implicit synchronization. Same arguments and result as
- * pk_w4a16_gemm minus the workspace, for decode shapes only (M <= 16,
+ * pk_w4a16_gemm minus the workspace, for decode shapes only (M <= 32,
  * N % 128 == 0, K % 128 == 0, group 128 or a scalar scale). Its split-K
  * partials live in a static 4 MiB device array owned by the library (plus
  * arrival counters for up to 4096 column tiles), held on every GPU that loads

@@ -1,12 +1,12 @@
-// W4A16 GEMM for decode shapes (M <= 16) on sm_100a.
+// W4A16 GEMM for decode shapes (M <= 32) on sm_100a.
 //
 // out[M, N] = A[M, K] @ (q[K, N] * s[K/128, N])  -- gemm_int4.int4_gemm
 // (gemm_int4.py:75-92) with group scales; q unpacked from Wp[K, N/2] with the
 // reference's nibble order (gemm_int4.py:43-50).
 //
 // Swap-AB: the weight tile is the MMA's M = 128 operand (128 output columns),
-// the activations its N = 16 operand (M padded to 16 by TMA zero fill), so
-// D[n, m] lives in 16 TMEM columns. One CTA owns 128 columns and a contiguous
+// the activations its N = NA operand (M padded to NA = 16 or 32 by TMA zero
+// fill), so D[n, m] lives in NA TMEM columns. One CTA owns 128 columns and a contiguous
 // range of 128-row K stages (one quantization group each). Warp roles:
 //   warps 0-3  epilogue: per group, read the fp32 partial D_g from TMEM and
 //              accumulate s[g, n] * D_g in registers (the scale is applied in
@@ -38,29 +38,36 @@ constexpr int kThreads = (kDeqWarp0 + kDeqWarps) * 32;  // 448
 
 constexpr int kBN = 128;      // output columns per CTA (MMA M)
 constexpr int kBK = 128;      // K rows per stage = one quantization group
-constexpr int kMmaN = 16;     // padded M (MMA N)
-constexpr int kSlots = 4;     // TMA stage ring
-constexpr int kDeqBufs = 3;   // ring of dequantized 64-row half stages
 constexpr int kGroupSlots = 8;                       // TMEM ring of per-group partials
-constexpr int kTmemCols = kGroupSlots * kMmaN;       // 128
 constexpr int kMaxClusterSplit = 8;
-
-// shared memory (bytes from a 1024-aligned base)
-constexpr int kAtileBytes = 2 * kMmaN * 128;         // two 64-column SW128 boxes: 4096
 constexpr int kWBytes = kBK * (kBN / 2);             // 128 rows x 64 B: 8192
-constexpr int kSlotBytes = kAtileBytes + kWBytes;    // 12288
-constexpr int kSlotA = 0;
-constexpr int kSlotW = kAtileBytes;
 constexpr int kDeqBytes = kBN * 64 * 2;              // 16384 per half stage
 constexpr int kDeqLBO = 8192;                        // between the two 64-column atoms
-constexpr int kDeqOff = kSlots * kSlotBytes;         // 49152
-constexpr int kBarOff = kDeqOff + kDeqBufs * kDeqBytes;  // 98304
-constexpr int kNumBars = 2 * kSlots + 2 * kDeqBufs + 2 * kGroupSlots;
-constexpr int kSmemBytes = kBarOff + kNumBars * 8 + 16 + 1024;
-constexpr int kRedOff = kDeqOff;                     // split-K partials reuse the dequant ring
+constexpr int kMaxNA = 32;
 
-static_assert(kMmaN * kBN * 4 <= kDeqBufs * kDeqBytes, "reduction buffer fits");
-static_assert(kSmemBytes <= 113 * 1024, "two CTAs per SM");
+// Per activation width NA (M padded to the MMA's N): 16 for M <= 16, 32 for
+// M <= 32. Shared memory from a 1024-aligned base: a ring of TMA slots (the
+// activation tile, then the packed weights), the dequantized half-stage ring,
+// barriers. NA = 16 keeps a 6-slot ring (2-6 % faster than 4 slots with 3
+// dequant buffers); NA = 32 keeps 4 so that two CTAs still share an SM.
+template <int NA>
+struct DecCfg {
+  static constexpr int kSlots = NA == 16 ? 6 : 4;
+  static constexpr int kDeqBufs = 2;
+  static constexpr int kTmemCols = kGroupSlots * NA;   // 128 / 256
+  static constexpr int kAtileBytes = 2 * NA * 128;     // two 64-column SW128 boxes
+  static constexpr int kSlotBytes = kAtileBytes + kWBytes;
+  static constexpr int kSlotA = 0;
+  static constexpr int kSlotW = kAtileBytes;
+  static constexpr int kDeqOff = kSlots * kSlotBytes;
+  static constexpr int kBarOff = kDeqOff + kDeqBufs * kDeqBytes;
+  static constexpr int kNumBars = 2 * kSlots + 2 * kDeqBufs + 2 * kGroupSlots;
+  static constexpr int kSmemBytes = kBarOff + kNumBars * 8 + 16 + 1024;
+  static constexpr int kRedOff = kDeqOff;              // split-K partials reuse the dequant ring
+  static_assert(NA * kBN * 4 <= kDeqBufs * kDeqBytes, "reduction buffer fits");
+  static_assert(kSmemBytes <= 113 * 1024, "two CTAs per SM");
+  static_assert(2 * kTmemCols <= 512, "two CTAs' TMEM fits an SM");
+};
 
 template <typename T>
 struct TypeFmt;
@@ -83,7 +90,7 @@ __device__ __forceinline__ void store_out(void* out, int out_dtype, int64_t idx,
     static_cast<float*>(out)[idx] = v;
 }
 
-template <typename T, bool kGrouped>
+template <typename T, bool kGrouped, int NA>
 __global__ void __launch_bounds__(kThreads, 2)
     w4a16_decode_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmW, const T* __restrict__ scales,
@@ -91,14 +98,15 @@ __global__ void __launch_bounds__(kThreads, 2)
                         void* __restrict__ out, int out_dtype, int64_t ldo,
                         float* __restrict__ partials, unsigned* __restrict__ sems,
                         int* __restrict__ status) {
+  using C = DecCfg<NA>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOff);
-  uint64_t* slot_empty = full + kSlots;
-  uint64_t* deq_full = slot_empty + kSlots;
-  uint64_t* deq_empty = deq_full + kDeqBufs;
-  uint64_t* tm_full = deq_empty + kDeqBufs;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* slot_empty = full + C::kSlots;
+  uint64_t* deq_full = slot_empty + C::kSlots;
+  uint64_t* deq_empty = deq_full + C::kDeqBufs;
+  uint64_t* tm_full = deq_empty + C::kDeqBufs;
   uint64_t* tm_empty = tm_full + kGroupSlots;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tm_empty + kGroupSlots);
   int* s_flag = reinterpret_cast<int*>(tmem_holder + 1);
@@ -114,11 +122,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int S = g_end - g_begin;
 
   if (warp == kTmaWarp && lane == 0) {
-    for (int i = 0; i < kSlots; ++i) {
+    for (int i = 0; i < C::kSlots; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&slot_empty[i], 1);
     }
-    for (int i = 0; i < kDeqBufs; ++i) {
+    for (int i = 0; i < C::kDeqBufs; ++i) {
       mbar_init(&deq_full[i], kDeqWarps);
       mbar_init(&deq_empty[i], 1);
     }
@@ -130,7 +138,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
   }
-  if (warp == kMmaWarp) tmem_alloc(tmem_holder, kTmemCols);
+  if (warp == kMmaWarp) tmem_alloc(tmem_holder, C::kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -147,38 +155,38 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       for (int s = 0; s < S && !fail; ++s) {
-        const int slot = s % kSlots;
-        if (s >= kSlots)
-          fail = !mbar_wait(&slot_empty[slot], ((s / kSlots) - 1) & 1, status, kSiteDecodeFull);
+        const int slot = s % C::kSlots;
+        if (s >= C::kSlots)
+          fail = !mbar_wait(&slot_empty[slot], ((s / C::kSlots) - 1) & 1, status, kSiteDecodeFull);
         if (fail) break;
-        uint8_t* base = smem + slot * kSlotBytes;
+        uint8_t* base = smem + slot * C::kSlotBytes;
         const int g = g_begin + s;
-        mbar_arrive_expect_tx(&full[slot], kSlotBytes);
-        tma_load_2d(base + kSlotW, &tmW, &full[slot], tile * (kBN / 2), g * kBK);
-        tma_load_2d(base + kSlotA, &tmA, &full[slot], g * kBK, 0);
-        tma_load_2d(base + kSlotA + kMmaN * 128, &tmA, &full[slot], g * kBK + 64, 0);
+        mbar_arrive_expect_tx(&full[slot], C::kSlotBytes);
+        tma_load_2d(base + C::kSlotW, &tmW, &full[slot], tile * (kBN / 2), g * kBK);
+        tma_load_2d(base + C::kSlotA, &tmA, &full[slot], g * kBK, 0);
+        tma_load_2d(base + C::kSlotA + NA * 128, &tmA, &full[slot], g * kBK + 64, 0);
         issued = s + 1;
       }
     }
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t kIdesc = make_idesc(TypeFmt<T>::kFmt, true, false, 128, kMmaN);
-      const uint32_t deq_base = smem_u32(smem + kDeqOff);
+      constexpr uint32_t kIdesc = make_idesc(TypeFmt<T>::kFmt, true, false, 128, NA);
+      const uint32_t deq_base = smem_u32(smem + C::kDeqOff);
       for (int s = 0; s < S && !fail; ++s) {
-        const int slot = s % kSlots;
+        const int slot = s % C::kSlots;
         const int gs = s % kGroupSlots;
         if (kGrouped && s >= kGroupSlots)
           fail = !mbar_wait(&tm_empty[gs], ((s / kGroupSlots) - 1) & 1, status, kSiteDecodeMma);
         for (int h = 0; h < 2 && !fail; ++h) {
           const int u = 2 * s + h;
-          const int buf = u % kDeqBufs;
-          fail = !mbar_wait(&deq_full[buf], (u / kDeqBufs) & 1, status, kSiteDecodeMma);
+          const int buf = u % C::kDeqBufs;
+          fail = !mbar_wait(&deq_full[buf], (u / C::kDeqBufs) & 1, status, kSiteDecodeMma);
           if (fail) break;
           tc_fence_after();
-          const uint32_t a_tile = smem_u32(smem + slot * kSlotBytes + kSlotA) + h * (kMmaN * 128);
+          const uint32_t a_tile = smem_u32(smem + slot * C::kSlotBytes + C::kSlotA) + h * (NA * 128);
           const uint32_t d_tile = deq_base + buf * kDeqBytes;
-          const uint32_t d_tmem = tmem + (kGrouped ? gs * kMmaN : 0);
+          const uint32_t d_tmem = tmem + (kGrouped ? gs * NA : 0);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const uint64_t adesc = make_smem_desc(d_tile + j * 2048, kDeqLBO, 1024);
@@ -207,17 +215,17 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int r8 = r & 7;
     const uint32_t row_off = (r >> 3) * 1024 + r8 * 128;
     for (int s = 0; s < S && !fail; ++s) {
-      const int slot = s % kSlots;
-      fail = !mbar_wait(&full[slot], (s / kSlots) & 1, status, kSiteDecodeFull);
+      const int slot = s % C::kSlots;
+      fail = !mbar_wait(&full[slot], (s / C::kSlots) & 1, status, kSiteDecodeFull);
       for (int h = 0; h < 2 && !fail; ++h) {
         const int u = 2 * s + h;
-        const int buf = u % kDeqBufs;
-        if (u >= kDeqBufs)
-          fail = !mbar_wait(&deq_empty[buf], ((u / kDeqBufs) - 1) & 1, status, kSiteDecodeMma);
+        const int buf = u % C::kDeqBufs;
+        if (u >= C::kDeqBufs)
+          fail = !mbar_wait(&deq_empty[buf], ((u / C::kDeqBufs) - 1) & 1, status, kSiteDecodeMma);
         if (fail) break;
-        const uint4 wv = *reinterpret_cast<const uint4*>(smem + slot * kSlotBytes + kSlotW +
+        const uint4 wv = *reinterpret_cast<const uint4*>(smem + slot * C::kSlotBytes + C::kSlotW +
                                                          (64 * h + r) * 64 + wq * 16);
-        uint8_t* dq = smem + kDeqOff + buf * kDeqBytes + row_off;
+        uint8_t* dq = smem + C::kDeqOff + buf * kDeqBytes + row_off;
         const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -235,9 +243,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 
   // ---------------- epilogue: per-group scale in fp32 ----------------
-  float acc[kMmaN];
+  float acc[NA];
 #pragma unroll
-  for (int m = 0; m < kMmaN; ++m) acc[m] = 0.0f;
+  for (int m = 0; m < NA; ++m) acc[m] = 0.0f;
   const int p = tid;  // TMEM lane (epilogue threads only)
   const int nl = (p & ~7) | int4_codes8_column(p & 7);
   const int64_t n = static_cast<int64_t>(tile) * kBN + nl;
@@ -253,24 +261,33 @@ __global__ void __launch_bounds__(kThreads, 2)
         fail = !mbar_wait(&tm_full[gs], (s / kGroupSlots) & 1, status, kSiteDecodeFinal);
         if (fail) break;
         tc_fence_after();
-        uint32_t raw[kMmaN];
-        tmem_ld_32x32b_x16(lane_base + gs * kMmaN, raw);
-        tmem_ld_wait();
+        // 16 columns at a time: 32 accumulators plus a 32-column load would
+        // not fit the 72 registers two CTAs per SM leave a thread
+#pragma unroll
+        for (int c = 0; c < NA / 16; ++c) {
+          uint32_t raw[16];
+          tmem_ld_32x32b_x16(lane_base + gs * NA + c * 16, raw);
+          tmem_ld_wait();
+#pragma unroll
+          for (int m = 0; m < 16; ++m)
+            acc[c * 16 + m] = fmaf(sc, __uint_as_float(raw[m]), acc[c * 16 + m]);
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tm_empty[gs]);
-#pragma unroll
-        for (int m = 0; m < kMmaN; ++m) acc[m] = fmaf(sc, __uint_as_float(raw[m]), acc[m]);
       }
     } else if (S > 0) {
       fail = !mbar_wait(&tm_full[0], 0, status, kSiteDecodeFinal);
       if (!fail) {
         tc_fence_after();
-        uint32_t raw[kMmaN];
-        tmem_ld_32x32b_x16(lane_base, raw);
-        tmem_ld_wait();
 #pragma unroll
-        for (int m = 0; m < kMmaN; ++m) acc[m] = __uint_as_float(raw[m]);
+        for (int c = 0; c < NA / 16; ++c) {
+          uint32_t raw[16];
+          tmem_ld_32x32b_x16(lane_base + c * 16, raw);
+          tmem_ld_wait();
+#pragma unroll
+          for (int m = 0; m < 16; ++m) acc[c * 16 + m] = __uint_as_float(raw[m]);
+        }
       }
     }
   }
@@ -278,10 +295,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   // ---------------- split-K reduction and output ----------------
   fail = __syncthreads_or(fail) != 0;
   if (use_cluster) {
-    float* red = reinterpret_cast<float*>(smem + kRedOff);
+    float* red = reinterpret_cast<float*>(smem + C::kRedOff);
     if (!fail && warp < kEpiWarps) {
 #pragma unroll
-      for (int m = 0; m < kMmaN; ++m)
+      for (int m = 0; m < NA; ++m)
         if (m < M) red[m * kBN + nl] = acc[m];
     }
     cluster_sync();
@@ -308,13 +325,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else if (split == 1) {
     if (!fail && warp < kEpiWarps) {
 #pragma unroll
-      for (int m = 0; m < kMmaN; ++m)
+      for (int m = 0; m < NA; ++m)
         if (m < M) store_out(out, out_dtype, m * ldo + n, acc[m] * scalar_scale);
     }
   } else if (!fail && warp < kEpiWarps) {
     float* mine = partials + (static_cast<int64_t>(tile) * split + ks) * M * kBN;
 #pragma unroll
-    for (int m = 0; m < kMmaN; ++m)
+    for (int m = 0; m < NA; ++m)
       if (m < M) __stcg(mine + m * kBN + nl, acc[m]);
     __threadfence();
     named_bar_sync(1, kEpiWarps * 32);
@@ -324,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       __threadfence();
       const float* tp = partials + static_cast<int64_t>(tile) * split * M * kBN;
 #pragma unroll
-      for (int m = 0; m < kMmaN; ++m) {
+      for (int m = 0; m < NA; ++m) {
         if (m < M) {
           // eight partials' loads in flight before the adds (split order kept)
           float sum = 0.0f;
@@ -350,11 +367,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (fail && warp == kTmaWarp && lane == 0) {
     // let copies already issued land before the CTA's shared memory is released
-    for (int s = 0; s < issued; ++s) mbar_wait(&full[s % kSlots], (s / kSlots) & 1, nullptr, 0);
+    for (int s = 0; s < issued; ++s) mbar_wait(&full[s % C::kSlots], (s / C::kSlots) & 1, nullptr, 0);
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
+  if (warp == kMmaWarp) tmem_dealloc(tmem, C::kTmemCols);
 }
 
 CUtensorMapDataType tmap_type(int dt) {
@@ -363,7 +380,7 @@ CUtensorMapDataType tmap_type(int dt) {
 
 // Whether a cluster of `split` CTAs of this kernel can be resident (cached per
 // device and split; 0 unknown, 1 yes, 2 no).
-template <typename Kern>
+template <int NA, typename Kern>
 bool cluster_fits(Kern kernel, int split) {
   static int cache[64][kMaxClusterSplit + 1] = {};
   int dev = 0;
@@ -373,7 +390,7 @@ bool cluster_fits(Kern kernel, int split) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1, split, 1);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.dynamicSmemBytes = DecCfg<NA>::kSmemBytes;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
     attr.val.clusterDim.x = 1;
@@ -394,7 +411,7 @@ bool cluster_fits(Kern kernel, int split) {
 
 bool decode_supported(int64_t M, int64_t N, int64_t K, int group, const void* scales,
                       int64_t lda, const void* a) {
-  if (M < 1 || M > kMmaN) return false;
+  if (M < 1 || M > kMaxNA) return false;
   if (N % kBN != 0 || K % kBK != 0) return false;
   if (N / kBN > kMaxCounters) return false;
   if (scales != nullptr && group != kBK) return false;
@@ -425,10 +442,14 @@ size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int split) {
   return kCounterBytes + static_cast<size_t>(tiles) * split * M * kBN * sizeof(float);
 }
 
-cudaError_t launch_w4a16_decode(const DecodeArgs& p, cudaStream_t s, const char** why) {
+namespace {
+
+template <int NA>
+cudaError_t launch_decode_na(const DecodeArgs& p, cudaStream_t s, const char** why) {
+  constexpr int kSmemBytes = DecCfg<NA>::kSmemBytes;
   CUtensorMap tmA, tmW;
   const CUtensorMapDataType dt = tmap_type(p.a_dtype);
-  if (!encode_tmap_2d(&tmA, dt, p.a, p.K, p.M, p.lda * 2, 64, kMmaN,
+  if (!encode_tmap_2d(&tmA, dt, p.a, p.K, p.M, p.lda * 2, 64, NA,
                       CU_TENSOR_MAP_SWIZZLE_128B, why))
     return cudaErrorInvalidValue;
   if (!encode_tmap_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.wp, p.N / 2, p.K, p.N / 2, kBN / 2,
@@ -442,7 +463,7 @@ cudaError_t launch_w4a16_decode(const DecodeArgs& p, cudaStream_t s, const char*
     if (e != cudaSuccess) return e;
     int use_cluster = 0;
     if (p.split > 1) {
-      if (p.split <= kMaxClusterSplit && !p.force_workspace && cluster_fits(kernel, p.split)) {
+      if (p.split <= kMaxClusterSplit && !p.force_workspace && cluster_fits<NA>(kernel, p.split)) {
         use_cluster = 1;
       } else if (p.partials == nullptr || p.sems == nullptr) {
         *why = "this split-K launch needs a workspace (cluster reduction unavailable)";
@@ -475,12 +496,19 @@ cudaError_t launch_w4a16_decode(const DecodeArgs& p, cudaStream_t s, const char*
   };
   if (p.a_dtype == PK_BF16) {
     auto sp = static_cast<const __nv_bfloat16*>(p.scales);
-    return grouped ? launch(w4a16_decode_kernel<__nv_bfloat16, true>, sp)
-                   : launch(w4a16_decode_kernel<__nv_bfloat16, false>, sp);
+    return grouped ? launch(w4a16_decode_kernel<__nv_bfloat16, true, NA>, sp)
+                   : launch(w4a16_decode_kernel<__nv_bfloat16, false, NA>, sp);
   }
   auto sp = static_cast<const __half*>(p.scales);
-  return grouped ? launch(w4a16_decode_kernel<__half, true>, sp)
-                 : launch(w4a16_decode_kernel<__half, false>, sp);
+  return grouped ? launch(w4a16_decode_kernel<__half, true, NA>, sp)
+                 : launch(w4a16_decode_kernel<__half, false, NA>, sp);
+}
+
+}  // namespace
+
+// M <= 16 on 16 activation columns, M <= 32 on 32 (the MMA's N).
+cudaError_t launch_w4a16_decode(const DecodeArgs& p, cudaStream_t s, const char** why) {
+  return p.M <= 16 ? launch_decode_na<16>(p, s, why) : launch_decode_na<32>(p, s, why);
 }
 
 }  // namespace pk

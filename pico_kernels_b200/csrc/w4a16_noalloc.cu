@@ -10,7 +10,7 @@
 // library keeps until the process exits.
 //
 // Contract:
-//   * decode shapes only (what pk_w4a16_gemm runs on its decode path: M <= 16,
+//   * decode shapes only (what pk_w4a16_gemm runs on its decode path: M <= 32,
 //     N % 128 == 0, K % 128 == 0, group 128 or a scalar scale);
 //   * the reduction scratch a call needs -- tiles * split * M * 128 fp32
 //     partials -- must fit kNoAllocPartialBytes (4 MiB) and the tile count
@@ -85,7 +85,7 @@ extern "C" PK_API int pk_w4a16_gemm_noalloc(const void* a, int a_dtype, int64_t 
   if (split_k < 0) return fail(PK_ERR_SHAPE, "split_k must be >= 0");
   if (!decode_supported(M, N, K, group_size, scales, lda, a))
     return fail(PK_ERR_UNSUPPORTED,
-                "no-alloc entry point covers decode shapes only (M <= 16, N % 128 == 0, "
+                "no-alloc entry point covers decode shapes only (M <= 32, N % 128 == 0, "
                 "K % 128 == 0, group 128 or scalar scale, 16-byte aligned A)");
   int split = split_k > 0 ? split_k : decode_pick_split(M, N, K);
   if (split > K / 128) split = static_cast<int>(K / 128);

@@ -40,7 +40,7 @@ def check(y: torch.Tensor, ref: np.ndarray, dt, what=""):
     return rel
 
 
-@pytest.mark.parametrize("M", [1, 4, 16])
+@pytest.mark.parametrize("M", [1, 4, 16, 17, 24, 32])
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
 def test_decode_4096(M, dt):
     a, w, ref = make_case(M, 4096, 4096, dt)
@@ -52,8 +52,9 @@ def test_decode_4096(M, dt):
 
 
 @pytest.mark.parametrize("split", [1, 2, 3, 8, 32])
-def test_decode_split_k_deterministic(split):
-    a, w, ref = make_case(4, 4096, 4096, torch.bfloat16, seed=3)
+@pytest.mark.parametrize("M", [4, 32])
+def test_decode_split_k_deterministic(split, M):
+    a, w, ref = make_case(M, 4096, 4096, torch.bfloat16, seed=3)
     packed, scales = pk.quantize_int4_grouped(w.cuda(), 128)
     a = a.cuda()
     y1 = pk.int4_gemm(a, packed, scales, split_k=split)
@@ -74,9 +75,13 @@ def test_decode_splits_agree():
 
 def test_decode_llama70b_shapes():
     for (N, K) in ((28672, 8192), (8192, 28672)):
-        a, w, ref = make_case(1, N, K, torch.bfloat16, seed=7)
+        a, w, ref = make_case(32, N, K, torch.bfloat16, seed=7)
         packed, scales = pk.quantize_int4_grouped(w.cuda(), 128)
-        check(pk.int4_gemm(a.cuda(), packed, scales), ref, torch.bfloat16, f"N={N} K={K}")
+        y = pk.int4_gemm(a.cuda(), packed, scales)             # M = 32: decode kernel
+        rel = check(y, ref, torch.bfloat16, f"N={N} K={K}")
+        assert rel < 1e-5, rel  # exact codes, fp32 scale after the MMA
+        y4 = pk.int4_gemm(a[:4].cuda(), packed, scales)        # M = 4
+        check(y4, ref[:4], torch.bfloat16, f"M=4 N={N} K={K}")
 
 
 def test_decode_bf16_output():
@@ -111,9 +116,10 @@ def test_ragged_shapes_generic_kernel(M, N, K, group):
     assert np.abs(yy - ref).max() <= 1e-4 * max(1.0, np.abs(ref).max())
 
 
-@pytest.mark.parametrize("M,N,K", [(20, 256, 384), (33, 96, 192)])
+@pytest.mark.parametrize("M,N,K", [(40, 256, 384), (33, 96, 192), (20, 192, 320)])
 def test_small_m_prefill_path(M, N, K):
-    """M > 16 with K % 64 == 0 takes the tensor-core prefill kernel (bf16 q*s)."""
+    """M > 32, or N / K not multiples of 128, with K % 64 == 0 takes the
+    tensor-core prefill kernel (bf16 q*s)."""
     a, w, ref = make_case(M, N, K, torch.bfloat16, seed=12)
     packed, scales = pk.quantize_int4_grouped(w.cuda(), 128)
     check(pk.int4_gemm(a.cuda(), packed, scales), ref, torch.bfloat16, f"M={M}")

@@ -66,6 +66,6 @@ def test_noalloc_rejects_requests_beyond_its_scratch():
 
 
 def test_noalloc_rejects_non_decode_shapes():
-    a, packed, scales = _case(32, 256, 512, seed=6)
-    out = torch.zeros((32, 256), dtype=torch.float32, device="cuda")
+    a, packed, scales = _case(40, 256, 512, seed=6)    # M > 32: not a decode shape
+    out = torch.zeros((40, 256), dtype=torch.float32, device="cuda")
     assert _noalloc(a, packed, scales, 0, out) == _lib.PK_ERR_UNSUPPORTED
