@@ -341,6 +341,34 @@ int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t* wp, co
     return PK_OK;
   }
 
+  // 32 < M <= 256 where it is faster (skinny_preferred): the swap-AB
+  // tensor-core kernel dequantizes every weight once, two CTAs per SM.
+  if (split_k == 0 && skinny_supported(M, N, K, group_size, scales, lda, a) &&
+      (reinterpret_cast<uintptr_t>(wp) & 15) == 0 && skinny_preferred(M, N, K)) {
+    DecodeArgs p{};
+    p.a = a;
+    p.lda = lda;
+    p.wp = wp;
+    p.scales = scales;
+    p.group = group_size;
+    p.scalar_scale = scales ? 1.0f : scalar_scale;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.out = out;
+    p.out_dtype = out_dtype;
+    p.ldo = ldo;
+    p.a_dtype = a_dtype;
+    p.split = 1;
+    p.status = device_status_ptr();
+    const char* why = "";
+    cudaError_t e = launch_w4a16_skinny(p, s, &why);
+    if (e == cudaErrorInvalidValue && why[0] != '\0') return fail(PK_ERR_ALIGN, "%s", why);
+    if (e != cudaSuccess) return cuda_fail(e, "w4a16 skinny launch");
+    ok();
+    return PK_OK;
+  }
+
   // Tensor-core prefill path: 64-row K stages, scales on 64-row boundaries.
   const bool prefill_ok = (K % 64) == 0 && (N % 64) == 0 && (lda % 8) == 0 &&
                           (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&

@@ -30,6 +30,9 @@ enum WaitSite : int {
   kSiteGemvProducer = 301,
   kSiteGemvConsumer = 302,
   kSiteGemvPeers = 303,
+  kSiteSkinnyFull = 401,
+  kSiteSkinnyMma = 402,
+  kSiteSkinnyFinal = 403,
 };
 
 // Host-side tensor map encoding (cuTensorMapEncodeTiled via the runtime's
@@ -107,6 +110,12 @@ bool decode_supported(int64_t M, int64_t N, int64_t K, int group, const void* sc
                       int64_t lda, const void* a);
 int decode_pick_split(int64_t M, int64_t N, int64_t K);
 size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int split);
+
+// ---- w4a16_skinny.cu (32 < M <= 256, swap-AB, weights dequantized once) ----
+bool skinny_supported(int64_t M, int64_t N, int64_t K, int group, const void* scales,
+                      int64_t lda, const void* a);
+bool skinny_preferred(int64_t M, int64_t N, int64_t K);
+cudaError_t launch_w4a16_skinny(const DecodeArgs& p, cudaStream_t s, const char** why);
 cudaError_t launch_w4a16_decode(const DecodeArgs& args, cudaStream_t s, const char** why);
 
 // ---- w4a16_gemv.cu (M <= 2 on the CUDA cores; cluster or stream-K split) -

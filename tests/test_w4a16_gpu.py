@@ -166,3 +166,58 @@ def test_prefill_dequant_once_per_tensor_scale():
     c = pk.int4_gemm(a, pk.pack_int4_n(w_q), scale)
     ref = a.float() @ (w_q.float() * scale)
     assert (torch.norm(c - ref) / torch.norm(ref)).item() < 1e-5
+
+
+@pytest.mark.parametrize("M,N,K", [(33, 1024, 2048), (64, 1024, 2048), (100, 1024, 2048),
+                                   (128, 1024, 2048), (129, 20480, 512), (200, 20480, 512),
+                                   (256, 20480, 512)])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_skinny_prefill_vs_oracle(M, N, K, dt):
+    """32 < M <= 256 on shapes where the swap-AB kernel is chosen (each weight
+    dequantized once, q*s rounded to A's dtype as in the prefill kernel):
+    activation widths 64, 128 and 256."""
+    a, w, ref = make_case(M, N, K, dt, seed=M)
+    packed, scales = pk.quantize_int4_grouped(w.cuda(), 128)
+    y = pk.int4_gemm(a.cuda(), packed, scales)
+    assert y.shape == (M, N)
+    check(y, ref, dt, f"M={M}")
+    # same operand values as the fused prefill kernel (split_k=1 skips this
+    # path): the two agree to fp32 summation order
+    y_pf = pk.int4_gemm(a.cuda(), packed, scales, split_k=1)
+    assert (torch.norm(y - y_pf) / torch.norm(y_pf)).item() < 1e-5
+    assert pk.device_status() == (0, 0)
+
+
+def test_skinny_prefill_variants():
+    """group 64, per-tensor scale, bf16 output, ldo > N through the C-ABI."""
+    a, w, ref = make_case(72, 512, 1024, torch.bfloat16, group=64, seed=77)
+    packed, scales = pk.quantize_int4_grouped(w.cuda(), 64)
+    check(pk.int4_gemm(a.cuda(), packed, scales, group_size=64), ref, torch.bfloat16, "g64")
+    yb = pk.int4_gemm(a.cuda(), packed, scales, group_size=64, out_dtype=torch.bfloat16)
+    assert yb.dtype == torch.bfloat16
+    assert torch.equal(yb, pk.int4_gemm(a.cuda(), packed, scales, group_size=64).to(torch.bfloat16))
+    torch.manual_seed(2)
+    a2 = torch.randn(96, 512, device="cuda", dtype=torch.float16)
+    w2 = torch.randn(512, 256, device="cuda", dtype=torch.float16)
+    w_q, scale = pk.quantize_int4(w2)
+    c = pk.int4_gemm(a2, pk.pack_int4_n(w_q), scale)
+    ref2 = a2.float() @ (w_q.float() * scale)
+    assert (torch.norm(c - ref2) / torch.norm(ref2)).item() < 1e-5
+    from pico_kernels_b200 import _lib as L
+    lib = L.load()
+    a3, w3, ref3 = make_case(48, 256, 512, torch.bfloat16, seed=78)
+    p3, s3 = pk.quantize_int4_grouped(w3.cuda(), 128)
+    a3 = a3.cuda()
+    out = torch.full((48, 320), 5.0, device="cuda")
+    rc = lib.pk_w4a16_gemm(L.ptr(a3), L.PK_BF16, 512, L.ptr(p3), L.ptr(s3), 1.0, 128, 48, 256, 512,
+                           L.ptr(out), L.PK_F32, 320, 0, None, 0,
+                           torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, L.last_error()
+    check(out[:, :256], ref3, torch.bfloat16, "ldo")
+    assert torch.all(out[:, 256:] == 5.0)
+
+
+def test_skinny_prefill_llama70b_m256():
+    a, w, ref = make_case(256, 28672, 8192, torch.bfloat16, seed=79)
+    packed, scales = pk.quantize_int4_grouped(w.cuda(), 128)
+    check(pk.int4_gemm(a.cuda(), packed, scales), ref, torch.bfloat16, "70B up M=256")
