@@ -121,7 +121,10 @@ PK_API size_t pk_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int split
  * large layers it splits K over the SMs and reduces through the workspace,
  * and without one it falls back to the tensor-core decode kernel, which
  * serves the other shapes up to M = 32 (N and K multiples of 128, group 128
- * or a scalar scale); larger M runs the tcgen05 prefill kernel. From
+ * or a scalar scale). For 32 < M <= 256 (N % 128 == 0, K % 64 == 0) a
+ * swap-AB tensor-core kernel that dequantizes each weight once runs where a
+ * model of measured per-stage times favours it over the tcgen05 prefill
+ * kernel, which serves the rest. From
  * M = 1024 the weights are dequantized once into the workspace (16-bit
  * B[K, N] after the counters, pk_w4a16_workspace_size bytes) and the dense
  * tensor-core GEMM runs on it; without that workspace the fused kernel runs.
