@@ -84,6 +84,9 @@ _lock = threading.Lock()
 def load(path: Path | str | None = None) -> ctypes.CDLL:
     """Load (once) and return the shared library; raise if it is missing."""
     global _lib
+    lib = _lib
+    if lib is not None:  # every call after the first: no lock on the hot path
+        return lib
     with _lock:
         if _lib is None:
             p = Path(path) if path else LIB_PATH
@@ -127,7 +130,15 @@ def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+# torch's raw current-stream query (an int, no Stream object), when present;
+# the public call below is the fallback and gives the same handle.
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_of(t: torch.Tensor) -> int:
+    """Handle of the current CUDA stream of ``t``'s device."""
+    if _raw_stream is not None:
+        return _raw_stream(t.get_device())
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
@@ -152,11 +163,16 @@ def device_status(reset: bool = True) -> tuple[int, int]:
 _workspaces: dict[tuple[int, int, str], torch.Tensor] = {}
 
 
-def workspace(device: torch.device, nbytes: int, tag: str = "splitk") -> torch.Tensor | None:
+def workspace(device: torch.device, nbytes: int, tag: str = "splitk",
+              stream: int | None = None) -> torch.Tensor | None:
+    """The cached workspace of at least ``nbytes`` for (device, stream, tag);
+    ``stream`` is the current stream's handle when the caller has it."""
     if nbytes == 0:
         return None
-    key = (device.index if device.index is not None else torch.cuda.current_device(),
-           torch.cuda.current_stream(device).cuda_stream, tag)
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    if stream is None:
+        stream = torch.cuda.current_stream(device).cuda_stream
+    key = (index, stream, tag)
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)

@@ -130,7 +130,8 @@ def int4_gemm(a: torch.Tensor, w_packed: torch.Tensor, scale,
     N = 2 * N_half
     if a.stride(1) != 1 or a.stride(0) < K:
         a = a.contiguous()
-    w_packed = w_packed.contiguous()
+    if not w_packed.is_contiguous():
+        w_packed = w_packed.contiguous()
 
     scales = None
     scalar = 1.0
@@ -147,16 +148,27 @@ def int4_gemm(a: torch.Tensor, w_packed: torch.Tensor, scale,
         if group <= 0 or (K + group - 1) // group != G:
             raise _lib.ShapeError(f"{G} scale rows do not tile K={K} with group_size={group}")
         scales = scale if scale.dtype == a.dtype else scale.to(a.dtype)
-        scales = scales.contiguous()
+        if not scales.is_contiguous():
+            scales = scales.contiguous()
     else:
         scalar = float(scale)
 
     out = torch.empty((M, N), dtype=out_dtype, device=a.device)
     lib = _lib.load()
-    ws_bytes = lib.pk_w4a16_workspace_size(M, N, K, split_k)
-    ws = _lib.workspace(a.device, ws_bytes)
-    _lib.check(lib.pk_w4a16_gemm(
+    key = (M, N, K, split_k)
+    ws_bytes = _ws_bytes.get(key)
+    if ws_bytes is None:
+        ws_bytes = _ws_bytes[key] = lib.pk_w4a16_workspace_size(M, N, K, split_k)
+    stream = _lib.stream_of(a)
+    ws = _lib.workspace(a.device, ws_bytes, stream=stream) if ws_bytes else None
+    st = lib.pk_w4a16_gemm(
         a.data_ptr(), _lib.dtype_code(a.dtype), a.stride(0), w_packed.data_ptr(),
         _lib.ptr(scales), scalar, group, M, N, K, out.data_ptr(), _lib.dtype_code(out_dtype), N,
-        split_k, _lib.ptr(ws), ws_bytes, _lib.stream_of(a)), "int4_gemm")
+        split_k, _lib.ptr(ws), ws_bytes, stream)
+    if st:
+        _lib.check(st, "int4_gemm")
     return out
+
+
+# pk_w4a16_workspace_size per (M, N, K, split_k): a pure function of the shape
+_ws_bytes: dict[tuple[int, int, int, int], int] = {}
