@@ -5,6 +5,8 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <utility>
+#include <vector>
 
 #include "pk_internal.h"
 
@@ -108,9 +110,72 @@ size_t prefill_workspace_bytes(int64_t N, int64_t K) {
   return kCounterBytes + static_cast<size_t>(K) * static_cast<size_t>(N) * 2;
 }
 
+namespace {
+
+// Encoded maps of recent calls, per host thread: a decode loop calls the same
+// layers with the same buffers, and a map depends only on these fields (the
+// address, the tensor's shape and stride, the box and the swizzle), so equal
+// fields give an equal map and the driver call can be skipped.
+struct TmapKey {
+  uint64_t base, inner, outer, stride;
+  uint32_t dtype, box_inner, box_outer, swizzle;
+  bool operator==(const TmapKey& o) const {
+    return base == o.base && inner == o.inner && outer == o.outer && stride == o.stride &&
+           dtype == o.dtype && box_inner == o.box_inner && box_outer == o.box_outer &&
+           swizzle == o.swizzle;
+  }
+};
+constexpr int kTmapCache = 32;
+struct TmapCache {
+  TmapKey key[kTmapCache];
+  CUtensorMap map[kTmapCache];
+  int used = 0, next = 0;
+};
+thread_local TmapCache tmap_cache;
+
+}  // namespace
+
+cudaError_t set_max_smem(const void* kernel, int bytes) {
+  // kernel -> (bytes, bit per device already set): the attribute persists in
+  // the device's context, so later launches skip the runtime call
+  static std::mutex mu;
+  static std::vector<std::pair<const void*, std::pair<int, uint64_t>>> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+  const uint64_t bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (auto& d : done)
+      if (d.first == kernel && d.second.first >= bytes && (d.second.second & bit) != 0)
+        return cudaSuccess;
+  }
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess || bit == 0) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  for (auto& d : done) {
+    if (d.first == kernel) {
+      if (d.second.first != bytes) d.second = {bytes, 0};
+      d.second.second |= bit;
+      return e;
+    }
+  }
+  done.push_back({kernel, {bytes, bit}});
+  return e;
+}
+
 bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
                     uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                     uint32_t box_outer, CUtensorMapSwizzle swizzle, const char** why) {
+  const TmapKey key{reinterpret_cast<uint64_t>(base), inner, outer, row_stride_bytes,
+                    static_cast<uint32_t>(dtype), box_inner, box_outer,
+                    static_cast<uint32_t>(swizzle)};
+  TmapCache& c = tmap_cache;
+  for (int i = 0; i < c.used; ++i) {
+    if (c.key[i] == key) {
+      *map = c.map[i];
+      return true;
+    }
+  }
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) {
     *why = "cuTensorMapEncodeTiled unavailable";
@@ -127,6 +192,9 @@ bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* bas
     *why = "cuTensorMapEncodeTiled rejected the operand (alignment or box)";
     return false;
   }
+  const int slot = c.used < kTmapCache ? c.used++ : (c.next++ % kTmapCache);
+  c.key[slot] = key;
+  c.map[slot] = *map;
   return true;
 }
 

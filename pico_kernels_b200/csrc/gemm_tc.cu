@@ -742,7 +742,7 @@ cudaError_t launch_typed(const GemmArgs& g, cudaStream_t s, const char** why) {
   const int units = p.num_m * p.num_n * p.split;
   const int grid = units < num_sms() ? units : num_sms();
   auto kernel = gemm_tc_kernel<kKind, kInt4>;
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  cudaError_t e = set_max_smem(reinterpret_cast<const void*>(kernel), C::kSmem);
   if (e != cudaSuccess) return e;
   kernel<<<grid, C::kThreads, C::kSmem, s>>>(tmA, tmB, tmS, p);
   return cudaGetLastError();
@@ -806,7 +806,7 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t s, const char** why) {
   p.a_is_f16 = g.a_dtype == PK_F16;
   p.status = g.status;
   auto kernel = gemm_pair_kernel<kKind>;
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  cudaError_t e = set_max_smem(reinterpret_cast<const void*>(kernel), C::kSmem);
   if (e != cudaSuccess) return e;
   const int units = p.num_m * p.num_n;
   const int slots = pair_slots<kKind>(s);

@@ -43,6 +43,10 @@ bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* bas
 
 int num_sms();  // SM count of the current device (cached)
 
+// cudaFuncSetAttribute(kernel, MaxDynamicSharedMemorySize, bytes) once per
+// kernel and device; later calls return without the runtime call.
+cudaError_t set_max_smem(const void* kernel, int bytes);
+
 // W4A16 with large M: dequantize the weights once into a 16-bit workspace
 // B[K, N] (prefill_workspace_bytes) and run the dense tensor-core GEMM.
 bool prefill_dequant_once(int64_t M, int64_t N, int64_t K);

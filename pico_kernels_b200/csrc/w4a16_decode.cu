@@ -459,7 +459,7 @@ cudaError_t launch_decode_na(const DecodeArgs& p, cudaStream_t s, const char** w
 
   auto launch = [&](auto kernel, auto scales_ptr) -> cudaError_t {
     cudaError_t e =
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        set_max_smem(reinterpret_cast<const void*>(kernel), kSmemBytes);
     if (e != cudaSuccess) return e;
     int use_cluster = 0;
     if (p.split > 1) {

@@ -622,7 +622,7 @@ cudaError_t launch_w4a16_gemv(const DecodeArgs& a, cudaStream_t s, const char** 
 
   auto launch = [&](auto kernel, int smem_bytes) -> cudaError_t {
     cudaError_t e =
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+        set_max_smem(reinterpret_cast<const void*>(kernel), smem_bytes);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(G), 1, 1);

@@ -267,7 +267,7 @@ cudaError_t launch_skinny_na(const DecodeArgs& p, cudaStream_t s, const char** w
     tmS = tmW;  // unused
   }
   auto launch = [&](auto kernel) -> cudaError_t {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    cudaError_t e = set_max_smem(reinterpret_cast<const void*>(kernel), kSmem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(p.N / kBN), 1, 1);
