@@ -57,7 +57,7 @@ struct Cfg {
   static constexpr int kWTile = kInt4 ? kBK * (kBN / 2) : 0;  // 8 / 4 KB
   static constexpr int kSRows = kBN / 64;                     // scale rows of 64 (128 B)
   static constexpr int kSTile = kInt4 ? kBN * 2 : 0;          // 512 / 256 B
-  static constexpr int kStages = 4;
+  static constexpr int kStages = kInt4 ? 6 : 4;        // int4: 6 x 25 KB (+2-4 % over 4)
   static constexpr int kBBufs = kInt4 ? 2 : 0;                // dequantized B ring
   static constexpr int kStageBytes = kATile + (kInt4 ? kWTile + 1024 : kBTile);
   static constexpr int kStageOff = 0;
