@@ -89,6 +89,8 @@ struct Params {
   int* status;
   const float* scale_a;  // fp8 with device scales: out_scale = 1 / (*scale_a * *scale_b)
   const float* scale_b;
+  int whole;             // pair kernel: units that are whole tiles; each later tile is two
+                         // units of half its columns (the last wave's tail), 16-bit kinds
 };
 
 // The epilogue multiplier: the host's out_scale, or, for scales that live on
@@ -530,9 +532,24 @@ struct PairCfg {
   static constexpr int kAccCols = kBN;
   static constexpr uint32_t kIdesc = make_idesc(kKind == kF16 ? 1u : 0u, false, true, 256, kBN);
   static constexpr uint32_t kIdescF16 = make_idesc(0u, false, true, 256, kBN);
+  // half-width units (N = 128: 64 columns, one 16-bit swizzle atom, per CTA)
+  static constexpr uint32_t kIdescHalf = make_idesc(kKind == kF16 ? 1u : 0u, false, true, 256, kBN / 2);
+  static constexpr uint32_t kIdescHalfF16 = make_idesc(0u, false, true, 256, kBN / 2);
   static_assert(2 * kAccCols <= 512, "two accumulator sets fit TMEM");
   static_assert(kSmem <= 227 * 1024, "shared memory");
 };
+
+// Pair-schedule unit u: whole tile u, or half `half` (0: columns 0-127, 1:
+// 128-255) of tile whole + (u - whole) / 2.
+__device__ __forceinline__ void pair_unit(int u, const Params& p, int& tile, int& half) {
+  if (u < p.whole) {
+    tile = u;
+    half = -1;
+  } else {
+    tile = p.whole + ((u - p.whole) >> 1);
+    half = (u - p.whole) & 1;
+  }
+}
 
 template <int kKind>
 __global__ void __launch_bounds__(PairCfg<kKind>::kThreads, 1)
@@ -552,7 +569,7 @@ __global__ void __launch_bounds__(PairCfg<kKind>::kThreads, 1)
   const uint32_t rank = cluster_ctarank();
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int k_tiles = (p.K + C::kBK - 1) / C::kBK;
-  const int num_units = p.num_m * p.num_n;
+  const int num_units = p.whole + 2 * (p.num_m * p.num_n - p.whole);
 
   if (warp == kTmaWarp && lane == 0) {
     for (int i = 0; i < C::kStages; ++i) {
@@ -581,10 +598,15 @@ __global__ void __launch_bounds__(PairCfg<kKind>::kThreads, 1)
       const uint32_t full0 = cluster_map(smem_u32(&full[0]), 0);
       int it = 0;
       for (int u = pair; u < num_units && !fail; u += npairs) {
-        int tm, tn, ks;
-        tile_coords(u, p, tm, tn, ks);
+        int tile, half, tm, tn, ks;
+        pair_unit(u, p, tile, half);
+        tile_coords(tile, p, tm, tn, ks);
         const int row = tm * C::kBM + static_cast<int>(rank) * C::kHalfM;
-        const int col = tn * C::kBN + static_cast<int>(rank) * C::kHalfN;
+        // whole tile: this CTA's 128 columns; half unit: its 64 of the half's 128
+        const int col = half < 0 ? tn * C::kBN + static_cast<int>(rank) * C::kHalfN
+                                 : tn * C::kBN + half * (C::kBN / 2) + static_cast<int>(rank) * (C::kHalfN / 2);
+        const int boxes = half < 0 ? C::kBBoxes : C::kBBoxes / 2;
+        const uint32_t tx = 2u * (C::kATile + boxes * (C::kBTile / C::kBBoxes));
         for (int kt = 0; kt < k_tiles && !fail; ++kt, ++it) {
           const int st = it % C::kStages;
           if (it >= C::kStages)
@@ -592,11 +614,10 @@ __global__ void __launch_bounds__(PairCfg<kKind>::kThreads, 1)
           if (fail) break;
           uint8_t* base = smem + st * C::kStageBytes;
           const uint32_t bar = full0 + st * 8;
-          if (rank == 0) mbar_arrive_expect_tx(&full[st], 2 * C::kStageBytes);
+          if (rank == 0) mbar_arrive_expect_tx(&full[st], tx);
           const int k0 = kt * C::kBK;
           tma_load_2d_pair(base, &tmA, bar, k0, row);
-#pragma unroll
-          for (int b = 0; b < C::kBBoxes; ++b)
+          for (int b = 0; b < boxes; ++b)
             tma_load_2d_pair(base + C::kATile + b * C::kBLBO, &tmB, bar, col + b * C::kBAtomN, k0);
         }
       }
@@ -606,6 +627,10 @@ __global__ void __launch_bounds__(PairCfg<kKind>::kThreads, 1)
     if (rank == 0 && lane == 0) {
       int it = 0, local = 0;
       for (int u = pair; u < num_units && !fail; u += npairs, ++local) {
+        int tile, half;
+        pair_unit(u, p, tile, half);
+        const uint32_t idesc = half < 0 ? (p.a_is_f16 ? C::kIdescF16 : C::kIdesc)
+                                        : (p.a_is_f16 ? C::kIdescHalfF16 : C::kIdescHalf);
         const int ab = local & 1;
         if (local >= 2)
           fail = !mbar_wait_cluster(&acc_empty[ab], ((local >> 1) - 1) & 1, p.status, kSiteGemmMma);
@@ -625,11 +650,9 @@ __global__ void __launch_bounds__(PairCfg<kKind>::kThreads, 1)
             const uint64_t bd = make_smem_desc(b_base + s * C::kBStepBytes, C::kBLBO, 1024);
             const uint32_t acc = (kt > 0 || s > 0) ? 1u : 0u;
             if (kKind == kF8)
-              umma_f8_pair(d_tmem, ad, bd, C::kIdesc, acc);
-            else if (p.a_is_f16)
-              umma_f16_pair(d_tmem, ad, bd, C::kIdescF16, acc);
+              umma_f8_pair(d_tmem, ad, bd, idesc, acc);
             else
-              umma_f16_pair(d_tmem, ad, bd, C::kIdesc, acc);
+              umma_f16_pair(d_tmem, ad, bd, idesc, acc);
           }
           umma_commit_pair(&empty[st]);
         }
@@ -644,8 +667,9 @@ __global__ void __launch_bounds__(PairCfg<kKind>::kThreads, 1)
     const float out_scale = epilogue_scale(p);
     int local = 0;
     for (int u = pair; u < num_units && !fail; u += npairs, ++local) {
-      int tm, tn, ks;
-      tile_coords(u, p, tm, tn, ks);
+      int tile, half, tm, tn, ks;
+      pair_unit(u, p, tile, half);
+      tile_coords(tile, p, tm, tn, ks);
       const int ab = local & 1;
       fail = !mbar_wait(&acc_full[ab], (local >> 1) & 1, p.status, kSiteGemmEpilogue);
       if (fail) break;
@@ -654,9 +678,10 @@ __global__ void __launch_bounds__(PairCfg<kKind>::kThreads, 1)
           static_cast<int64_t>(tm) * C::kBM + static_cast<int>(rank) * C::kHalfM + q * 32 + lane;
       const bool row_ok = row < p.M;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + ab * C::kAccCols;
-      const int col0 = tn * C::kBN;
+      const int col0 = tn * C::kBN + (half < 0 ? 0 : half * (C::kBN / 2));
+      const int ncols = half < 0 ? C::kBN : C::kBN / 2;
 #pragma unroll 1
-      for (int c = 0; c < C::kBN / 32; ++c) {
+      for (int c = 0; c < ncols / 32; ++c) {
         uint32_t raw[32];
         tmem_ld_32x32b_x32(taddr + c * 32, raw);
         tmem_ld_wait();
@@ -808,8 +833,16 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t s, const char** why) {
   auto kernel = gemm_pair_kernel<kKind>;
   cudaError_t e = set_max_smem(reinterpret_cast<const void*>(kernel), C::kSmem);
   if (e != cudaSuccess) return e;
-  const int units = p.num_m * p.num_n;
+  const int tiles = p.num_m * p.num_n;
   const int slots = pair_slots<kKind>(s);
+  // A partial last wave of 16-bit tiles runs as half-width units (two per
+  // tile, 64 columns per CTA: one swizzle atom) when they still fit one wave,
+  // so it takes about half a tile's time. 8-bit B halves would be narrower
+  // than a 128-byte swizzle atom: fp8 keeps whole tiles.
+  p.whole = tiles;
+  const int tail = tiles % slots;
+  if (kKind == kF16 && tiles > slots && tail > 0 && 2 * tail <= slots) p.whole = tiles - tail;
+  const int units = p.whole + 2 * (tiles - p.whole);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attrs[2];
   attrs[0].id = cudaLaunchAttributeClusterDimension;
