@@ -187,6 +187,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
                    const __grid_constant__ CUtensorMap tmS, const Params p) {
   using C = Cfg<kKind, kInt4>;
   constexpr int BM = C::kBM, BN = C::kBN;
+  constexpr int kBBufs = C::kBBufs > 0 ? C::kBBufs : 1;  // divisor for the int4-only paths
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -279,8 +280,8 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
           fail = !mbar_wait(&full[st], (it / C::kStages) & 1, p.status, kSiteGemmMma);
           int bb = 0;
           if (kInt4 && !fail) {
-            bb = bit % C::kBBufs;
-            fail = !mbar_wait(&bfull[bb], (bit / C::kBBufs) & 1, p.status, kSiteGemmMma);
+            bb = bit % kBBufs;
+            fail = !mbar_wait(&bfull[bb], (bit / kBBufs) & 1, p.status, kSiteGemmMma);
           }
           if (fail) break;
           tc_fence_after();
@@ -426,10 +427,10 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
       const int kt0 = (ks * k_tiles_total) / p.split, kt1 = ((ks + 1) * k_tiles_total) / p.split;
       for (int kt = kt0; kt < kt1 && !fail; ++kt, ++it, ++bit) {
         const int st = it % C::kStages;
-        const int bb = bit % C::kBBufs;
+        const int bb = bit % kBBufs;
         fail = !mbar_wait(&full[st], (it / C::kStages) & 1, p.status, kSiteGemmDequant);
         if (!fail && bit >= C::kBBufs)
-          fail = !mbar_wait(&bempty[bb], ((bit / C::kBBufs) - 1) & 1, p.status, kSiteGemmDequant);
+          fail = !mbar_wait(&bempty[bb], ((bit / kBBufs) - 1) & 1, p.status, kSiteGemmDequant);
         if (fail) break;
         const uint8_t* stage = smem + C::kStageOff + st * C::kStageBytes;
         const uint8_t* sc = stage + C::kATile + C::kWTile;
