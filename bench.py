@@ -364,11 +364,19 @@ class Workload:
             a_host.copy_(self.sets[0][0])
             a_dev = torch.empty((M, K), dtype=torch.bfloat16, device=self.device)
 
+            # single GPU: the output buffer is reused across steps (int4_gemm's
+            # out=), as a decode loop would; sharded: the exchange's or NCCL's
+            y_dev = (torch.empty((M, N), dtype=torch.float32, device=self.device)
+                     if world == 1 else None)
+
             def fn(i):
                 _, packed, scales = self.sets[i % self.n_sets]
                 a_dev.copy_(a_host, non_blocking=True)
-                y = sharded.sharded_int4_gemm(a_dev, packed, scales, 128, world,
-                                              exchange=self.exchange)
+                if y_dev is not None:
+                    y = pk.int4_gemm(a_dev, packed, scales, group_size=128, out=y_dev)
+                else:
+                    y = sharded.sharded_int4_gemm(a_dev, packed, scales, 128, world,
+                                                  exchange=self.exchange)
                 y_host.copy_(y, non_blocking=True)
             return fn, M * K * 2, M * N * 4
         if self.kind == "dense":

@@ -107,13 +107,15 @@ def quantize_int4_grouped(w: torch.Tensor, group_size: int = 128,
 def int4_gemm(a: torch.Tensor, w_packed: torch.Tensor, scale,
               BLOCK_M: int = 64, BLOCK_N: int = 64, BLOCK_K: int = 64, *,
               group_size: int | None = None, out_dtype: torch.dtype = torch.float32,
-              split_k: int = 0) -> torch.Tensor:
+              split_k: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
     """``a @ (W_int4 * scale)`` where ``w_packed`` is ``(K, N//2)`` uint8.
 
     ``scale``: the reference's per-tensor float, or a ``[G, N]`` tensor of
     group scales (``group_size`` defaults to ``K // G``). ``BLOCK_*`` are
     accepted for signature compatibility; the tile shape is fixed by the
-    sm_100a kernels. Output fp32 (or ``out_dtype=torch.bfloat16``).
+    sm_100a kernels. Output fp32 (or ``out_dtype=torch.bfloat16``), written to
+    ``out`` when given (a contiguous ``[M, N]`` tensor of ``out_dtype`` on
+    ``a``'s device; a decode loop reuses it instead of allocating per call).
     """
     del BLOCK_M, BLOCK_N, BLOCK_K
     _lib.require_cuda(a, w_packed)
@@ -153,7 +155,12 @@ def int4_gemm(a: torch.Tensor, w_packed: torch.Tensor, scale,
     else:
         scalar = float(scale)
 
-    out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    elif (out.shape != (M, N) or out.dtype != out_dtype or out.device != a.device
+          or not out.is_contiguous()):
+        raise _lib.ShapeError(f"out must be a contiguous [{M}, {N}] {out_dtype} tensor on "
+                              f"{a.device}")
     lib = _lib.load()
     key = (M, N, K, split_k)
     ws_bytes = _ws_bytes.get(key)

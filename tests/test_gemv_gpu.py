@@ -148,3 +148,19 @@ def test_workspace_shared_across_kernels():
         rel3 = np.linalg.norm(y3.cpu().numpy() - ref3) / np.linalg.norm(ref3)
         assert rel3 < 5e-3
     assert pk.device_status() == (0, 0)
+
+
+def test_out_parameter_reuses_the_buffer():
+    """int4_gemm(out=...) writes into the given buffer (no allocation) and
+    rejects one of the wrong shape, dtype or layout."""
+    a, packed, scales, ref = make_case(1, 4096, 4096, seed=61)
+    buf = torch.full((1, 4096), 3.0, device="cuda")
+    y = pk.int4_gemm(a, packed, scales, out=buf)
+    assert y is buf
+    assert torch.equal(buf, pk.int4_gemm(a, packed, scales))
+    check_tight(buf, ref)
+    for bad in (torch.empty(2, 4096, device="cuda"),
+                torch.empty(1, 4096, device="cuda", dtype=torch.bfloat16),
+                torch.empty(4096, 2, device="cuda").t()):
+        with pytest.raises(AssertionError):
+            pk.int4_gemm(a, packed, scales, out=bad)
