@@ -203,11 +203,14 @@ class Workload:
     step that runs one GEMM on set i through the C ABI.
 
     Sharded workloads: every rank builds the same seeded layer and keeps its
-    contiguous slice of N columns; a step is the local GEMM, then the NCCL
-    all-gather of the [M, N/p] blocks into [M, N] (reordered for M > 1)."""
+    contiguous slice of N columns; a step is one kernel per rank that also
+    writes every rank's output (the fused exchange), or, where no kernel with
+    the exchange covers the shape or ``exchange`` is False, the local GEMM
+    then the NCCL all-gather of the [M, N/p] blocks into [M, N] (reordered for
+    M > 1)."""
 
     def __init__(self, name: str, wl: dict, device: torch.device, split_k: int,
-                 world: int = 1, rank: int = 0, dist=None):
+                 world: int = 1, rank: int = 0, dist=None, exchange: bool = True):
         from pico_kernels_b200 import _lib
         self.name, self.wl, self.device = name, wl, device
         self.lib = _lib.load()
@@ -271,20 +274,26 @@ class Workload:
         self.ws_bytes = (self.lib.pk_w4a16_workspace_size(M, self.NL, K, split_k)
                          if self.kind == "w4a16" else 0)
         self.ws = _lib.workspace(device, self.ws_bytes, tag="bench")
-        # M = 1 sharded layers: the GEMV writes every rank's output itself
+        # sharded W4A16 layers whose local kernel is the GEMV, the decode or
+        # the skinny kernel: it writes every rank's output itself
+        # (pk_w4a16_gemm_sharded); one probe call per rank decides, and every
+        # rank gets the same answer (the kernel choice depends on the shape only)
         self.exchange = None
-        if self.sharded and self.world > 1 and self.kind == "w4a16" and split_k == 0:
+        if (exchange and self.sharded and self.world > 1 and self.kind == "w4a16"
+                and split_k == 0 and M <= 256):
             from pico_kernels_b200 import sharded
-            if M == 1:  # the GEMV's shape (pk_w4a16_gemm_sharded covers it)
-                self.exchange = sharded.PeerExchange(max_m=M, n_full=N, dtype=self.out_dtype)
-                ex = self.exchange
-                self.ex_ws_bytes = max(self.lib.pk_w4a16_workspace_size(M, self.NL, K, 0), 1 << 16)
-                self.ex_ws = _lib.workspace(device, self.ex_ws_bytes, tag="exchange")
-                import ctypes
-                self.ex_outs = [(ctypes.c_uint64 * self.world)(*[b + par * ex.buf_bytes for b in ex.bases])
-                                for par in (0, 1)]
-                self.ex_flags = (ctypes.c_uint64 * self.world)(*[b + ex.flag_off for b in ex.bases])
-                self.ex_calls = 0
+            self.exchange = sharded.PeerExchange(max_m=M, n_full=N, dtype=self.out_dtype)
+            ex = self.exchange
+            self.ex_ws_bytes = max(self.lib.pk_w4a16_workspace_size(M, self.NL, K, 0), 1 << 16)
+            self.ex_ws = _lib.workspace(device, self.ex_ws_bytes, tag="exchange")
+            import ctypes
+            self.ex_outs = [(ctypes.c_uint64 * self.world)(*[b + par * ex.buf_bytes for b in ex.bases])
+                            for par in (0, 1)]
+            self.ex_flags = (ctypes.c_uint64 * self.world)(*[b + ex.flag_off for b in ex.bases])
+            self.ex_calls = 0
+            if self.fused_call(0) == _lib.PK_ERR_UNSUPPORTED:
+                ex.close()  # collective, like the constructor
+                self.exchange = None
         torch.cuda.synchronize()
 
     def gemm(self, i: int) -> torch.Tensor:
@@ -313,7 +322,7 @@ class Workload:
             self.full.copy_(self.gather.view(self.world, self.M, self.NL).permute(1, 0, 2)
                             .reshape(self.M, self.N))
 
-    def fused_step(self, i: int) -> None:
+    def fused_call(self, i: int) -> int:
         import ctypes
         lib, L, M, K, NL = self.lib, self._lib, self.M, self.K, self.NL
         a, packed, scales = self.sets[i]
@@ -324,7 +333,12 @@ class Workload:
             self.out_code, self.N, self.rank * NL, self.world, self.rank, ctypes.addressof(outs),
             ctypes.addressof(self.ex_flags), L.ptr(self.ex_ws), self.ex_ws_bytes,
             torch.cuda.current_stream().cuda_stream)
-        L.check(st, self.name + " (fused exchange)")
+        if st != L.PK_OK:
+            self.ex_calls -= 1
+        return st
+
+    def fused_step(self, i: int) -> None:
+        self._lib.check(self.fused_call(i), self.name + " (fused exchange)")
 
     def step(self, i: int) -> None:
         if self.exchange is not None:
@@ -451,7 +465,8 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
     torch.cuda.set_device(device)
     dist = init_dist(world, local)
     peaks = load_peaks()
-    work = Workload(args.workload, wl, device, args.split_k, world, rank, dist)
+    work = Workload(args.workload, wl, device, args.split_k, world, rank, dist,
+                    exchange=args.exchange == "fused")
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     chunk = 1000 if work.hbm else 20
     gathered = work.sharded and world > 1
@@ -500,9 +515,9 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
         breakdown = {"gemm_us": round(gemm_ms / nb * 1e3, 3),
                      "allgather_us": round(gath_ms / nb * 1e3, 3), "steps": nb}
         if work.exchange is not None:
-            breakdown["step"] = ("one kernel per rank: the GEMV stores its columns into every "
-                                 "rank's output over NVLink and ends with a flag barrier; "
-                                 "gemm_us / allgather_us time the unfused local GEMV and an "
+            breakdown["step"] = ("one kernel per rank: the local GEMM stores its columns into "
+                                 "every rank's output over NVLink and ends with a flag barrier; "
+                                 "gemm_us / allgather_us time the unfused local GEMM and an "
                                  "NCCL all-gather of its output for comparison")
         del g_gemm, g_gath
 
@@ -573,7 +588,7 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
             par = "single GPU (unsharded)"
         elif work.exchange is not None:
             par = (f"N sharded over {world} GPUs ({work.NL} columns each), output exchanged inside "
-                   "the GEMV (NVLink peer stores + flag barrier)")
+                   "the local GEMM kernel (NVLink peer stores + flag barrier)")
         else:
             par = f"N sharded over {world} GPUs ({work.NL} columns each), NCCL all-gather of the output"
     
@@ -732,6 +747,9 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--split-k", type=int, default=0)
+    ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused",
+                    help="sharded W4A16 layers: output exchange inside the kernel where it "
+                         "covers the shape, or always the NCCL all-gather")
     ap.add_argument("--e2e-steps", type=int, default=2000)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")

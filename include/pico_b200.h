@@ -175,8 +175,9 @@ PK_API int pk_ipc_close(void* ptr);
 
 /* One rank's slice of an N-sharded W4A16 layer, y[M, N_full] = A @ dequant(W),
  * where this rank holds columns [n_offset, n_offset + N) (Wp [K, N/2],
- * scales [K/g, N]). The GEMV writes its columns straight into every rank's
- * output buffer peer_out[r] (fp32 or bf16 [M, ldo] with ldo >= N_full, mapped
+ * scales [K/g, N]). The local kernel (the one pk_w4a16_gemm picks with
+ * split_k = 0: GEMV, decode or skinny) writes its columns straight into every
+ * rank's output buffer peer_out[r] (fp32 or bf16 [M, ldo] with ldo >= N_full, mapped
  * with pk_ipc_open), then its last CTA adds 1 to every peer's arrival count
  * peer_flag[r] (release, system scope) and waits, at most ~2 s, until its own
  * count reaches the next multiple of world - 1: on return every rank's
@@ -187,8 +188,11 @@ PK_API int pk_ipc_close(void* ptr);
  * rewritten by the next call before its reader is done (alternate two
  * buffers). Needs a workspace of
  * pk_w4a16_workspace_size bytes (at least 64 KB). Covers the GEMV's shapes
- * (M = 1, and M = 2 on slices of 16 MB or more; world <= 8); returns
- * PK_ERR_UNSUPPORTED otherwise, so the caller can exchange with NCCL instead.
+ * (M = 1, and M = 2 on slices of 16 MB or more), the decode kernel's (M <= 32,
+ * K % 128 == 0, N % 128 == 0, group 128) and the skinny kernel's where
+ * pk_w4a16_gemm would pick it (32 < M <= 256); world <= 8. Returns
+ * PK_ERR_UNSUPPORTED otherwise (the fused prefill kernel has no exchange), so
+ * the caller can exchange with NCCL instead.
  * Replaces the all-gather that gemm_int4.int4_gemm's callers would need on a
  * sharded layer (no counterpart in the reference). */
 PK_API int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t* wp,

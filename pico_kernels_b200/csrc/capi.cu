@@ -727,12 +727,35 @@ int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t
   if (!is16(a_dtype)) return fail(PK_ERR_DTYPE, "A must be f16 or bf16");
   if (out_dtype != PK_F32 && out_dtype != PK_BF16)
     return fail(PK_ERR_DTYPE, "output must be f32 or bf16");
-  if (!(gemv_preferred(M, N, K) && gemv_supported(M, N, K, group_size, scales, lda, a, wp)))
-    return fail(PK_ERR_UNSUPPORTED, "the fused exchange covers the GEMV's shapes only");
-  size_t need = gemv_workspace_bytes(M, N, K);
+  if (scales != nullptr && group_size <= 0) return fail(PK_ERR_SHAPE, "group_size must be > 0");
+  // The same kernel choice as pk_w4a16_gemm's automatic split: the CUDA-core
+  // GEMV, the tensor-core decode kernel (M <= 32) or the skinny swap-AB
+  // kernel (32 < M <= 256, where it beats the fused prefill kernel).
+  enum { kGemv, kDecode, kSkinny } path;
+  if (gemv_preferred(M, N, K) && gemv_supported(M, N, K, group_size, scales, lda, a, wp))
+    path = kGemv;
+  else if (decode_supported(M, N, K, group_size, scales, lda, a))
+    path = kDecode;
+  else if (skinny_supported(M, N, K, group_size, scales, lda, a) &&
+           (reinterpret_cast<uintptr_t>(wp) & 15) == 0 && skinny_preferred(M, N, K))
+    path = kSkinny;
+  else
+    return fail(PK_ERR_UNSUPPORTED,
+                "the fused exchange covers the GEMV, decode and skinny kernels' shapes only");
+  int split = 1;
+  size_t need = kCounterBytes;
+  if (path == kGemv) {
+    need = gemv_workspace_bytes(M, N, K);
+  } else if (path == kDecode) {
+    split = decode_pick_split(M, N, K);
+    if (split > K / 128) split = static_cast<int>(K / 128);
+    need = decode_workspace_bytes(M, N, K, split);
+    if (N / 128 >= kMaxCounters - 1)
+      return fail(PK_ERR_SHAPE, "too many column tiles for the sharded decode kernel");
+  }
   if (need < kCounterBytes) need = kCounterBytes;
   if (workspace == nullptr || workspace_bytes < need)
-    return fail(PK_ERR_WORKSPACE, "the sharded GEMV needs %zu workspace bytes, got %zu", need,
+    return fail(PK_ERR_WORKSPACE, "the sharded GEMM needs %zu workspace bytes, got %zu", need,
                 workspace_bytes);
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
     return fail(PK_ERR_ALIGN, "workspace must be 256-byte aligned");
@@ -753,11 +776,11 @@ int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t
   p.out_dtype = out_dtype;
   p.ldo = ldo;
   p.a_dtype = a_dtype;
-  p.split = 1;
+  p.split = split;
   p.status = device_status_ptr();
   p.sems = ws_counters(workspace);
   p.partials = ws_partials(workspace);
-  GemvShard sh{};
+  OutputShard sh{};
   sh.n_offset = n_offset;
   sh.world = world;
   sh.rank = rank;
@@ -767,9 +790,11 @@ int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t
   }
   sh.done = ws_counters(workspace) + (kMaxCounters - 1);
   const char* why = "";
-  cudaError_t e = launch_w4a16_gemv(p, as_stream(stream), &why, &sh);
+  cudaError_t e = path == kGemv     ? launch_w4a16_gemv(p, as_stream(stream), &why, &sh)
+                  : path == kDecode ? launch_w4a16_decode(p, as_stream(stream), &why, &sh)
+                                    : launch_w4a16_skinny(p, as_stream(stream), &why, &sh);
   if (e == cudaErrorInvalidValue && why[0] != '\0') return fail(PK_ERR_ALIGN, "%s", why);
-  if (e != cudaSuccess) return cuda_fail(e, "sharded w4a16 gemv launch");
+  if (e != cudaSuccess) return cuda_fail(e, "sharded w4a16 gemm launch");
   ok();
   return PK_OK;
 }

@@ -566,4 +566,72 @@ __device__ __forceinline__ void dequant8(uint32_t w, uint32_t s01, uint32_t s23,
   out[3] = p67;
 }
 
+// ---------------------------------------------------------------------------
+// Fused output exchange of an N-sharded layer: every rank's kernel stores its
+// column slice into all ranks' output buffers (plain peer stores over NVLink;
+// no multicast object), then one flag barrier per call. `P` has the fields
+// world, rank, peer_flag[] (8-byte aligned words: the arrival count, then,
+// for this rank only, its expected count) and done (a zeroed per-grid CTA
+// completion counter).
+// ---------------------------------------------------------------------------
+constexpr int kMaxPeers = 8;
+
+__device__ __forceinline__ void store_elem(void* out, int out_dtype, int64_t idx, float v) {
+  if (out_dtype == PK_BF16)
+    static_cast<__nv_bfloat16*>(out)[idx] = __float2bfloat16_rn(v);
+  else
+    static_cast<float*>(out)[idx] = v;
+}
+
+// Output element idx (row-major in the local slice's coordinates, leading
+// dimension ldo): to `out`, or for a sharded call to idx + n_offset of every
+// rank's buffer.
+__device__ __forceinline__ void emit_out(void* out, const OutputShard& x, int out_dtype,
+                                         int64_t idx, float v) {
+  if (x.world == 0) {
+    store_elem(out, out_dtype, idx, v);
+    return;
+  }
+  for (int r = 0; r < x.world; ++r)
+    store_elem(reinterpret_cast<void*>(x.peer_out[r]), out_dtype, idx + x.n_offset, v);
+}
+
+// Called by every thread of every CTA after its output stores. The CTA's
+// peer stores are ordered before one system-scope fence by thread 0 through
+// the barrier (the grid-synchronisation pattern), taken only by CTAs that
+// stored; the grid's last CTA adds 1 to each peer's flag (release, system
+// scope) and waits, bounded, until its own flag reaches its next expected
+// count, advanced in device memory so CUDA graph replays stay in step.
+template <typename P>
+__device__ __forceinline__ void peer_exchange_finish(const P& p, bool stored, int* status,
+                                                     int where) {
+  const bool any = __syncthreads_or(stored) != 0;
+  if (threadIdx.x + threadIdx.y + threadIdx.z != 0) return;
+  if (any) __threadfence_system();
+  const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+  unsigned prev;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p.done) : "memory");
+  if (prev != total - 1) return;
+  *p.done = 0u;  // re-arm; the next call starts after this grid completes
+  for (int r = 0; r < p.world; ++r) {
+    if (r == p.rank) continue;
+    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.peer_flag[r]) : "memory");
+  }
+  unsigned* expected = reinterpret_cast<unsigned*>(p.peer_flag[p.rank]) + 1;
+  const uint32_t target = *expected + static_cast<uint32_t>(p.world - 1);
+  *expected = target;
+  const unsigned* own = reinterpret_cast<const unsigned*>(p.peer_flag[p.rank]);
+  const long long t0 = clock64();
+  while (true) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(own) : "memory");
+    if (static_cast<int>(v - target) >= 0) break;
+    if (clock64() - t0 > PK_WAIT_CYCLES) {
+      record_error(status, PK_ERR_TIMEOUT, where);
+      break;
+    }
+    __nanosleep(100);
+  }
+}
+
 }  // namespace pk

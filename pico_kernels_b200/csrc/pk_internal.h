@@ -23,6 +23,7 @@ enum WaitSite : int {
   kSiteDecodeFull = 101,
   kSiteDecodeMma = 102,
   kSiteDecodeFinal = 103,
+  kSiteDecodePeers = 104,
   kSiteGemmProducer = 201,
   kSiteGemmMma = 202,
   kSiteGemmEpilogue = 203,
@@ -33,6 +34,7 @@ enum WaitSite : int {
   kSiteSkinnyFull = 401,
   kSiteSkinnyMma = 402,
   kSiteSkinnyFinal = 403,
+  kSiteSkinnyPeers = 404,
 };
 
 // Host-side tensor map encoding (cuTensorMapEncodeTiled via the runtime's
@@ -90,6 +92,18 @@ cudaError_t launch_fp8_quantize(const void* x, int dtype, int64_t n, float scale
 cudaError_t launch_dequant_int4(const uint8_t* wp, const void* scales, int group, int dtype,
                                 int64_t K, int64_t N, void* out, cudaStream_t s);
 
+// Output exchange of an N-sharded layer (GEMV, decode and skinny kernels):
+// the kernel writes its columns [n_offset, n_offset + N) into every rank's
+// buffer, then flags each peer. world == 0 marks an unsharded call (the
+// kernels then store to their `out` argument and ignore the rest).
+struct OutputShard {
+  int64_t n_offset;
+  int world, rank;
+  uint64_t peer_out[8];
+  uint64_t peer_flag[8];  // 8 bytes each: arrival count, then (own only) expected count
+  unsigned* done;  // zeroed completion counter (workspace)
+};
+
 // ---- w4a16_decode.cu -----------------------------------------------------
 struct DecodeArgs {
   const void* a;
@@ -119,25 +133,18 @@ size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int split);
 bool skinny_supported(int64_t M, int64_t N, int64_t K, int group, const void* scales,
                       int64_t lda, const void* a);
 bool skinny_preferred(int64_t M, int64_t N, int64_t K);
-cudaError_t launch_w4a16_skinny(const DecodeArgs& p, cudaStream_t s, const char** why);
-cudaError_t launch_w4a16_decode(const DecodeArgs& args, cudaStream_t s, const char** why);
+cudaError_t launch_w4a16_skinny(const DecodeArgs& p, cudaStream_t s, const char** why,
+                                const OutputShard* shard = nullptr);
+cudaError_t launch_w4a16_decode(const DecodeArgs& args, cudaStream_t s, const char** why,
+                                const OutputShard* shard = nullptr);
 
 // ---- w4a16_gemv.cu (M <= 2 on the CUDA cores; cluster or stream-K split) -
 bool gemv_preferred(int64_t M, int64_t N, int64_t K);  // faster than the decode kernel here
 bool gemv_supported(int64_t M, int64_t N, int64_t K, int group, const void* scales, int64_t lda,
                     const void* a, const void* wp);
 size_t gemv_workspace_bytes(int64_t M, int64_t N, int64_t K);  // 0: no split-K fixup needed
-// Output exchange of an N-sharded layer: the GEMV writes its columns
-// [n_offset, n_offset + N) into every rank's buffer, then flags each peer.
-struct GemvShard {
-  int64_t n_offset;
-  int world, rank;
-  uint64_t peer_out[8];
-  uint64_t peer_flag[8];  // 8 bytes each: arrival count, then (own only) expected count
-  unsigned* done;  // zeroed completion counter (workspace)
-};
 cudaError_t launch_w4a16_gemv(const DecodeArgs& args, cudaStream_t s, const char** why,
-                              const GemvShard* shard = nullptr);
+                              const OutputShard* shard = nullptr);
 
 // ---- gemm_tc.cu (persistent tcgen05 GEMM: fp8, dense split-K, W4A16 prefill)
 struct GemmArgs {

@@ -83,13 +83,6 @@ struct TypeFmt<__half> {
 __device__ __forceinline__ float ld_scale(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 __device__ __forceinline__ float ld_scale(const __half* p) { return __half2float(*p); }
 
-__device__ __forceinline__ void store_out(void* out, int out_dtype, int64_t idx, float v) {
-  if (out_dtype == PK_BF16)
-    static_cast<__nv_bfloat16*>(out)[idx] = __float2bfloat16_rn(v);
-  else
-    static_cast<float*>(out)[idx] = v;
-}
-
 template <typename T, bool kGrouped, int NA>
 __global__ void __launch_bounds__(kThreads, 2)
     w4a16_decode_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -97,7 +90,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                         int M, int N, int K, int split, int use_cluster, float scalar_scale,
                         void* __restrict__ out, int out_dtype, int64_t ldo,
                         float* __restrict__ partials, unsigned* __restrict__ sems,
-                        int* __restrict__ status) {
+                        int* __restrict__ status, const __grid_constant__ OutputShard peers) {
   using C = DecCfg<NA>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -294,6 +287,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   // ---------------- split-K reduction and output ----------------
   fail = __syncthreads_or(fail) != 0;
+  bool stored = false;  // this thread wrote output (sharded exchange: fence before arriving)
   if (use_cluster) {
     float* red = reinterpret_cast<float*>(smem + C::kRedOff);
     if (!fail && warp < kEpiWarps) {
@@ -317,8 +311,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int j = 0; j < kMaxClusterSplit; ++j)
           if (j < split) sum += x[j];
         const int m = e / kBN, l = e % kBN;
-        store_out(out, out_dtype, m * ldo + static_cast<int64_t>(tile) * kBN + l,
-                  sum * scalar_scale);
+        emit_out(out, peers, out_dtype, m * ldo + static_cast<int64_t>(tile) * kBN + l,
+                 sum * scalar_scale);
+        stored = true;
       }
     }
     cluster_sync();  // keep every CTA's shared memory alive until all reads are done
@@ -326,7 +321,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (!fail && warp < kEpiWarps) {
 #pragma unroll
       for (int m = 0; m < NA; ++m)
-        if (m < M) store_out(out, out_dtype, m * ldo + n, acc[m] * scalar_scale);
+        if (m < M) emit_out(out, peers, out_dtype, m * ldo + n, acc[m] * scalar_scale);
+      stored = true;
     }
   } else if (!fail && warp < kEpiWarps) {
     float* mine = partials + (static_cast<int64_t>(tile) * split + ks) * M * kBN;
@@ -358,9 +354,10 @@ __global__ void __launch_bounds__(kThreads, 2)
             for (int jj = 0; jj < 8; ++jj)
               if (j0 + jj < split) sum += x[jj];
           }
-          store_out(out, out_dtype, m * ldo + n, sum * scalar_scale);
+          emit_out(out, peers, out_dtype, m * ldo + n, sum * scalar_scale);
         }
       }
+      stored = true;
       if (tid == 0) sems[tile] = 0u;  // re-arm for the next call
     }
   }
@@ -372,6 +369,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) tmem_dealloc(tmem, C::kTmemCols);
+  if (peers.world > 1) peer_exchange_finish(peers, stored, status, kSiteDecodePeers);
 }
 
 CUtensorMapDataType tmap_type(int dt) {
@@ -445,7 +443,8 @@ size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int split) {
 namespace {
 
 template <int NA>
-cudaError_t launch_decode_na(const DecodeArgs& p, cudaStream_t s, const char** why) {
+cudaError_t launch_decode_na(const DecodeArgs& p, cudaStream_t s, const char** why,
+                             const OutputShard& peers) {
   constexpr int kSmemBytes = DecCfg<NA>::kSmemBytes;
   CUtensorMap tmA, tmW;
   const CUtensorMapDataType dt = tmap_type(p.a_dtype);
@@ -492,7 +491,7 @@ cudaError_t launch_decode_na(const DecodeArgs& p, cudaStream_t s, const char** w
     return cudaLaunchKernelEx(&cfg, kernel, tmA, tmW, scales_ptr, static_cast<int>(p.M),
                               static_cast<int>(p.N), static_cast<int>(p.K), p.split, use_cluster,
                               p.scalar_scale, p.out, p.out_dtype, p.ldo, p.partials, p.sems,
-                              p.status);
+                              p.status, peers);
   };
   if (p.a_dtype == PK_BF16) {
     auto sp = static_cast<const __nv_bfloat16*>(p.scales);
@@ -506,9 +505,21 @@ cudaError_t launch_decode_na(const DecodeArgs& p, cudaStream_t s, const char** w
 
 }  // namespace
 
-// M <= 16 on 16 activation columns, M <= 32 on 32 (the MMA's N).
-cudaError_t launch_w4a16_decode(const DecodeArgs& p, cudaStream_t s, const char** why) {
-  return p.M <= 16 ? launch_decode_na<16>(p, s, why) : launch_decode_na<32>(p, s, why);
+// M <= 16 on 16 activation columns, M <= 32 on 32 (the MMA's N). With a
+// shard, the output goes to every rank's buffer and the grid ends with the
+// flag barrier of the fused exchange.
+cudaError_t launch_w4a16_decode(const DecodeArgs& p, cudaStream_t s, const char** why,
+                                const OutputShard* shard) {
+  OutputShard peers{};
+  if (shard != nullptr) {
+    if (shard->world < 1 || shard->world > kMaxPeers || shard->done == nullptr) {
+      *why = "sharded decode: 1 <= world <= 8 and a workspace are required";
+      return cudaErrorInvalidValue;
+    }
+    peers = *shard;
+  }
+  return p.M <= 16 ? launch_decode_na<16>(p, s, why, peers)
+                   : launch_decode_na<32>(p, s, why, peers);
 }
 
 }  // namespace pk

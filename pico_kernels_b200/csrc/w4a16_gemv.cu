@@ -166,8 +166,6 @@ __device__ __forceinline__ unsigned atomic_add_acq_rel(unsigned* p, unsigned v) 
   return old;
 }
 
-constexpr int kMaxPeers = 8;
-
 struct GemvParams {
   int N, K, group;
   int group_shift;     // log2(group) when group is a power of two, else -1
@@ -196,43 +194,9 @@ __device__ __forceinline__ void store_col(const GemvParams& p, int m, int64_t co
   }
 }
 
-// After every CTA's stores: the last CTA raises each peer's flag (release,
-// system scope) and waits, bounded, for all peers' contributions to this
-// GPU's copy.
+// After every CTA's stores: the shared flag barrier of the fused exchange.
 __device__ __forceinline__ void sharded_finish(const GemvParams& p, bool stored) {
-  // The CTA's peer stores are ordered before one system-scope fence by thread
-  // 0 through the barrier (the grid-synchronisation pattern), taken only by
-  // CTAs that stored: a fence in every thread cost ~12 us per call on the
-  // 70B layer, one in every CTA ~6 us.
-  const bool any = __syncthreads_or(stored) != 0;
-  if (threadIdx.x != 0) return;
-  if (any) __threadfence_system();
-  const unsigned total = gridDim.x;
-  unsigned prev;
-  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p.done) : "memory");
-  if (prev != total - 1) return;
-  *p.done = 0u;  // re-arm; the next call starts after this grid completes
-  for (int r = 0; r < p.world; ++r) {
-    if (r == p.rank) continue;
-    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.peer_flag[r]) : "memory");
-  }
-  // this GPU's expected count lives beside its flag and is advanced here, so
-  // the barrier also holds when a CUDA graph replays the launch
-  unsigned* expected = reinterpret_cast<unsigned*>(p.peer_flag[p.rank]) + 1;
-  const uint32_t target = *expected + static_cast<uint32_t>(p.world - 1);
-  *expected = target;
-  const unsigned* own = reinterpret_cast<const unsigned*>(p.peer_flag[p.rank]);
-  const long long t0 = clock64();
-  while (true) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(own) : "memory");
-    if (static_cast<int>(v - target) >= 0) break;
-    if (clock64() - t0 > PK_WAIT_CYCLES) {
-      record_error(p.status, PK_ERR_TIMEOUT, kSiteGemvPeers);
-      break;
-    }
-    __nanosleep(100);
-  }
+  peer_exchange_finish(p, stored, p.status, kSiteGemvPeers);
 }
 
 // Index of the scale group holding K row `row` (a shift for power-of-two groups).
@@ -563,7 +527,7 @@ size_t gemv_workspace_bytes(int64_t M, int64_t N, int64_t K) {
 }
 
 cudaError_t launch_w4a16_gemv(const DecodeArgs& a, cudaStream_t s, const char** why,
-                              const GemvShard* shard) {
+                              const OutputShard* shard) {
   CUtensorMap tmW, tmA, tmS;
   const CUtensorMapDataType dt = tmap_type16(a.a_dtype);
   if (!encode_tmap_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.wp, a.N / 2, a.K, a.N / 2, kRowBytes,

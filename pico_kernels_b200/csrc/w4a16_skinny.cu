@@ -67,20 +67,13 @@ struct SkFmt<__half> {
   static constexpr uint32_t kFmt = 0;
 };
 
-__device__ __forceinline__ void sk_store(void* out, int out_dtype, int64_t idx, float v) {
-  if (out_dtype == PK_BF16)
-    static_cast<__nv_bfloat16*>(out)[idx] = __float2bfloat16_rn(v);
-  else
-    static_cast<float*>(out)[idx] = v;
-}
-
 template <typename T, bool kGrouped, int NA>
 __global__ void __launch_bounds__(kThreads, 2)
     w4a16_skinny_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmW,
                         const __grid_constant__ CUtensorMap tmS, int M, int K, int group,
                         float scalar_scale, void* __restrict__ out, int out_dtype, int64_t ldo,
-                        int* __restrict__ status) {
+                        int* __restrict__ status, const __grid_constant__ OutputShard peers) {
   using C = SkCfg<NA>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -210,6 +203,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 
   // ---------------- epilogue: D[n, m] -> out[m, n] ----------------
+  bool stored = false;  // this thread wrote output (sharded exchange: fence before arriving)
   if (warp < kEpiWarps && !fail && S > 0) {
     fail = !mbar_wait(acc_full, 0, status, kSiteSkinnyFinal);
     if (!fail) {
@@ -226,9 +220,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int m = c * 32 + i;
-          if (m < M) sk_store(out, out_dtype, m * ldo + n, __uint_as_float(raw[i]) * sc);
+          if (m < M) emit_out(out, peers, out_dtype, m * ldo + n, __uint_as_float(raw[i]) * sc);
         }
       }
+      stored = true;
     }
   }
 
@@ -241,6 +236,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) tmem_dealloc(tmem, C::kTmemCols);
+  if (peers.world > 1) peer_exchange_finish(peers, stored, status, kSiteSkinnyPeers);
 }
 
 CUtensorMapDataType sk_tmap_type(int dt) {
@@ -248,7 +244,8 @@ CUtensorMapDataType sk_tmap_type(int dt) {
 }
 
 template <int NA>
-cudaError_t launch_skinny_na(const DecodeArgs& p, cudaStream_t s, const char** why) {
+cudaError_t launch_skinny_na(const DecodeArgs& p, cudaStream_t s, const char** why,
+                             const OutputShard& peers) {
   constexpr int kSmem = SkCfg<NA>::kSmemBytes;
   CUtensorMap tmA, tmW, tmS;
   const CUtensorMapDataType dt = sk_tmap_type(p.a_dtype);
@@ -281,7 +278,7 @@ cudaError_t launch_skinny_na(const DecodeArgs& p, cudaStream_t s, const char** w
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, tmA, tmW, tmS, static_cast<int>(p.M),
                               static_cast<int>(p.K), p.group > 0 ? p.group : kBK, p.scalar_scale,
-                              p.out, p.out_dtype, p.ldo, p.status);
+                              p.out, p.out_dtype, p.ldo, p.status, peers);
   };
   if (p.a_dtype == PK_BF16)
     return grouped ? launch(w4a16_skinny_kernel<__nv_bfloat16, true, NA>)
@@ -329,10 +326,21 @@ bool skinny_preferred(int64_t M, int64_t N, int64_t K) {
   return sk < 0.95 * pf;
 }
 
-cudaError_t launch_w4a16_skinny(const DecodeArgs& p, cudaStream_t s, const char** why) {
-  if (p.M <= 64) return launch_skinny_na<64>(p, s, why);
-  if (p.M <= 128) return launch_skinny_na<128>(p, s, why);
-  return launch_skinny_na<256>(p, s, why);
+// With a shard, the output goes to every rank's buffer and the grid ends
+// with the flag barrier of the fused exchange.
+cudaError_t launch_w4a16_skinny(const DecodeArgs& p, cudaStream_t s, const char** why,
+                                const OutputShard* shard) {
+  OutputShard peers{};
+  if (shard != nullptr) {
+    if (shard->world < 1 || shard->world > kMaxPeers || shard->done == nullptr) {
+      *why = "sharded skinny GEMM: 1 <= world <= 8 and a workspace are required";
+      return cudaErrorInvalidValue;
+    }
+    peers = *shard;
+  }
+  if (p.M <= 64) return launch_skinny_na<64>(p, s, why, peers);
+  if (p.M <= 128) return launch_skinny_na<128>(p, s, why, peers);
+  return launch_skinny_na<256>(p, s, why, peers);
 }
 
 }  // namespace pk

@@ -10,10 +10,12 @@ block with the local kernel, then one ``all_gather_into_tensor`` assembles
 exchange; for M = 1 the gathered buffer already is the row-major output, for
 M > 1 the rank-major blocks are interleaved back into rows.
 
-For the GEMV's shapes (M = 1) a ``PeerExchange`` replaces the all-gather: the
-GEMV writes its columns straight into every rank's output buffer over NVLink
-(buffers mapped with CUDA IPC handles) and ends with a flag barrier, so the
-layer is one kernel per rank (``pk_w4a16_gemm_sharded``).
+Where the local kernel is the CUDA-core GEMV (M <= 2), the tensor-core decode
+kernel (M <= 32) or the skinny swap-AB kernel (32 < M <= 256 where the library
+picks it), a ``PeerExchange`` replaces the all-gather: the kernel writes its
+columns straight into every rank's output buffer over NVLink (buffers mapped
+with CUDA IPC handles) and ends with a flag barrier, so the layer is one kernel
+per rank (``pk_w4a16_gemm_sharded``).
 
 fp8 scales are per tensor and must be global: callers quantize the whole
 activation and weight (or all-reduce the absmax) before slicing, so every
@@ -137,7 +139,8 @@ class PeerExchange:
         """This rank's slice of ``A @ dequant(W)`` written to every rank's buffer.
 
         Returns ``[M, n_full]`` (valid until two calls later), or None when
-        the shape is not one the fused GEMV covers (every rank gets None).
+        no kernel with the fused exchange covers the shape (every rank gets
+        None: the choice depends on the shape only).
         """
         M, K = a.shape
         n_local = scales_shard.shape[1]
@@ -179,8 +182,8 @@ def sharded_int4_gemm(a: torch.Tensor, packed_shard: torch.Tensor, scales_shard:
                       exchange: Optional[PeerExchange] = None, **kw) -> torch.Tensor:
     """``A @ dequant(W)`` for a W4A16 layer whose columns are sharded over ranks.
 
-    With an ``exchange`` and a GEMV shape the output travels inside the GEMV
-    (``PeerExchange``); otherwise each rank computes its block and one NCCL
+    With an ``exchange`` and a shape its kernels cover, the output travels
+    inside the local kernel (``PeerExchange``); otherwise each rank computes its block and one NCCL
     all-gather assembles the layer. ``local_gemm(a, packed, scales,
     group_size=...)`` defaults to ``gemm_int4.int4_gemm`` (the sm_100a
     kernels); tests may pass another implementation to exercise the sharding

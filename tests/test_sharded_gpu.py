@@ -1,9 +1,10 @@
 """N-sharded W4A16 / fp8 layers on GPUs with NCCL (one process per GPU).
 
 With at least two GPUs, two ranks each compute their column slice with the
-sm_100a kernels and all-gather the output over NVLink; the result must equal
-the unsharded kernel's output (same kernels, same per-column arithmetic).
-With one GPU the single-rank path is checked.
+sm_100a kernels and all-gather the output over NVLink (NCCL, or the fused
+peer-store exchange inside the GEMV, decode and skinny kernels); the result
+must equal the unsharded kernel's output (same kernels, same per-column
+arithmetic). With one GPU the single-rank paths are checked.
 """
 
 import os
@@ -60,22 +61,59 @@ def _worker(rank, world, port, q):
         n0, n1 = sharded.shard_columns(1024, world, rank)
         y = sharded.sharded_fp8_gemm(a8, sa, b8[:, n0:n1].contiguous(), sb, world)
         ok.append(bool(torch.equal(y, full)))
-        # fused exchange: the GEMV writes every rank's output over NVLink
-        ex = sharded.PeerExchange(max_m=2, n_full=8192)
-        try:
-            for it, (M, K) in enumerate(((1, 4096), (1, 2048), (1, 4096))):
-                a, packed, scales = _layer(M, 8192, K, dev)
-                a = a + it  # a different input on every call
-                full = pk.int4_gemm(a, packed, scales)
-                p_r, s_r = sharded.shard_int4(packed, scales, world, rank)
-                y = sharded.sharded_int4_gemm(a, p_r, s_r, 128, world, exchange=ex)
-                rel = (torch.norm(y - full) / torch.norm(full)).item()
-                ok.append(rel < 1e-5 and pk.device_status() == (0, 0))
-        finally:
-            ex.close()
+        # fused exchange: the local kernel writes every rank's output over
+        # NVLink -- the GEMV (M = 1), the decode kernel (M = 16, 32: cluster
+        # split-K) and the skinny kernel (M = 64, 200)
+        for n_full, max_m, cases in ((8192, 64, ((1, 4096), (1, 2048), (16, 1024), (32, 2048),
+                                                  (1, 4096), (64, 1024))),
+                                     (40960, 256, ((200, 512), (200, 512)))):
+            ex = sharded.PeerExchange(max_m=max_m, n_full=n_full)
+            try:
+                for it, (M, K) in enumerate(cases):
+                    a, packed, scales = _layer(M, n_full, K, dev)
+                    a = a + it  # a different input on every call
+                    full = pk.int4_gemm(a, packed, scales)
+                    p_r, s_r = sharded.shard_int4(packed, scales, world, rank)
+                    y = ex.int4_gemm(a, p_r, s_r, 128)
+                    if y is None:
+                        ok.append(("not fused", M, K))
+                        continue
+                    rel = (torch.norm(y - full) / torch.norm(full)).item()
+                    ok.append(rel < 1e-5 and pk.device_status() == (0, 0))
+            finally:
+                ex.close()
         q.put((rank, ok))
     finally:
         dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1024, 2048), (16, 1024, 2048), (32, 1024, 1024),
+                                   (64, 1024, 1024), (200, 20480, 512)])
+def test_sharded_entry_one_rank(M, N, K):
+    """pk_w4a16_gemm_sharded at world = 1 (no flag barrier): each kernel with
+    the exchange epilogue writes exactly its column slice of the full-width
+    buffer, bit-identical to the unsharded call (same kernel, same split)."""
+    import ctypes
+    from pico_kernels_b200 import _lib
+    dev = torch.device("cuda")
+    a, packed, scales = _layer(M, N, K, dev)
+    ref = pk.int4_gemm(a, packed, scales)
+    lib = _lib.load()
+    n_off, n_full = 256, N + 512
+    y = torch.full((M, n_full), 7.0, device=dev)
+    flag = torch.zeros(4, dtype=torch.int64, device=dev)
+    ws = torch.zeros(max(lib.pk_w4a16_workspace_size(M, N, K, 0), 1 << 16), dtype=torch.uint8,
+                     device=dev)
+    outs = (ctypes.c_uint64 * 1)(y.data_ptr())
+    flags = (ctypes.c_uint64 * 1)(flag.data_ptr())
+    rc = lib.pk_w4a16_gemm_sharded(
+        a.data_ptr(), _lib.PK_BF16, K, packed.data_ptr(), scales.data_ptr(), 1.0, 128, M, N, K,
+        _lib.PK_F32, n_full, n_off, 1, 0, ctypes.addressof(outs), ctypes.addressof(flags),
+        ws.data_ptr(), ws.numel(), _lib.stream_of(a))
+    _lib.check(rc, "pk_w4a16_gemm_sharded")
+    assert pk.device_status() == (0, 0)
+    assert torch.equal(y[:, n_off:n_off + N], ref)
+    assert bool((y[:, :n_off] == 7.0).all()) and bool((y[:, n_off + N:] == 7.0).all())
 
 
 def test_single_rank_path():
