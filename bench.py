@@ -378,19 +378,20 @@ class Workload:
             a_host.copy_(self.sets[0][0])
             a_dev = torch.empty((M, K), dtype=torch.bfloat16, device=self.device)
 
-            # single GPU: the output buffer is reused across steps (int4_gemm's
-            # out=), as a decode loop would; sharded: the exchange's or NCCL's
-            y_dev = (torch.empty((M, N), dtype=torch.float32, device=self.device)
-                     if world == 1 else None)
+            if world == 1:
+                # one public call with host buffers: H2D of A, the GEMM, D2H of
+                # Y, all inside pk_w4a16_gemm_host
+                def fn(i):
+                    _, packed, scales = self.sets[i % self.n_sets]
+                    pk.int4_gemm_host(a_host, packed, scales, group_size=128, out=y_host)
+                return fn, M * K * 2, M * N * 4
 
+            # sharded: the exchange's or NCCL's output buffer
             def fn(i):
                 _, packed, scales = self.sets[i % self.n_sets]
                 a_dev.copy_(a_host, non_blocking=True)
-                if y_dev is not None:
-                    y = pk.int4_gemm(a_dev, packed, scales, group_size=128, out=y_dev)
-                else:
-                    y = sharded.sharded_int4_gemm(a_dev, packed, scales, 128, world,
-                                                  exchange=self.exchange)
+                y = sharded.sharded_int4_gemm(a_dev, packed, scales, 128, world,
+                                              exchange=self.exchange)
                 y_host.copy_(y, non_blocking=True)
             return fn, M * K * 2, M * N * 4
         if self.kind == "dense":
@@ -623,7 +624,10 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
         "e2e": {"value": round(e2e_value, 4), "unit": unit, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "us_per_step": round(e2e_ms / e2e_steps * 1e3, 3),
-                "path": "pico_kernels_b200 public API (ctypes C ABI), pinned host buffers"},
+                "path": ("pico_kernels_b200.int4_gemm_host -> pk_w4a16_gemm_host (H2D of A, "
+                         "the GEMM and D2H of y in one C-ABI call), pinned host buffers"
+                         if work.kind == "w4a16" and not (work.sharded and world > 1) else
+                         "pico_kernels_b200 public API (ctypes C ABI), pinned host buffers")},
         "gpu_launches": args.steps,
         "clocks": clocks.summary(t0, t1),
     }

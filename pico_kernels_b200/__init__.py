@@ -10,7 +10,7 @@ from . import gemm, gemm_fp8, gemm_int4, gemm_splitk, gptq, linear, quantize  # 
 from ._lib import DtypeError, KernelError, ShapeError, device_status, load  # noqa: F401
 from .gemm_fp8 import fp8_gemm, fp8_gemm_precast  # noqa: F401
 from .gemm_splitk import triton_gemm, triton_gemm_splitk  # noqa: F401
-from .gemm_int4 import (int4_gemm, pack_int4_n, quantize_int4,  # noqa: F401
+from .gemm_int4 import (int4_gemm, int4_gemm_host, pack_int4_n, quantize_int4,  # noqa: F401
                         quantize_int4_grouped, unpack_int4_n)
 from .gptq import gptq_quantize_int4  # noqa: F401
 from .linear import W4A16Linear, quantize_linear_layers  # noqa: F401

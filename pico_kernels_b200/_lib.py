@@ -61,6 +61,8 @@ SIGNATURES = {
                              _int, _i64, _int, _vp, _sz, _vp]),
     "pk_w4a16_gemm_noalloc": (_int, [_vp, _int, _i64, _vp, _vp, _f32, _int, _i64, _i64, _i64,
                                      _vp, _int, _i64, _int, _vp]),
+    "pk_w4a16_gemm_host": (_int, [_vp, _int, _i64, _vp, _vp, _f32, _int, _i64, _i64, _i64, _vp,
+                                  _int, _vp, _vp, _vp, _sz, _vp]),
     "pk_fp8_quantize": (_int, [_vp, _int, _i64, _f32, _vp, _vp]),
     "pk_fp8_gemm": (_int, [_vp, _vp, _i64, _i64, _i64, _f32, _vp, _int, _vp]),
     "pk_fp8_quantize_device": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp]),

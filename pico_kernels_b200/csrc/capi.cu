@@ -510,6 +510,36 @@ int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t* wp, co
   return PK_OK;
 }
 
+int pk_w4a16_gemm_host(const void* a_host, int a_dtype, int64_t lda, const uint8_t* wp,
+                       const void* scales, float scalar_scale, int group_size, int64_t M,
+                       int64_t N, int64_t K, void* y_host, int out_dtype, void* a_dev,
+                       void* y_dev, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!a_host || !y_host || !a_dev || !y_dev) return fail(PK_ERR_SHAPE, "null pointer");
+  if (M <= 0 || N <= 0 || K <= 0 || lda < K)
+    return fail(PK_ERR_SHAPE, "need M, N, K > 0 and lda >= K (got M=%lld N=%lld K=%lld lda=%lld)",
+                (long long)M, (long long)N, (long long)K, (long long)lda);
+  if (!is16(a_dtype)) return fail(PK_ERR_DTYPE, "A must be f16 or bf16");
+  if (out_dtype != PK_F32 && out_dtype != PK_BF16)
+    return fail(PK_ERR_DTYPE, "output must be f32 or bf16");
+  cudaStream_t s = as_stream(stream);
+  const size_t row = static_cast<size_t>(K) * 2;
+  cudaError_t e =
+      lda == K ? cudaMemcpyAsync(a_dev, a_host, row * static_cast<size_t>(M),
+                                 cudaMemcpyHostToDevice, s)
+               : cudaMemcpy2DAsync(a_dev, row, a_host, static_cast<size_t>(lda) * 2, row,
+                                   static_cast<size_t>(M), cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return cuda_fail(e, "copy of A to the device");
+  const int st = pk_w4a16_gemm(a_dev, a_dtype, K, wp, scales, scalar_scale, group_size, M, N, K,
+                               y_dev, out_dtype, N, 0, workspace, workspace_bytes, stream);
+  if (st != PK_OK) return st;
+  const size_t y_bytes = static_cast<size_t>(M) * static_cast<size_t>(N) *
+                         (out_dtype == PK_F32 ? 4u : 2u);
+  e = cudaMemcpyAsync(y_host, y_dev, y_bytes, cudaMemcpyDeviceToHost, s);
+  if (e != cudaSuccess) return cuda_fail(e, "copy of y to the host");
+  ok();
+  return PK_OK;
+}
+
 int pk_fp8_quantize(const void* x, int dtype, int64_t n, float scale, uint8_t* x8,
                     void* stream) {
   if (!x || !x8 || n <= 0) return fail(PK_ERR_SHAPE, "need a non-empty input");

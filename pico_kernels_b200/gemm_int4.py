@@ -22,7 +22,7 @@ import torch
 from . import _lib
 
 __all__ = ["quantize_int4", "pack_int4_n", "unpack_int4_n", "quantize_int4_grouped",
-           "int4_gemm"]
+           "int4_gemm", "int4_gemm_host"]
 
 
 def quantize_int4(w: torch.Tensor) -> tuple[torch.Tensor, float]:
@@ -135,26 +135,7 @@ def int4_gemm(a: torch.Tensor, w_packed: torch.Tensor, scale,
     if not w_packed.is_contiguous():
         w_packed = w_packed.contiguous()
 
-    scales = None
-    scalar = 1.0
-    group = 0
-    if isinstance(scale, torch.Tensor) and scale.numel() > 1:
-        _lib.require_cuda(scale)
-        if scale.dim() != 2 or scale.shape[1] != N:
-            raise _lib.ShapeError(f"group scales must be [G, N={N}] (got {tuple(scale.shape)})")
-        G = scale.shape[0]
-        if group_size is not None:
-            group = group_size
-        else:  # several sizes can give G groups when the last one is ragged: prefer 128
-            group = next((g for g in (128, K // G) if g > 0 and (K + g - 1) // g == G), K // G)
-        if group <= 0 or (K + group - 1) // group != G:
-            raise _lib.ShapeError(f"{G} scale rows do not tile K={K} with group_size={group}")
-        scales = scale if scale.dtype == a.dtype else scale.to(a.dtype)
-        if not scales.is_contiguous():
-            scales = scales.contiguous()
-    else:
-        scalar = float(scale)
-
+    scales, scalar, group = _scale_args(scale, K, N, a.dtype, group_size)
     if out is None:
         out = torch.empty((M, N), dtype=out_dtype, device=a.device)
     elif (out.shape != (M, N) or out.dtype != out_dtype or out.device != a.device
@@ -179,3 +160,77 @@ def int4_gemm(a: torch.Tensor, w_packed: torch.Tensor, scale,
 
 # pk_w4a16_workspace_size per (M, N, K, split_k): a pure function of the shape
 _ws_bytes: dict[tuple[int, int, int, int], int] = {}
+
+
+def _scale_args(scale, K: int, N: int, dtype: torch.dtype, group_size: int | None):
+    """(group scales tensor or None, scalar scale, group size) for the C ABI."""
+    if isinstance(scale, torch.Tensor) and scale.numel() > 1:
+        _lib.require_cuda(scale)
+        if scale.dim() != 2 or scale.shape[1] != N:
+            raise _lib.ShapeError(f"group scales must be [G, N={N}] (got {tuple(scale.shape)})")
+        G = scale.shape[0]
+        if group_size is not None:
+            group = group_size
+        else:  # several sizes can give G groups when the last one is ragged: prefer 128
+            group = next((g for g in (128, K // G) if g > 0 and (K + g - 1) // g == G), K // G)
+        if group <= 0 or (K + group - 1) // group != G:
+            raise _lib.ShapeError(f"{G} scale rows do not tile K={K} with group_size={group}")
+        scales = scale if scale.dtype == dtype else scale.to(dtype)
+        if not scales.is_contiguous():
+            scales = scales.contiguous()
+        return scales, 1.0, group
+    return None, float(scale), 0
+
+
+def int4_gemm_host(a: torch.Tensor, w_packed: torch.Tensor, scale, *,
+                   group_size: int | None = None, out_dtype: torch.dtype = torch.float32,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """``int4_gemm`` for a caller whose activations and outputs live in host
+    memory: ``a`` is a CPU ``[M, K]`` fp16/bf16 tensor, ``w_packed`` and
+    ``scale`` are resident on the GPU. One C-ABI call (``pk_w4a16_gemm_host``)
+    copies A into a device staging buffer, runs the same kernels as
+    ``int4_gemm`` and copies the output into ``out`` (a CPU ``[M, N]`` tensor
+    of ``out_dtype``; allocated page-locked when None). Enqueued on the
+    current stream of the weights' device: synchronise it before reading
+    ``out``. Page-locked ``a`` and ``out`` make the copies asynchronous.
+    """
+    if a.is_cuda or (out is not None and out.is_cuda):
+        raise _lib.DtypeError("int4_gemm_host takes host tensors for a and out")
+    _lib.require_cuda(w_packed)
+    if a.dtype not in (torch.float16, torch.bfloat16):
+        raise _lib.DtypeError(f"a must be fp16 or bf16 (got {a.dtype})")
+    if a.dim() != 2 or w_packed.dim() != 2:
+        raise _lib.ShapeError("a and w_packed must be 2-D")
+    if w_packed.dtype != torch.uint8:
+        raise _lib.DtypeError("w_packed must be uint8")
+    M, K = a.shape
+    K2, N_half = w_packed.shape
+    if K2 != K:
+        raise _lib.ShapeError(f"inner dimensions differ: a has K={K}, w_packed has K={K2}")
+    N = 2 * N_half
+    if a.stride(1) != 1 or a.stride(0) < K:
+        a = a.contiguous()
+    if not w_packed.is_contiguous():
+        w_packed = w_packed.contiguous()
+    scales, scalar, group = _scale_args(scale, K, N, a.dtype, group_size)
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, pin_memory=True)
+    elif out.shape != (M, N) or out.dtype != out_dtype or not out.is_contiguous():
+        raise _lib.ShapeError(f"out must be a contiguous [{M}, {N}] {out_dtype} host tensor")
+    lib = _lib.load()
+    dev = w_packed.device
+    key = (M, N, K, 0)
+    ws_bytes = _ws_bytes.get(key)
+    if ws_bytes is None:
+        ws_bytes = _ws_bytes[key] = lib.pk_w4a16_workspace_size(M, N, K, 0)
+    stream = _lib.stream_of(w_packed)
+    ws = _lib.workspace(dev, ws_bytes, stream=stream) if ws_bytes else None
+    a_dev = _lib.workspace(dev, M * K * 2, tag="stage_a", stream=stream)
+    y_dev = _lib.workspace(dev, M * N * out.element_size(), tag="stage_y", stream=stream)
+    st = lib.pk_w4a16_gemm_host(
+        a.data_ptr(), _lib.dtype_code(a.dtype), a.stride(0), w_packed.data_ptr(),
+        _lib.ptr(scales), scalar, group, M, N, K, out.data_ptr(), _lib.dtype_code(out_dtype),
+        a_dev.data_ptr(), y_dev.data_ptr(), _lib.ptr(ws), ws_bytes, stream)
+    if st:
+        _lib.check(st, "int4_gemm_host")
+    return out
