@@ -104,6 +104,11 @@ struct OutputShard {
   unsigned* done;  // zeroed completion counter (workspace)
 };
 
+// ---- host_io.cu (row copies between mapped page-locked host memory and
+// device buffers, by a kernel chained with programmatic dependent launch) --
+cudaError_t launch_copy_rows(const void* src, int64_t src_pitch, void* dst, int64_t dst_pitch,
+                             int64_t row_bytes, int64_t rows, cudaStream_t s);
+
 // ---- w4a16_decode.cu -----------------------------------------------------
 struct DecodeArgs {
   const void* a;
