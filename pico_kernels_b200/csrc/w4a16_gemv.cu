@@ -21,10 +21,14 @@
 //    for a given SM count. (A variant with one 8-CTA cluster per slice and a
 //    distributed-shared-memory reduction measured slower even at 4096^2:
 //    8.1 vs 7.6 us, half the CTAs per SM.)
-//  * Pipeline. Warp 8 (one thread) is the TMA producer: per unit one 2D box
-//    of weights, the unit's group-scale rows and the activation tile
-//    A[0:M, k0:k0+256] into a ring of shared-memory slots, completing one
-//    mbarrier. Before griddepcontrol.wait it only prefetches weights and
+//  * Pipeline. Warp 8 (one thread) is the TMA producer: per unit four 2D
+//    boxes of 64 weight rows, the unit's group-scale rows and the activation
+//    tile A[0:M, k0:k0+256] into a ring of shared-memory slots; each weight
+//    box completes its own mbarrier (the first also carries the scales and
+//    activations), and a warp waits only for the box holding its rows, so
+//    the arithmetic of a CTA's first unit overlaps the rest of its transfer
+//    (4096^2 at M = 1 gives one unit per CTA). Before griddepcontrol.wait
+//    it only prefetches weights and
 //    scales into L2 (a hint that cannot return stale data), so with
 //    programmatic dependent launch the DRAM fetch overlaps the previous
 //    kernel's tail; every load into shared memory and every global write
@@ -66,6 +70,12 @@ constexpr int kProducerWarp = kWarps;
 constexpr int kThreads = (kWarps + 1) * 32;
 constexpr int kRowsPerWarp = kRows / kWarps;  // 32: one row per lane for the activations
 constexpr int kMaxM = 2;
+// A unit's weights arrive as kSub boxes of kSubRows rows, each completing its
+// own mbarrier, so the warps owning the first rows start while the rest of
+// the unit is still in flight (a CTA often has a single unit).
+constexpr int kSub = 4;
+constexpr int kSubRows = kRows / kSub;           // 64
+constexpr int kSubWBytes = kSubRows * kRowBytes;  // 8192
 constexpr int kMaxScaleRows = 4;        // scale rows a unit can touch (group >= 64)
 constexpr int kSmemTwoPerSm = 115712;   // per-CTA limit for two resident CTAs (228 KB SM)
 
@@ -87,7 +97,7 @@ struct GemvCfg {
   static constexpr int kScratchOff = kRingBytes;
   static constexpr int kScratchBytes = kPairBytes > kRedBytes ? kPairBytes : kRedBytes;
   static constexpr int kBarOff = kScratchOff + kScratchBytes;
-  static constexpr int kSmemBytes = kBarOff + 2 * kStages * 8 + 16 + 128;
+  static constexpr int kSmemBytes = kBarOff + (kSub + 1) * kStages * 8 + 16 + 128;
   static constexpr int kCtasPerSm = 2;
   static_assert(kSmemBytes <= kSmemTwoPerSm, "two CTAs must fit an SM");
 };
@@ -214,8 +224,8 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
                                              ~static_cast<uintptr_t>(127));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
-  uint64_t* empty = full + C::kStages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);  // [stage][sub-box]
+  uint64_t* empty = full + C::kStages * kSub;
   volatile int* last_flag = reinterpret_cast<volatile int*>(empty + C::kStages);
   float* red = reinterpret_cast<float*>(smem + C::kScratchOff);
 
@@ -233,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&full[s], 1);
+      for (int j = 0; j < kSub; ++j) mbar_init(&full[s * kSub + j], 1);
       mbar_init(&empty[s], kWarps);
     }
     fence_barrier_init();
@@ -245,15 +255,15 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
-      const uint32_t tx =
-          C::kWBytes + (kGrouped ? p.scale_rows * kCols * 2 : 0) + C::kABytes;
+      // sub-box 0 also carries the unit's scale rows and activations
+      const uint32_t tx0 = kSubWBytes + (kGrouped ? p.scale_rows * kCols * 2 : 0) + C::kABytes;
       tma_prefetch_desc(&tmW);
       tma_prefetch_desc(&tmA);
       if constexpr (kGrouped) tma_prefetch_desc(&tmS);
       const int pre = n_units < 2 * C::kStages ? n_units : 2 * C::kStages;
       for (int i = 0, s = static_cast<int>(u0 / KB), kb = static_cast<int>(u0 % KB); i < pre;
            ++i) {
-        tma_prefetch_l2_2d(&tmW, s * kRowBytes, kb * kRows);
+        for (int j = 0; j < kSub; ++j) tma_prefetch_l2_2d(&tmW, s * kRowBytes, kb * kRows + j * kSubRows);
         if constexpr (kGrouped) tma_prefetch_l2_2d(&tmS, s * kCols, group_of(kb * kRows, p));
         if (++kb == KB) kb = 0, ++s;
       }
@@ -270,11 +280,16 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
         }
         const int k0 = kb * kRows;
         uint8_t* base = smem + slot * C::kSlotBytes;
-        mbar_arrive_expect_tx(&full[slot], tx);
-        tma_load_2d(base, &tmW, &full[slot], slice * kRowBytes, k0);
+        uint64_t* fb = &full[slot * kSub];
+        mbar_arrive_expect_tx(&fb[0], tx0);
+        tma_load_2d(base, &tmW, &fb[0], slice * kRowBytes, k0);
         if constexpr (kGrouped)
-          tma_load_2d(base + C::kWBytes, &tmS, &full[slot], slice * kCols, group_of(k0, p));
-        tma_load_2d(base + C::kWBytes + C::kSBytes, &tmA, &full[slot], k0, 0);
+          tma_load_2d(base + C::kWBytes, &tmS, &fb[0], slice * kCols, group_of(k0, p));
+        tma_load_2d(base + C::kWBytes + C::kSBytes, &tmA, &fb[0], k0, 0);
+        for (int j = 1; j < kSub; ++j) {
+          mbar_arrive_expect_tx(&fb[j], kSubWBytes);
+          tma_load_2d(base + j * kSubWBytes, &tmW, &fb[j], slice * kRowBytes, k0 + j * kSubRows);
+        }
         issued = i + 1;
         if (++kb == KB) kb = 0, ++slice;
         if (++slot == C::kStages) slot = 0, ++round;
@@ -283,7 +298,8 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
         // let copies already issued land before the CTA's shared memory is released
         const int first = issued > C::kStages ? issued - C::kStages : 0;
         for (int i = first; i < issued; ++i)
-          mbar_wait(&full[i % C::kStages], (i / C::kStages) & 1, nullptr, 0);
+          for (int j = 0; j < kSub; ++j)
+            mbar_wait(&full[(i % C::kStages) * kSub + j], (i / C::kStages) & 1, nullptr, 0);
       }
     }
     __syncwarp();
@@ -308,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
          ++i, slice += (kb + 1 == KB), kb = (kb + 1 == KB ? 0 : kb + 1),
              slot = (slot + 1 == C::kStages ? 0 : slot + 1), round += (slot == 0)) {
       const int k0 = kb * kRows;
-      if (!failed && !mbar_wait_sleep(&full[slot], round & 1, p.status, kSiteGemvConsumer))
+      if (!failed && !mbar_wait_sleep(&full[slot * kSub], round & 1, p.status, kSiteGemvConsumer))
         failed = true;
       const uint8_t* base = smem + slot * C::kSlotBytes;
 
@@ -352,6 +368,12 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
         for (int q = 0; q < 4; ++q) sc[q] = pack2(p.scalar_scale, p.scalar_scale);
       }
       __syncwarp();
+      // this warp's rows are in sub-box warp * kRowsPerWarp / kSubRows
+      constexpr int kWarpsPerSub = kSubRows / kRowsPerWarp;
+      if (warp >= kWarpsPerSub && !failed &&
+          !mbar_wait_sleep(&full[slot * kSub + warp / kWarpsPerSub], round & 1, p.status,
+                           kSiteGemvConsumer))
+        failed = true;
 
       const uint32_t* wrow =
           reinterpret_cast<const uint32_t*>(base) + warp * kRowsPerWarp * 32 + lane;
@@ -531,7 +553,7 @@ cudaError_t launch_w4a16_gemv(const DecodeArgs& a, cudaStream_t s, const char** 
   CUtensorMap tmW, tmA, tmS;
   const CUtensorMapDataType dt = tmap_type16(a.a_dtype);
   if (!encode_tmap_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.wp, a.N / 2, a.K, a.N / 2, kRowBytes,
-                      kRows, CU_TENSOR_MAP_SWIZZLE_NONE, why))
+                      kSubRows, CU_TENSOR_MAP_SWIZZLE_NONE, why))
     return cudaErrorInvalidValue;
   if (!encode_tmap_2d(&tmA, dt, a.a, a.K, a.M, a.lda * 2, kRows, static_cast<uint32_t>(a.M),
                       CU_TENSOR_MAP_SWIZZLE_NONE, why))
