@@ -56,6 +56,38 @@ def test_host_only_calls_work_without_gpu():
     # GPTQ producer: odd N and oversized groups are rejected on the host
     assert lib.pk_gptq_int4(16, 16, 64, 33, 16, 16, 16, _lib.PK_F32, 16, None) == _lib.PK_ERR_SHAPE
     assert lib.pk_gptq_int4(16, 16, 64, 32, 256, 16, 16, _lib.PK_F32, 16, None) == _lib.PK_ERR_SHAPE
+    # host-buffer W4A16: missing staging buffers, a short row stride and a bad
+    # output dtype are caught before any copy is enqueued
+    args = dict(a_host=64, a_dtype=_lib.PK_BF16, lda=256, wp=64, scales=64, scalar=1.0, group=128,
+                M=1, N=256, K=256, y_host=64, out_dtype=_lib.PK_F32, a_dev=64, y_dev=64, ws=None,
+                ws_bytes=0, stream=None)
+
+    def host_call(**kw):
+        a = dict(args, **kw)
+        return lib.pk_w4a16_gemm_host(*a.values())
+    assert host_call(a_dev=None) == _lib.PK_ERR_SHAPE
+    assert host_call(y_host=None) == _lib.PK_ERR_SHAPE
+    assert host_call(lda=128) == _lib.PK_ERR_SHAPE
+    assert host_call(M=0) == _lib.PK_ERR_SHAPE
+    assert host_call(a_dtype=_lib.PK_F32) == _lib.PK_ERR_DTYPE
+    assert host_call(out_dtype=_lib.PK_I8) == _lib.PK_ERR_DTYPE
+    # sharded W4A16: bad world / rank / slice are shape errors; shapes no kernel
+    # with the fused exchange serves (M > 256) report PK_ERR_UNSUPPORTED so the
+    # caller falls back to NCCL
+    outs = (ctypes.c_uint64 * 2)(4096, 8192)
+    flags = (ctypes.c_uint64 * 2)(4096, 8192)
+    sh = dict(a=4096, a_dtype=_lib.PK_BF16, lda=1024, wp=4096, scales=4096, scalar=1.0,
+              group=128, M=1, N=1024, K=1024, out_dtype=_lib.PK_F32, ldo=2048, n_offset=0,
+              world=2, rank=0, outs=ctypes.addressof(outs), flags=ctypes.addressof(flags),
+              ws=4096, ws_bytes=1 << 20, stream=None)
+
+    def sharded_call(**kw):
+        a = dict(sh, **kw)
+        return lib.pk_w4a16_gemm_sharded(*a.values())
+    assert sharded_call(world=9) == _lib.PK_ERR_SHAPE
+    assert sharded_call(rank=2) == _lib.PK_ERR_SHAPE
+    assert sharded_call(n_offset=1536) == _lib.PK_ERR_SHAPE
+    assert sharded_call(M=300) == _lib.PK_ERR_UNSUPPORTED
 
 
 def test_workspace_size_is_host_only():
