@@ -2,9 +2,9 @@
  * pico_b200.h -- C ABI of the B200 (sm_100a) quantized-matmul path.
  *
  * Drop-in boundary for pico-kernels' quantized-matmul functions. Every entry
- * point takes plain device pointers, sizes and a cudaStream_t passed as
- * `void*` (NULL = legacy default stream); no framework types cross the
- * boundary. Every entry point is asynchronous on `stream` except where noted,
+ * point takes plain device pointers (pk_w4a16_gemm_host also host pointers),
+ * sizes and a cudaStream_t passed as `void*` (NULL = legacy default stream);
+ * no framework types cross the boundary. Every entry point is asynchronous on `stream` except where noted,
  * returns a pk_status (0 = success), and on failure leaves a message for
  * pk_last_error_string(). Shapes and layouts follow the reference:
  *   - matrices are row-major with an explicit leading dimension in elements;
