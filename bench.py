@@ -41,14 +41,17 @@ L2_BYTES = 126 * 2 ** 20
 
 WORKLOADS = {
     # HBM-bound decode GEMMs: metric GB/s of algorithmic bytes
-    "w4a16_decode_m1": dict(kind="w4a16", M=1, N=4096, K=4096),
+    "w4a16_decode_m1": dict(kind="w4a16", M=1, N=4096, K=4096,
+                            ncu_traffic=(8.69e6, "profiles/w4a16_gemv_m1_4096.md")),
     "w4a16_decode_m4": dict(kind="w4a16", M=4, N=4096, K=4096),
     "w4a16_decode_m16": dict(kind="w4a16", M=16, N=4096, K=4096),
     # tensor-bound prefill GEMM: metric TFLOP/s
-    "w4a16_prefill": dict(kind="w4a16", M=4096, N=11008, K=4096),
+    "w4a16_prefill": dict(kind="w4a16", M=4096, N=11008, K=4096,
+                          ncu_traffic=(368e6, "profiles/w4a16_prefill_4096x11008x4096.md")),
     # scaled e4m3 GEMMs: metric TFLOP/s, cast excluded as upstream
     "fp8_2048": dict(kind="fp8", M=2048, N=2048, K=2048),
-    "fp8_4096": dict(kind="fp8", M=4096, N=4096, K=4096),
+    "fp8_4096": dict(kind="fp8", M=4096, N=4096, K=4096,
+                     ncu_traffic=(34.3e6, "profiles/fp8_gemm_4096.md")),
     "fp8_8192": dict(kind="fp8", M=8192, N=8192, K=8192),
     # dense bf16 GEMM, fp32 out (gemm.py:103, the comparison partner of the
     # split-K kernel): metric TFLOP/s
@@ -58,7 +61,8 @@ WORKLOADS = {
     # with NCCL; strong scaling: the layer is fixed, ranks split it
     "llama70b_up_m1": dict(kind="w4a16", M=1, N=28672, K=8192, sharded=True),
     "llama70b_up_m32": dict(kind="w4a16", M=32, N=28672, K=8192, sharded=True),
-    "llama70b_up_m256": dict(kind="w4a16", M=256, N=28672, K=8192, sharded=True),
+    "llama70b_up_m256": dict(kind="w4a16", M=256, N=28672, K=8192, sharded=True,
+                             ncu_traffic=(129.6e6, "profiles/w4a16_skinny_m256_llama70b_up.md")),
     "llama70b_down_m1": dict(kind="w4a16", M=1, N=8192, K=28672, sharded=True),
     "llama70b_down_m32": dict(kind="w4a16", M=32, N=8192, K=28672, sharded=True),
     "llama70b_down_m256": dict(kind="w4a16", M=256, N=8192, K=28672, sharded=True),
@@ -570,6 +574,13 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
             peak = bf16
             peak_note = f"{'sustained' if long_region else 'burst'} bf16 ({peaks['source']})"
         bound, punit = "tensor", "TFLOP/s"
+    # DRAM bytes per launch of the dominant kernel: --traffic, else the figure
+    # of the committed ncu capture of this workload's kernel (single GPU only:
+    # a shard's kernel reads a different slice)
+    traffic, traffic_src = args.traffic, "--traffic" if args.traffic is not None else None
+    if traffic is None and "ncu_traffic" in wl and (world == 1 or not work.sharded):
+        traffic, traffic_src = wl["ncu_traffic"]
+        traffic_src = f"ncu dram__bytes_read.sum + dram__bytes_write.sum, {traffic_src}"
     value = replicas * per * args.steps / sec / scale
     achieved = local_per / sec_per_launch / scale
     e2e_value = replicas * per * e2e_steps / (e2e_ms * 1e-3) / scale
@@ -617,7 +628,8 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
         "config": wl_cfg,
         "roofline": {
             "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": punit,
-            "frac": round(achieved / peak, 4), "peak_source": peak_note, "traffic": args.traffic,
+            "frac": round(achieved / peak, 4), "peak_source": peak_note,
+            "traffic": traffic, "traffic_source": traffic_src,
             ("algorithmic_bytes_per_launch" if work.hbm else "algorithmic_flops_per_launch"): local_per,
             "sms": sms,
         },
