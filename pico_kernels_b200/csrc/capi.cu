@@ -547,9 +547,20 @@ int pk_w4a16_gemm_host(const void* a_host, int a_dtype, int64_t lda, const uint8
     e = cudaMemcpy2DAsync(a_dev, row, a_host, static_cast<size_t>(lda) * 2, row,
                           static_cast<size_t>(M), cudaMemcpyHostToDevice, s);
   if (e != cudaSuccess) return cuda_fail(e, "copy of A to the device");
+  // Shapes the decode kernel supports run on it or on the GEMV, both of
+  // which write their output with plain stores: those go straight to the
+  // page-locked output through its device mapping, and the copy out is not
+  // needed. Other kernels write y_dev.
+  const bool direct_out =
+      y_map != nullptr && decode_supported(M, N, K, group_size, scales, K, a_dev);
   const int st = pk_w4a16_gemm(a_dev, a_dtype, K, wp, scales, scalar_scale, group_size, M, N, K,
-                               y_dev, out_dtype, N, 0, workspace, workspace_bytes, stream);
+                               direct_out ? y_map : y_dev, out_dtype, N, 0, workspace,
+                               workspace_bytes, stream);
   if (st != PK_OK) return st;
+  if (direct_out) {
+    ok();
+    return PK_OK;
+  }
   const int64_t y_bytes = M * N * (out_dtype == PK_F32 ? 4 : 2);
   if (y_map != nullptr)
     e = launch_copy_rows(y_dev, y_bytes, y_map, y_bytes, y_bytes, 1, s);
