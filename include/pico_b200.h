@@ -162,11 +162,13 @@ PK_API int pk_w4a16_gemm_noalloc(const void* a, int a_dtype, int64_t lda, const 
  * memory, in one call: copies A [M, K] from a_host (row stride lda elements)
  * into the device staging buffer a_dev (>= M*K*2 bytes, rows packed to K),
  * runs pk_w4a16_gemm (split_k = 0) into the device staging buffer y_dev
- * (>= M*N elements of out_dtype), then copies y into y_host [M, N]. All three
+ * (>= M*N elements of out_dtype), then copies y into y_host [M, N]. All
  * steps are enqueued on `stream`; synchronise it before reading y_host. With
  * page-locked host buffers (cudaHostAlloc / torch pin_memory) the copies are
- * asynchronous; pageable buffers also work but the copies then block the
- * host. workspace as for pk_w4a16_gemm. This is the host-buffer form of
+ * done by a small kernel on the buffers' device mapping, and for the decode
+ * shapes (those the GEMV or the decode kernel serves) the GEMM writes y_host
+ * directly, leaving y_dev untouched; pageable buffers also work, through
+ * cudaMemcpyAsync, which then blocks the host. workspace as for pk_w4a16_gemm. This is the host-buffer form of
  * gemm_int4.int4_gemm (gemm_int4.py:75-92) with the caller's tensor moves
  * (`a.cuda()`, `c.cpu()`) folded in. */
 PK_API int pk_w4a16_gemm_host(const void* a_host, int a_dtype, int64_t lda, const uint8_t* wp,
