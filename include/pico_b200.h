@@ -6,7 +6,8 @@
  * sizes and a cudaStream_t passed as `void*` (NULL = legacy default stream);
  * no framework types cross the boundary. Every entry point is asynchronous on
  * `stream` except where noted, returns a pk_status (0 = success), and on
- * failure leaves a message for pk_last_error_string(). Shapes and layouts follow the reference:
+ * failure leaves a message for pk_last_error_string(). Shapes and layouts
+ * follow the reference:
  *   - matrices are row-major with an explicit leading dimension in elements;
  *   - packed int4 weights are uint8 [K, N/2], byte [k, j] holding column 2j
  *     in its low nibble and column 2j+1 in its high nibble (gemm_int4.py:65-72);
