@@ -171,3 +171,22 @@ def test_gptq_packed_form_reduces_to_rtn_without_feedback():
     err_g = np.linalg.norm(x @ (wq_gptq - w).T)
     err_r = np.linalg.norm(x @ (wq_rtn - w).T)
     assert err_g < 0.9 * err_r, (err_g, err_r)
+
+
+def test_group_rtn_properties_random_shapes():
+    """Size-independent properties of the oracle's per-group RTN on seeded
+    random shapes (ragged last groups, several group sizes): codes stay in
+    [-7, 7], each group's largest magnitude maps to +-7, every weight lies
+    within half a step of its reconstruction, and packing round-trips."""
+    rng = np.random.default_rng(11)
+    for K, N, g in ((200, 6, 64), (128, 10, 128), (333, 4, 32), (96, 2, 96)):
+        w = (rng.standard_normal((K, N)) * rng.uniform(1e-3, 10)).astype(np.float32)
+        codes, s = o.group_quant_codes(w, g)
+        assert codes.min() >= -7 and codes.max() <= 7
+        rows = np.repeat(np.asarray(s, dtype=np.float32), g, axis=0)[:K]
+        err = np.abs(w - codes.astype(np.float32) * rows)
+        assert np.all(err <= 0.5 * rows * (1 + 1e-5) + 1e-30)
+        for gi in range(0, K, g):
+            blk = np.abs(codes[gi:gi + g])
+            assert np.all(blk.max(axis=0) == 7)
+        assert np.array_equal(o.unpack_int4_n(o.pack_int4_n(codes)), codes)
