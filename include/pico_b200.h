@@ -144,13 +144,18 @@ PK_API int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t*
  * counterpart in the reference. It exists for callers that cannot call
  * cudaMalloc: a runtime that plans all device memory itself and forbids
  * libraries from allocating, or a latency-critical decode loop that cannot
- * afford cudaMalloc's implicit synchronization. Same arguments and result as
+ * afford cudaMalloc's implicit synchronization. Same arguments as
  * pk_w4a16_gemm minus the workspace, for decode shapes only (M <= 32,
- * N % 128 == 0, K % 128 == 0, group 128 or a scalar scale). Its split-K
+ * N % 128 == 0, K % 128 == 0, group 128 or a scalar scale). It always runs
+ * the tensor-core decode kernel with its K splits reduced through memory, so
+ * its output equals pk_w4a16_gemm's with the same explicit split_k bit for
+ * bit, and pk_w4a16_gemm's automatic route (the GEMV at M = 1) within the
+ * W4A16 tolerance. Its split-K
  * partials live in a static 4 MiB device array owned by the library (plus
  * arrival counters for up to 4096 column tiles), held on every GPU that loads
- * the library until exit; a request needing more (tiles * split * M * 512
- * bytes) fails with PK_ERR_WORKSPACE before launching. The first call on a
+ * the library until exit. With split_k = 0 the automatic split is lowered
+ * until tiles * split * M * 512 bytes fit (down to no split); an explicit
+ * split_k that does not fit fails with PK_ERR_WORKSPACE before launching. The first call on a
  * device looks up the array's address; make it before any stream capture.
  * All calls on a device share the array: each clears the counters it uses on
  * its stream, and calls that overlap on the GPU race. */

@@ -625,6 +625,21 @@ int fp8_gemm_impl(const uint8_t* a8, const uint8_t* b8, int64_t M, int64_t N, in
   return PK_OK;
 }
 
+// Kernel of the fused exchange for a shape, or -1 when none has one: decided
+// from the shape alone (aligned stand-in pointers, lda = K), so that every
+// rank of an N-sharded layer reaches the same answer.
+enum { kPathGemv = 0, kPathDecode = 1, kPathSkinny = 2 };
+int sharded_path(int64_t M, int64_t N, int64_t K, int group, bool grouped) {
+  const void* aligned = reinterpret_cast<const void*>(256);
+  const void* sc = grouped ? aligned : nullptr;
+  if (gemv_preferred(M, N, K) && gemv_supported(M, N, K, group, sc, K, aligned, aligned))
+    return kPathGemv;
+  if (decode_supported(M, N, K, group, sc, K, aligned)) return kPathDecode;
+  if (skinny_supported(M, N, K, group, sc, K, aligned) && skinny_preferred(M, N, K))
+    return kPathSkinny;
+  return -1;
+}
+
 }  // namespace
 
 extern "C" {
@@ -791,23 +806,30 @@ int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t
   if (scales != nullptr && group_size <= 0) return fail(PK_ERR_SHAPE, "group_size must be > 0");
   // The same kernel choice as pk_w4a16_gemm's automatic split: the CUDA-core
   // GEMV, the tensor-core decode kernel (M <= 32) or the skinny swap-AB
-  // kernel (32 < M <= 256, where it beats the fused prefill kernel).
-  enum { kGemv, kDecode, kSkinny } path;
-  if (gemv_preferred(M, N, K) && gemv_supported(M, N, K, group_size, scales, lda, a, wp))
-    path = kGemv;
-  else if (decode_supported(M, N, K, group_size, scales, lda, a))
-    path = kDecode;
-  else if (skinny_supported(M, N, K, group_size, scales, lda, a) &&
-           (reinterpret_cast<uintptr_t>(wp) & 15) == 0 && skinny_preferred(M, N, K))
-    path = kSkinny;
-  else
+  // kernel (32 < M <= 256, where it beats the fused prefill kernel). The
+  // choice, and with it the PK_ERR_UNSUPPORTED that sends callers to the NCCL
+  // all-gather, depends on the shape only, so every rank of a layer takes the
+  // same path; a rank whose pointers or leading dimension the chosen kernel
+  // cannot read gets PK_ERR_ALIGN, an error, never a silent fallback that its
+  // peers would not take.
+  const int path = sharded_path(M, N, K, group_size, scales != nullptr);
+  if (path < 0)
     return fail(PK_ERR_UNSUPPORTED,
                 "the fused exchange covers the GEMV, decode and skinny kernels' shapes only");
+  const bool readable =
+      path == kPathGemv     ? gemv_supported(M, N, K, group_size, scales, lda, a, wp)
+      : path == kPathDecode ? decode_supported(M, N, K, group_size, scales, lda, a)
+                            : skinny_supported(M, N, K, group_size, scales, lda, a) &&
+                                  (reinterpret_cast<uintptr_t>(wp) & 15) == 0;
+  if (!readable)
+    return fail(PK_ERR_ALIGN,
+                "sharded W4A16: A, the packed weights and the scales must be 16-byte aligned "
+                "with lda a multiple of 8");
   int split = 1;
   size_t need = kCounterBytes;
-  if (path == kGemv) {
+  if (path == kPathGemv) {
     need = gemv_workspace_bytes(M, N, K);
-  } else if (path == kDecode) {
+  } else if (path == kPathDecode) {
     split = decode_pick_split(M, N, K);
     if (split > K / 128) split = static_cast<int>(K / 128);
     need = decode_workspace_bytes(M, N, K, split);
@@ -851,8 +873,8 @@ int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t
   }
   sh.done = ws_counters(workspace) + (kMaxCounters - 1);
   const char* why = "";
-  cudaError_t e = path == kGemv     ? launch_w4a16_gemv(p, as_stream(stream), &why, &sh)
-                  : path == kDecode ? launch_w4a16_decode(p, as_stream(stream), &why, &sh)
+  cudaError_t e = path == kPathGemv     ? launch_w4a16_gemv(p, as_stream(stream), &why, &sh)
+                  : path == kPathDecode ? launch_w4a16_decode(p, as_stream(stream), &why, &sh)
                                     : launch_w4a16_skinny(p, as_stream(stream), &why, &sh);
   if (e == cudaErrorInvalidValue && why[0] != '\0') return fail(PK_ERR_ALIGN, "%s", why);
   if (e != cudaSuccess) return cuda_fail(e, "sharded w4a16 gemm launch");

@@ -12,10 +12,16 @@
 // Contract:
 //   * decode shapes only (what pk_w4a16_gemm runs on its decode path: M <= 32,
 //     N % 128 == 0, K % 128 == 0, group 128 or a scalar scale);
+//   * the kernel is always the tensor-core decode kernel reducing its K
+//     splits through the scratch (never the GEMV that pk_w4a16_gemm picks at
+//     M = 1): its result equals pk_w4a16_gemm's with the same explicit split_k
+//     bit for bit, and pk_w4a16_gemm's automatic route within the W4A16
+//     tolerance;
 //   * the reduction scratch a call needs -- tiles * split * M * 128 fp32
 //     partials -- must fit kNoAllocPartialBytes (4 MiB) and the tile count
-//     kNoAllocMaxTiles; larger requests fail with PK_ERR_WORKSPACE and launch
-//     nothing;
+//     kNoAllocMaxTiles. With split_k = 0 the automatic split is lowered until
+//     it fits (down to 1, which needs no scratch); an explicit split_k that
+//     does not fit fails with PK_ERR_WORKSPACE and launches nothing;
 //   * the first call on each device looks up the array's device address
 //     (cudaGetSymbolAddress, with that device current); make that first call
 //     before any stream capture;
@@ -90,7 +96,14 @@ extern "C" PK_API int pk_w4a16_gemm_noalloc(const void* a, int a_dtype, int64_t 
   int split = split_k > 0 ? split_k : decode_pick_split(M, N, K);
   if (split > K / 128) split = static_cast<int>(K / 128);
   const int64_t tiles = N / 128;
-  const size_t partial_bytes = static_cast<size_t>(tiles) * split * M * 128 * sizeof(float);
+  const size_t per_split = static_cast<size_t>(tiles) * M * 128 * sizeof(float);
+  if (split_k == 0 && split > 1) {
+    // The automatic split shrinks to what the scratch holds (down to no split,
+    // which needs none); only a split the caller asked for is rejected.
+    const int64_t fit = tiles > kNoAllocMaxTiles ? 1 : static_cast<int64_t>(kNoAllocPartialBytes / per_split);
+    if (fit < split) split = fit < 1 ? 1 : static_cast<int>(fit);
+  }
+  const size_t partial_bytes = per_split * split;
   if (split > 1 && (tiles > kNoAllocMaxTiles || partial_bytes > kNoAllocPartialBytes))
     return fail(PK_ERR_WORKSPACE,
                 "request exceeds the static split-K scratch (4 MiB of partials, 4096 tiles); "

@@ -75,6 +75,17 @@ def gather_columns(local: torch.Tensor, world: int,
     return y
 
 
+def _readable(t: torch.Tensor) -> torch.Tensor:
+    """``t`` in the layout the sharded kernels read: unit stride along the
+    last dimension, a row stride of 16 bytes' multiple and a 16-byte aligned
+    start (a fresh copy when the tensor is a view that misses one)."""
+    elem = t.element_size()
+    if (t.stride(-1) == 1 and (t.stride(0) * elem) % 16 == 0 and t.stride(0) >= t.shape[1]
+            and t.data_ptr() % 16 == 0):
+        return t
+    return t.clone(memory_format=torch.contiguous_format)
+
+
 class _DeviceArray:
     """Zero-copy view of raw device memory for torch.as_tensor."""
 
@@ -139,13 +150,36 @@ class PeerExchange:
         """This rank's slice of ``A @ dequant(W)`` written to every rank's buffer.
 
         Returns ``[M, n_full]`` (valid until two calls later), or None when
-        no kernel with the fused exchange covers the shape (every rank gets
-        None: the choice depends on the shape only).
+        no kernel with the fused exchange covers the shape. Every rank of the
+        layer gets the same answer: the library decides from the shape alone
+        (``pk_w4a16_gemm_sharded``), and the operands are first brought into
+        the layout its kernels read (contiguous, 16-byte aligned, scales in
+        A's dtype), so a rank cannot fall back to the all-gather on its own
+        while its peers wait in the fused kernel.
         """
+        _lib.require_cuda(a, packed_shard, scales_shard)
+        for t in (a, packed_shard, scales_shard):
+            if t.device != self.device:
+                raise _lib.DtypeError(f"operands must be on {self.device} (got {t.device})")
+        if a.dtype not in (torch.float16, torch.bfloat16):
+            raise _lib.DtypeError(f"a must be fp16 or bf16 (got {a.dtype})")
+        if packed_shard.dtype != torch.uint8:
+            raise _lib.DtypeError("packed_shard must be uint8")
+        if a.dim() != 2 or packed_shard.dim() != 2 or scales_shard.dim() != 2:
+            raise _lib.ShapeError("a, packed_shard and scales_shard must be 2-D")
         M, K = a.shape
         n_local = scales_shard.shape[1]
+        if packed_shard.shape != (K, n_local // 2) or n_local % 2:
+            raise _lib.ShapeError(f"packed_shard must be [{K}, {n_local // 2}] "
+                                  f"(got {tuple(packed_shard.shape)})")
+        if scales_shard.shape[0] != (K + group_size - 1) // group_size:
+            raise _lib.ShapeError(f"scales_shard must have ceil(K / {group_size}) rows")
         if M > self.max_m or n_local * self.world != self.n_full:
             return None
+        a = _readable(a)
+        packed_shard = _readable(packed_shard)
+        scales_shard = _readable(scales_shard if scales_shard.dtype == a.dtype
+                                 else scales_shard.to(a.dtype))
         ws_bytes = max(self.lib.pk_w4a16_workspace_size(M, n_local, K, 0), 1 << 16)
         ws = _lib.workspace(a.device, ws_bytes, tag="sharded")
         self.calls += 1
@@ -153,10 +187,9 @@ class PeerExchange:
         outs = (ctypes.c_uint64 * self.world)(*[b + parity * self.buf_bytes for b in self.bases])
         flags = (ctypes.c_uint64 * self.world)(*[b + self.flag_off for b in self.bases])
         outs_p, flags_p = ctypes.addressof(outs), ctypes.addressof(flags)
-        scales = scales_shard if scales_shard.dtype == a.dtype else scales_shard.to(a.dtype)
         rc = self.lib.pk_w4a16_gemm_sharded(
             a.data_ptr(), _lib.dtype_code(a.dtype), a.stride(0), packed_shard.data_ptr(),
-            scales.data_ptr(), 1.0, group_size, M, n_local, K, _lib.dtype_code(self.dtype),
+            scales_shard.data_ptr(), 1.0, group_size, M, n_local, K, _lib.dtype_code(self.dtype),
             self.n_full, self.rank * n_local, self.world, self.rank, outs_p, flags_p,
             ws.data_ptr(), ws.numel(), _lib.stream_of(a))
         if rc == _lib.PK_ERR_UNSUPPORTED:

@@ -88,6 +88,19 @@ def test_host_only_calls_work_without_gpu():
     assert sharded_call(rank=2) == _lib.PK_ERR_SHAPE
     assert sharded_call(n_offset=1536) == _lib.PK_ERR_SHAPE
     assert sharded_call(M=300) == _lib.PK_ERR_UNSUPPORTED
+    # the fused-or-NCCL choice depends on the shape only: a misaligned A or
+    # leading dimension on a covered shape is an error (never UNSUPPORTED,
+    # which would send this rank alone to the all-gather), and an uncovered
+    # shape is UNSUPPORTED whatever the pointers
+    assert sharded_call(a=4098) == _lib.PK_ERR_ALIGN
+    assert sharded_call(lda=1025) == _lib.PK_ERR_ALIGN
+    assert sharded_call(wp=4100) == _lib.PK_ERR_ALIGN
+    assert sharded_call(M=300, a=4098) == _lib.PK_ERR_UNSUPPORTED
+    assert sharded_call(M=64, N=256, K=256, ldo=512, a=4098) in (_lib.PK_ERR_UNSUPPORTED,
+                                                                 _lib.PK_ERR_ALIGN)
+    assert sharded_call(M=64, N=256, K=256, ldo=512, a=4098) == \
+        (_lib.PK_ERR_UNSUPPORTED if sharded_call(M=64, N=256, K=256, ldo=512, ws=None)
+         == _lib.PK_ERR_UNSUPPORTED else _lib.PK_ERR_ALIGN)
 
 
 def test_workspace_size_is_host_only():

@@ -107,3 +107,54 @@ def test_shard_columns_rules():
     assert sharded.shard_columns(8192, 8, 0) == (0, 1024)
     with pytest.raises(ValueError):
         sharded.shard_columns(1000, 8, 0)
+
+
+def _decision_worker(rank, world, port, q):
+    """Each rank asks the library to run its slice of the same layer; rank 1's
+    activations start 2 bytes off a 16-byte boundary (a view with an offset).
+    No rank may be told UNSUPPORTED (the signal to fall back to the NCCL
+    all-gather) unless every rank is: the aligned rank reaches the workspace
+    check (it would launch the fused kernel), the misaligned one gets an
+    error. Fake pointers: every call returns before touching a GPU."""
+    import ctypes
+
+    from pico_kernels_b200 import _lib
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        lib = _lib.load()
+        outs = (ctypes.c_uint64 * world)(*[4096 * (r + 1) for r in range(world)])
+        flags = (ctypes.c_uint64 * world)(*[1 << 20 + r for r in range(world)])
+        codes = {}
+        for M, N, K in ((1, 3584, 8192), (32, 1024, 28672), (300, 1024, 1024)):
+            a = 4096 + (2 if rank == 1 else 0)
+            codes[M] = lib.pk_w4a16_gemm_sharded(
+                a, _lib.PK_BF16, K, 8192, 16384, 1.0, 128, M, N, K, _lib.PK_F32, N * world,
+                rank * N, world, rank, ctypes.addressof(outs), ctypes.addressof(flags), None, 0,
+                None)
+        got = [None] * world
+        dist.all_gather_object(got, codes)
+        q.put((rank, got))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fused_exchange_decision_agrees_across_gloo_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_decision_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    rank, got = q.get(timeout=5)
+    from pico_kernels_b200 import _lib
+    for M in (1, 32, 300):
+        unsupported = [g[M] == _lib.PK_ERR_UNSUPPORTED for g in got]
+        assert all(unsupported) or not any(unsupported), (M, [g[M] for g in got])
+    assert got[0][1] == _lib.PK_ERR_WORKSPACE and got[1][1] == _lib.PK_ERR_ALIGN
+    assert got[0][32] == _lib.PK_ERR_WORKSPACE and got[1][32] == _lib.PK_ERR_ALIGN
+    assert got[0][300] == got[1][300] == _lib.PK_ERR_UNSUPPORTED
