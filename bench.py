@@ -4,19 +4,23 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload NAME]
 
-Default workload: W4A16 decode GEMM, Llama-7B q_proj shape (M=1, K=N=4096,
-int4 weights with group-128 bf16 scales, bf16 activations, fp32 output) --
-the configuration BASELINE.json's headline metric is quoted on. A step is
-one GEMM over one set of weights; 32 rotating weight sets (277 MB) keep every
-step's weights out of the 126 MB L2. Steps are launched from CUDA graphs.
+Default workload on one GPU: W4A16 decode GEMM, Llama-7B q_proj shape (M=1,
+K=N=4096, int4 weights with group-128 bf16 scales, bf16 activations, fp32
+output) -- the configuration BASELINE.json's headline metric is quoted on. A
+step is one GEMM over one set of weights; rotating weight sets (> 2x the
+126 MB L2) keep every step's weights out of L2. Steps are launched from CUDA
+graphs; each graph is replayed once before the timed region.
 
-Multi-GPU (torchrun, one process per GPU): the GEMMs are independent, so each
-rank runs its own stream of steps (weak scaling, no data-path collective);
-time is the max over ranks. The sharded Llama-70B configurations with an
-NCCL all-gather of the output are separate workloads (--workload llama70b_*).
+Default workload on N > 1 GPUs (torchrun, one process per GPU): the
+Llama-70B up_proj layer at M=1 (K=8192, N=28672) with
+its columns sharded over the ranks and the output exchanged inside the
+kernel over NVLink (strong scaling). Rank 0 first times the same layer on
+its GPU alone (``strong_scaling``), and after the timed region every rank
+checks its assembled [M, N] output against the unsharded GEMM on its own GPU
+(``parity``). Time is the max over ranks.
 
---impl reference times the reference's CPU path (the numpy restatement in
-oracle/, dequantize-then-matmul in fp32) on the host cores, rank 0 only.
+--impl reference times the reference's CPU torch computation of the same
+workload (oracle/cpu_reference.py) on all host cores, rank 0 only.
 """
 
 from __future__ import annotations
@@ -30,7 +34,6 @@ import threading
 import time
 from pathlib import Path
 
-import numpy as np
 import torch
 
 ROOT = Path(__file__).resolve().parent
@@ -41,17 +44,14 @@ L2_BYTES = 126 * 2 ** 20
 
 WORKLOADS = {
     # HBM-bound decode GEMMs: metric GB/s of algorithmic bytes
-    "w4a16_decode_m1": dict(kind="w4a16", M=1, N=4096, K=4096,
-                            ncu_traffic=(8.69e6, "profiles/w4a16_gemv_m1_4096.md")),
+    "w4a16_decode_m1": dict(kind="w4a16", M=1, N=4096, K=4096, ncu_traffic=8.69e6),
     "w4a16_decode_m4": dict(kind="w4a16", M=4, N=4096, K=4096),
     "w4a16_decode_m16": dict(kind="w4a16", M=16, N=4096, K=4096),
     # tensor-bound prefill GEMM: metric TFLOP/s
-    "w4a16_prefill": dict(kind="w4a16", M=4096, N=11008, K=4096,
-                          ncu_traffic=(368e6, "profiles/w4a16_prefill_4096x11008x4096.md")),
+    "w4a16_prefill": dict(kind="w4a16", M=4096, N=11008, K=4096, ncu_traffic=368e6),
     # scaled e4m3 GEMMs: metric TFLOP/s, cast excluded as upstream
     "fp8_2048": dict(kind="fp8", M=2048, N=2048, K=2048),
-    "fp8_4096": dict(kind="fp8", M=4096, N=4096, K=4096,
-                     ncu_traffic=(34.3e6, "profiles/fp8_gemm_4096.md")),
+    "fp8_4096": dict(kind="fp8", M=4096, N=4096, K=4096, ncu_traffic=34.3e6),
     "fp8_8192": dict(kind="fp8", M=8192, N=8192, K=8192),
     # dense bf16 GEMM, fp32 out (gemm.py:103, the comparison partner of the
     # split-K kernel): metric TFLOP/s
@@ -62,13 +62,14 @@ WORKLOADS = {
     "llama70b_up_m1": dict(kind="w4a16", M=1, N=28672, K=8192, sharded=True),
     "llama70b_up_m32": dict(kind="w4a16", M=32, N=28672, K=8192, sharded=True),
     "llama70b_up_m256": dict(kind="w4a16", M=256, N=28672, K=8192, sharded=True,
-                             ncu_traffic=(129.6e6, "profiles/w4a16_skinny_m256_llama70b_up.md")),
+                             ncu_traffic=129.6e6),
     "llama70b_down_m1": dict(kind="w4a16", M=1, N=8192, K=28672, sharded=True),
     "llama70b_down_m32": dict(kind="w4a16", M=32, N=8192, K=28672, sharded=True),
     "llama70b_down_m256": dict(kind="w4a16", M=256, N=8192, K=28672, sharded=True),
     "llama70b_up_fp8_m4096": dict(kind="fp8", M=4096, N=28672, K=8192, sharded=True),
 }
 DEFAULT_WORKLOAD = "w4a16_decode_m1"
+DEFAULT_SHARDED_WORKLOAD = "llama70b_up_m1"  # the default under torchrun (N > 1)
 
 
 def is_hbm_bound(wl: dict) -> bool:
@@ -202,6 +203,50 @@ def barrier(dist):
 # ---------------------------------------------------------------------------
 # workloads: device buffers, one step through the C ABI, algorithmic work
 # ---------------------------------------------------------------------------
+def input_sets(wl: dict, world: int) -> tuple[int, int]:
+    """(rotating input sets, bytes per set) so that one pass over the sets
+    reads more than twice the L2 on every rank."""
+    M, N, K = wl["M"], wl["N"], wl["K"]
+    NL = N // world if wl.get("sharded") else N
+    if wl["kind"] == "w4a16":
+        per_set = K * NL // 2 + (K // 128) * NL * 2 + M * K * 2
+    elif wl["kind"] == "dense":
+        per_set = (M * K + K * NL) * 2
+    else:
+        per_set = M * K + K * NL
+    return max(2, int(2 * L2_BYTES // per_set) + 1), per_set
+
+
+def workload_config(name: str, wl: dict, world: int) -> dict:
+    """The workload's identity, the same in both arms' lines: shape, data
+    types, input rotation and how the GPUs share it."""
+    M, N, K = wl["M"], wl["N"], wl["K"]
+    cfg = {"workload": name, "M": M, "N": N, "K": K}
+    if wl["kind"] == "w4a16":
+        cfg.update({"group_size": 128, "weights": "int4 packed [K, N/2] + bf16 scales [K/128, N]",
+                    "activations": "bf16", "output": "fp32"})
+    elif wl["kind"] == "dense":
+        cfg.update({"inputs": "bf16 [M,K] x bf16 [K,N]", "output": "fp32"})
+    else:
+        cfg.update({"inputs": "e4m3 [M,K] x e4m3 [K,N], per-tensor scales",
+                    "output": "bf16 (rescaled in the epilogue)",
+                    "cast": "excluded from the timed region (gemm_fp8.py:144)"})
+    sharded = bool(wl.get("sharded"))
+    n_sets, set_bytes = input_sets(wl, world)
+    if sharded and world > 1:
+        par = f"N sharded over {world} GPUs ({N // world} columns each), output assembled on every GPU"
+    elif sharded:
+        par = "single GPU (unsharded)"
+    else:
+        par = f"replicas x{world}" if world > 1 else "single GPU"
+    cfg.update({
+        "l2": f"{n_sets} rotating input sets per GPU ({n_sets * set_bytes / 2**20:.0f} MiB > 126 MiB L2)",
+        "launch": "CUDA graphs of back-to-back steps",
+        "parallelism": par,
+    })
+    return cfg
+
+
 class Workload:
     """Rotating input sets (so each step's inputs are not L2-resident) and the
     step that runs one GEMM on set i through the C ABI.
@@ -232,14 +277,7 @@ class Workload:
             raise ValueError(f"N={N} does not shard over {self.world} ranks")
         self.NL = N // self.world                      # local columns
         n0 = self.rank * self.NL
-        if self.kind == "w4a16":
-            per_set = K * self.NL // 2 + (K // 128) * self.NL * 2 + M * K * 2
-        elif self.kind == "dense":
-            per_set = (M * K + K * self.NL) * 2
-        else:
-            per_set = M * K + K * self.NL
-        self.n_sets = max(2, int(2 * L2_BYTES // per_set) + 1)
-        self.set_bytes = per_set
+        self.n_sets, self.set_bytes = input_sets(wl, self.world)
         g = torch.Generator(device=device).manual_seed(0)
         self.sets = []
         import pico_kernels_b200 as pk
@@ -249,7 +287,9 @@ class Workload:
                 w = (torch.randn(K, N, device=device, generator=g) * 0.02).to(torch.bfloat16)
                 packed, scales = pk.quantize_int4_grouped(w, 128)
                 del w
-                if self.sharded:
+                if self.sharded and self.world > 1:
+                    if not self.sets:  # the whole layer of set 0, for the parity check
+                        self.full0 = (packed, scales)
                     packed = packed[:, n0 // 2:(n0 + self.NL) // 2].contiguous()
                     scales = scales[:, n0:n0 + self.NL].contiguous()
                 a = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
@@ -343,6 +383,28 @@ class Workload:
 
     def fused_step(self, i: int) -> None:
         self._lib.check(self.fused_call(i), self.name + " (fused exchange)")
+
+    def step_output(self, i: int) -> torch.Tensor:
+        """Run one step on set ``i`` and return this rank's assembled [M, N]."""
+        if self.exchange is not None:
+            self.fused_step(i)
+            return self.exchange.output(self.ex_calls & 1, self.M)
+        out = self.gemm(i)
+        if not (self.sharded and self.world > 1):
+            return out
+        self.all_gather(out)
+        return self.gather.view(1, self.N) if self.M == 1 else self.full
+
+    def parity(self) -> float:
+        """Relative Frobenius difference between this rank's assembled output of
+        set 0 and the unsharded GEMM of the whole layer on this GPU."""
+        import pico_kernels_b200 as pk
+        a = self.sets[0][0]
+        packed, scales = self.full0
+        ref = pk.int4_gemm(a, packed, scales, group_size=128)
+        y = self.step_output(0).float()
+        torch.cuda.synchronize()
+        return float(torch.norm(y - ref) / torch.norm(ref))
 
     def step(self, i: int) -> None:
         if self.exchange is not None:
@@ -447,20 +509,56 @@ def capture_runner(step_fn, n_sets: int, steps: int, chunk: int = 1000):
     return (graph_for(chunk) if full else None), full, (graph_for(rem) if rem else None)
 
 
-def _time_graphs(runner_out, dist) -> float:
-    """Replay (graph, n, remainder) on the device; return ms (max over ranks)."""
+def _replay(runner_out) -> None:
     g, n, grem = runner_out
-    barrier(dist)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
     for _ in range(n):
         g.replay()
     if grem is not None:
         grem.replay()
+
+
+def _prime(runner_out) -> None:
+    """Replay each graph of a runner once, untimed: a graph's first launch
+    uploads it to the device, which must not land in the timed region."""
+    g, n, grem = runner_out
+    if g is not None and n:
+        g.replay()
+    if grem is not None:
+        grem.replay()
+    torch.cuda.synchronize()
+
+
+def _time_graphs(runner_out, dist) -> float:
+    """Replay (graph, n, remainder) on the device; return ms (max over ranks)."""
+    _prime(runner_out)
+    barrier(dist)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    _replay(runner_out)
     e1.record()
     torch.cuda.synchronize()
     return max_over_ranks(dist, e0.elapsed_time(e1))
+
+
+def single_gpu_leg(args, wl: dict, device: torch.device) -> dict:
+    """The whole sharded layer on this GPU alone (before the process group
+    forms), timed like the sharded run: the strong-scaling reference point."""
+    work = Workload(args.workload, wl, device, args.split_k, world=1, rank=0)
+    steps = max(args.warmup, min(args.steps, 2000 if work.hbm else 50))
+    chunk = 1000 if work.hbm else 20
+    warm = capture_runner(work.step, work.n_sets, args.warmup, chunk)
+    _replay(warm)
+    timed = capture_runner(work.step, work.n_sets, steps, chunk)
+    ms = _time_graphs(timed, None)
+    per = work.bytes_per_step() if work.hbm else work.flops_per_step()
+    us = ms / steps * 1e3
+    out = {"single_gpu_us": round(us, 3), "steps": steps,
+           "single_gpu_value": round(per / (us * 1e-6) / (1e9 if work.hbm else 1e12), 3)}
+    del warm, timed, work
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
@@ -468,21 +566,19 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    sharded_run = bool(wl.get("sharded")) and world > 1
+    strong = single_gpu_leg(args, wl, device) if sharded_run and rank == 0 else None
     dist = init_dist(world, local)
     peaks = load_peaks()
     work = Workload(args.workload, wl, device, args.split_k, world, rank, dist,
                     exchange=args.exchange == "fused")
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     chunk = 1000 if work.hbm else 20
-    gathered = work.sharded and world > 1
 
     warm = capture_runner(work.step, work.n_sets, args.warmup, chunk)
-    for _ in range(warm[1]):
-        warm[0].replay()
-    if warm[2] is not None:
-        warm[2].replay()
+    _replay(warm)
     timed = capture_runner(work.step, work.n_sets, args.steps, chunk)
-    torch.cuda.synchronize()
+    _prime(timed)  # exactly `steps` GEMMs are timed below, from warm graphs
 
     clocks = ClockSampler(local)
     clocks.start()
@@ -492,10 +588,7 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
     ev0.record()
-    for _ in range(timed[1]):
-        timed[0].replay()
-    if timed[2] is not None:
-        timed[2].replay()
+    _replay(timed)
     ev1.record()
     torch.cuda.synchronize()
     t1 = time.perf_counter()
@@ -507,29 +600,39 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
     if code != 0:
         raise RuntimeError(f"device status {code} at site {where}")
 
-    # sharded layers: time the local GEMM and the all-gather on their own too
-    breakdown = None
+    # sharded layers: every rank's assembled output against the unsharded GEMM
+    # on its own GPU (outside the timed region), and the step's parts timed alone
+    parity = breakdown = None
     gemm_ms_local = ms
-    if gathered:
+    if sharded_run:
+        rel = work.parity() if work.kind == "w4a16" else 0.0
+        code_p, where_p = pk.device_status()
+        parity = {"rel_frobenius_max_over_ranks": max_over_ranks(dist, rel),
+                  "bar": 1e-5, "device_status": [code_p, where_p],
+                  "against": "pk.int4_gemm of the whole layer (set 0) on each rank's GPU"}
         nb = min(args.steps, 1000 if work.hbm else 50)
         g_gemm = capture_runner(work.gemm_only, work.n_sets, nb, chunk)
         g_gath = capture_runner(work.gather_only, work.n_sets, nb, chunk)
         gemm_ms = _time_graphs(g_gemm, dist)
         gath_ms = _time_graphs(g_gath, dist)
         gemm_ms_local = gemm_ms * args.steps / nb
-        breakdown = {"gemm_us": round(gemm_ms / nb * 1e3, 3),
-                     "allgather_us": round(gath_ms / nb * 1e3, 3), "steps": nb}
+        step_us = ms_max / args.steps * 1e3
+        breakdown = {"step_us": round(step_us, 3), "local_gemm_us": round(gemm_ms / nb * 1e3, 3),
+                     "nccl_allgather_us": round(gath_ms / nb * 1e3, 3), "steps": nb}
         if work.exchange is not None:
+            breakdown["exchange_us"] = round(step_us - gemm_ms / nb * 1e3, 3)
             breakdown["step"] = ("one kernel per rank: the local GEMM stores its columns into "
                                  "every rank's output over NVLink and ends with a flag barrier; "
-                                 "gemm_us / allgather_us time the unfused local GEMM and an "
-                                 "NCCL all-gather of its output for comparison")
+                                 "exchange_us = step_us - local_gemm_us; nccl_allgather_us times "
+                                 "an NCCL all-gather of the same output for comparison")
+        else:
+            breakdown["step"] = "the local GEMM, then an NCCL all-gather of its output"
         del g_gemm, g_gath
 
     # end to end through the public API, host buffers in and out every step
     e2e_fn, h2d, d2h = work.e2e_step_fn()
-    e2e_steps = min(args.steps, args.e2e_steps if work.hbm else max(3, args.e2e_steps // 100))
-    for i in range(3):
+    e2e_steps = args.e2e_steps if work.hbm else max(3, args.e2e_steps // 100)
+    for i in range(20 if work.hbm else 3):
         e2e_fn(i)
     torch.cuda.synchronize()
     barrier(dist)
@@ -575,42 +678,20 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
             peak_note = f"{'sustained' if long_region else 'burst'} bf16 ({peaks['source']})"
         bound, punit = "tensor", "TFLOP/s"
     # DRAM bytes per launch of the dominant kernel: --traffic, else the figure
-    # of the committed ncu capture of this workload's kernel (single GPU only:
-    # a shard's kernel reads a different slice)
+    # of an ncu capture of this workload's kernel (single GPU only: a shard's
+    # kernel reads a different slice)
     traffic, traffic_src = args.traffic, "--traffic" if args.traffic is not None else None
     if traffic is None and "ncu_traffic" in wl and (world == 1 or not work.sharded):
-        traffic, traffic_src = wl["ncu_traffic"]
-        traffic_src = f"ncu dram__bytes_read.sum + dram__bytes_write.sum, {traffic_src}"
+        traffic = wl["ncu_traffic"]
+        traffic_src = "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel"
     value = replicas * per * args.steps / sec / scale
     achieved = local_per / sec_per_launch / scale
     e2e_value = replicas * per * e2e_steps / (e2e_ms * 1e-3) / scale
-    wl_cfg = {"workload": args.workload, "M": work.M, "N": work.N, "K": work.K}
-    if work.kind == "w4a16":
-        wl_cfg.update({"group_size": 128, "weights": "int4 packed [K, N/2] + bf16 scales [K/128, N]",
-                       "activations": "bf16", "output": "fp32",
-                       "split_k": args.split_k if args.split_k > 0 else "auto"})
-    elif work.kind == "dense":
-        wl_cfg.update({"inputs": "bf16 [M,K] x bf16 [K,N]", "output": "fp32"})
-    else:
-        wl_cfg.update({"inputs": "e4m3 [M,K] x e4m3 [K,N], per-tensor scales",
-                       "output": "bf16 (rescaled in the epilogue)",
-                       "cast": "excluded from the timed region (gemm_fp8.py:144)"})
-    if work.sharded:
-        if world == 1:
-            par = "single GPU (unsharded)"
-        elif work.exchange is not None:
-            par = (f"N sharded over {world} GPUs ({work.NL} columns each), output exchanged inside "
-                   "the local GEMM kernel (NVLink peer stores + flag barrier)")
-        else:
-            par = f"N sharded over {world} GPUs ({work.NL} columns each), NCCL all-gather of the output"
-    
-    else:
-        par = f"replicas x{world}" if world > 1 else "single GPU"
-    wl_cfg.update({
-        "l2": f"{work.n_sets} rotating input sets per GPU ({work.n_sets * work.set_bytes / 2**20:.0f} MiB > 126 MiB L2)",
-        "launch": "CUDA graphs of back-to-back steps",
-        "parallelism": par,
-    })
+    wl_cfg = workload_config(args.workload, wl, world)
+    path = {"split_k": args.split_k if args.split_k > 0 else "auto"}
+    if sharded_run:
+        path["exchange"] = ("inside the local kernel (NVLink peer stores + flag barrier)"
+                            if work.exchange is not None else "NCCL all_gather_into_tensor")
     line = {
         "metric": METRIC,
         "value": round(value, 3),
@@ -626,6 +707,7 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
         "dtype": "e4m3" if work.kind == "fp8" else "bf16",
         "data": "synthetic (seeded N(0,0.02) weights quantized on device, N(0,1) activations)",
         "config": wl_cfg,
+        "path": path,
         "roofline": {
             "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": punit,
             "frac": round(achieved / peak, 4), "peak_source": peak_note,
@@ -638,11 +720,15 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
                 "us_per_step": round(e2e_ms / e2e_steps * 1e3, 3),
                 "path": ("pico_kernels_b200.int4_gemm_host -> pk_w4a16_gemm_host (H2D of A, "
                          "the GEMM and D2H of y in one C-ABI call), pinned host buffers"
-                         if work.kind == "w4a16" and not (work.sharded and world > 1) else
+                         if work.kind == "w4a16" and not sharded_run else
                          "pico_kernels_b200 public API (ctypes C ABI), pinned host buffers")},
         "gpu_launches": args.steps,
         "clocks": clocks.summary(t0, t1),
     }
+    if strong is not None:
+        line["strong_scaling"] = strong
+    if parity is not None:
+        line["parity"] = parity
     if breakdown is not None:
         line["breakdown"] = breakdown
     if world == 1 and not args.no_cpu_baseline:
@@ -653,88 +739,39 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
 
 
 # ---------------------------------------------------------------------------
-# CPU reference path (the oracle's restatement of the reference's torch path)
+# CPU reference path: the reference's torch computation (oracle/cpu_reference)
 # ---------------------------------------------------------------------------
-def _cpu_threads() -> int:
-    try:
-        from threadpoolctl import threadpool_info
-        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
-        return max(n) if n else 1
-    except Exception:  # noqa: BLE001
-        return os.cpu_count() or 1
-
-
 def cpu_baseline(wl: dict, budget_s: float = 10.0) -> dict:
-    """Time the reference's CPU path on a bounded sample of the workload.
-
-    W4A16: unpack + dequantize + fp32 matmul (tests/test_gemm_int4.py:26);
-    fp8: (a8.float()/sa) @ (b8.float()/sb) (gemm_fp8.py:132); dense: fp32
-    matmul of the bf16 inputs (gemm.py:134-142). Large GEMMs are
-    sampled by output rows; the rate is scaled to the full step's unit.
-    """
-    from oracle import quant_ref as o
+    """Time the reference's CPU torch computation of one step of the workload
+    on all host cores: the whole GEMM (weight dequantization + fp32 matmul),
+    on a bounded column sample of large layers, scaled to all N columns."""
+    from oracle import cpu_reference as ref
+    cores = ref.use_all_cores()
     M, N, K = wl["M"], wl["N"], wl["K"]
-    rng = np.random.default_rng(0)
-    rows = M if M <= 16 else max(16, min(M, int(2e9 // (2 * N * K)) or 16))
-    if wl["kind"] == "w4a16":
-        w = rng.standard_normal((K, N), dtype=np.float32) * 0.02
-        codes, s32 = o.group_quant_codes(w, 128)
-        packed = o.pack_int4_n(codes)
-        scales = o.store_scales(s32, "bf16")
-        a = o.round_to_bf16(rng.standard_normal((rows, K), dtype=np.float32))
-
-        def once():  # per step: unpack + dequantize the weights
-            return o.dequant_weight(o.unpack_int4_n(packed), scales, 128)
-
-        def per_rows(wd):  # fp32 matmul of `rows` activation rows
-            return a @ wd
-    elif wl["kind"] == "dense":
-        a = o.round_to_bf16(rng.standard_normal((rows, K), dtype=np.float32))
-        b = o.round_to_bf16(rng.standard_normal((K, N), dtype=np.float32))
-
-        def once():
-            return b
-
-        def per_rows(bd):  # gemm.py:134-142 checks against a.float() @ b.float()
-            return a @ bd
+    # columns whose step is ~1e10 flops / 6.4e7 weights at most (whole N when it fits)
+    cap = min(int(1e10 // (2 * M * K)), int(64 * 2**20 // K))
+    cols = N if N <= cap else max(128, cap // 128 * 128)
+    kind = wl["kind"]
+    if kind == "w4a16":
+        step = ref.W4A16Step(M, K, cols)
+        what = "q.float() * scales (group 128, repeat_interleave along K), then A.float() @ W"
+    elif kind == "fp8":
+        step = ref.Fp8Step(M, K, cols)
+        what = "(a8.float() / sa) @ (b8.float() / sb)"
     else:
-        a8, sa = o.fp8_quantize(rng.standard_normal((rows, K), dtype=np.float32), "bf16")
-        b8, sb = o.fp8_quantize(rng.standard_normal((K, N), dtype=np.float32), "bf16")
-
-        def once():
-            return o.e4m3_bits_to_f32(b8) / np.float32(sb)
-
-        def per_rows(bd):
-            return (o.e4m3_bits_to_f32(a8) / np.float32(sa)) @ bd
-    n = 0
-    t_once = t_rows = 0.0
-    t0 = time.perf_counter()
-    while True:
-        ta = time.perf_counter()
-        wd = once()
-        tb = time.perf_counter()
-        per_rows(wd)
-        tc = time.perf_counter()
-        t_once += tb - ta
-        t_rows += tc - tb
-        n += 1
-        el = tc - t0
-        if el >= budget_s and n >= 2:
-            break
-    prep = {"w4a16": "weight dequant", "fp8": "B e4m3 -> f32", "dense": "no weight prep"}[wl["kind"]]
-    # one full step = one dequant + the matmul over all M rows
-    sec_per_step = t_once / n + (t_rows / n) * (M / rows)
-    hbm = is_hbm_bound(wl)
-    if hbm:
+        step = ref.DenseStep(M, K, cols)
+        what = "a.float() @ b.float()"
+    sec, n = ref.time_steps(step, budget_s)
+    sec_per_step = sec * N / cols
+    if is_hbm_bound(wl):
         per = K * N // 2 + (K // 128) * N * 2 + M * K * 2 + M * N * 4
         value, unit = per / sec_per_step / 1e9, "GB/s"
     else:
         value, unit = 2 * M * N * K / sec_per_step / 1e12, "TFLOP/s"
-    return {"value": round(value, 6), "unit": unit, "cores": _cpu_threads(), "kind": "port",
-            "sample": f"{n} repetitions of ({prep} + matmul of {rows} of {M} rows), "
-                      f"M={M} N={N} K={K}, {el:.1f} s, scaled to all rows; numpy restatement "
-                      f"of the reference's torch CPU path",
-            "ms_per_step": round(sec_per_step * 1e3, 3)}
+    sample = (f"{n} calls of {what} on {cols} of {N} columns (M={M}, K={K}), "
+              f"{n * sec:.1f} s, scaled to all N; torch {torch.__version__} on {cores} threads")
+    return {"value": round(value, 6), "unit": unit, "cores": cores, "kind": "port",
+            "sample": sample, "ms_per_step": round(sec_per_step * 1e3, 3)}
 
 
 def run_reference(args, wl: dict, world: int, rank: int) -> None:
@@ -744,9 +781,9 @@ def run_reference(args, wl: dict, world: int, rank: int) -> None:
     line = {
         "metric": METRIC, "value": base["value"], "unit": base["unit"], "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": base["ms_per_step"],
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "impl": "reference",
-        "config": {"workload": args.workload, "M": wl["M"], "N": wl["N"], "K": wl["K"]},
+        "higher_is_better": True, "scaling": "strong" if wl.get("sharded") else "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": workload_config(args.workload, wl, world),
         "cpu_baseline": base,
         "e2e": {"value": base["value"], "unit": base["unit"], "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -761,7 +798,9 @@ def main() -> None:
                     help="timed steps (default: 100000 for decode, 200 otherwise)")
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=None,
+                    help=f"default: {DEFAULT_WORKLOAD} on one GPU, {DEFAULT_SHARDED_WORKLOAD} "
+                         "sharded over the ranks under torchrun")
     ap.add_argument("--split-k", type=int, default=0)
     ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused",
                     help="sharded W4A16 layers: output exchange inside the kernel where it "
@@ -772,6 +811,9 @@ def main() -> None:
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per launch from an ncu capture, reported as-is")
     args = ap.parse_args()
+    world, rank, local = dist_env()
+    if args.workload is None:
+        args.workload = DEFAULT_SHARDED_WORKLOAD if world > 1 else DEFAULT_WORKLOAD
     wl = WORKLOADS[args.workload]
     hbm = is_hbm_bound(wl)
     if args.steps is None:
@@ -780,7 +822,6 @@ def main() -> None:
         args.warmup = 2000 if hbm else 20
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    world, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, wl, world, rank)
     else:
