@@ -569,11 +569,51 @@ def single_gpu_leg(args, wl: dict, device: torch.device) -> dict:
     return out
 
 
+def phase_leg(work, chunk: int) -> dict:
+    """Per-CTA phase times of the last launch in a chain of 64 steps, from the
+    %globaltimer stamps the decode GEMVs write (pk_debug_phase_stamps):
+    microseconds from the launch's first CTA entry, median and max over CTAs."""
+    from pico_kernels_b200 import _lib
+    lib = _lib.load()
+    rows = 4 * torch.cuda.get_device_properties(work.device).multi_processor_count
+    buf = torch.zeros((rows, 8), dtype=torch.int64, device=work.device)
+    torch.cuda.synchronize()
+    _lib.check(lib.pk_debug_phase_stamps(buf.data_ptr(), buf.numel() * 8), "phase stamps")
+    try:
+        runner = capture_runner(work.step, work.n_sets, 64, chunk)
+        _replay(runner)
+        torch.cuda.synchronize()
+    finally:
+        lib.pk_debug_phase_stamps(None, 0)
+    st = buf.cpu()
+    st = st[st[:, 0] > 0].double()
+    if len(st) == 0:
+        return {"ctas": 0}
+    t0 = st[:, 0].min()
+
+    def stat(x):
+        x = x / 1e3
+        return {"median": round(float(x.median()), 3), "max": round(float(x.max()), 3)}
+    return {
+        "ctas": len(st), "sms": int(st[:, 5].unique().numel()),
+        "entry_us": stat(st[:, 0] - t0),
+        "wait_released_us": stat(st[:, 1] - t0),
+        "first_weights_after_wait_us": stat(st[:, 2] - st[:, 1]),
+        "arithmetic_us": stat(st[:, 3] - st[:, 2]),
+        "reduction_and_store_us": stat(st[:, 4] - st[:, 3]),
+        "end_us": stat(st[:, 4] - t0),
+        "note": "last launch of a 64-step chain; times from its first CTA's entry (%globaltimer)",
+    }
+
+
 def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
     import pico_kernels_b200 as pk
+    from pico_kernels_b200 import _lib
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.weight_staging is not None:
+        _lib.check(_lib.load().pk_set_weight_staging(args.weight_staging), "weight staging")
     sharded_run = bool(wl.get("sharded")) and world > 1
     strong = single_gpu_leg(args, wl, device) if sharded_run and rank == 0 else None
     dist = init_dist(world, local)
@@ -638,6 +678,8 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
             breakdown["step"] = "the local GEMM, then an NCCL all-gather of its output"
         del g_gemm, g_gath
 
+    phases = phase_leg(work, chunk) if args.phases and work.kind == "w4a16" and work.M == 1 else None
+
     # end to end through the public API, host buffers in and out every step
     e2e_fn, h2d, d2h = work.e2e_step_fn()
     e2e_steps = args.e2e_steps if work.hbm else max(3, args.e2e_steps // 100)
@@ -697,7 +739,8 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
     achieved = local_per / sec_per_launch / scale
     e2e_value = replicas * per * e2e_steps / (e2e_ms * 1e-3) / scale
     wl_cfg = workload_config(args.workload, wl, world)
-    path = {"split_k": args.split_k if args.split_k > 0 else "auto"}
+    path = {"split_k": args.split_k if args.split_k > 0 else "auto",
+            "weight_staging": args.weight_staging if args.weight_staging is not None else 0}
     if sharded_run:
         path["exchange"] = ("inside the local kernel (NVLink peer stores + flag barrier)"
                             if work.exchange is not None else "NCCL all_gather_into_tensor")
@@ -740,6 +783,8 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
         line["parity"] = parity
     if breakdown is not None:
         line["breakdown"] = breakdown
+    if phases is not None:
+        line["phases"] = phases
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(wl, budget_s=args.cpu_seconds)
     print(json.dumps(line), flush=True)
@@ -814,6 +859,10 @@ def main() -> None:
     ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused",
                     help="sharded W4A16 layers: output exchange inside the kernel where it "
                          "covers the shape, or always the NCCL all-gather")
+    ap.add_argument("--weight-staging", type=int, choices=[0, 1], default=None,
+                    help="pk_set_weight_staging mode for the M = 1 GEMVs (library default: 0)")
+    ap.add_argument("--phases", action="store_true",
+                    help="also report per-CTA phase times of the M = 1 GEMV (extra, untimed)")
     ap.add_argument("--e2e-steps", type=int, default=2000)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")

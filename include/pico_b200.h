@@ -101,6 +101,21 @@ PK_API int pk_pack_int4_n(const int8_t* q, int64_t K, int64_t N, uint8_t* packed
  * the reference's round-trip test (tests/test_gemm_int4.py:33-42). */
 PK_API int pk_unpack_int4_n(const uint8_t* packed, int64_t K, int64_t N, int8_t* q, void* stream);
 
+/* Fake quantization with the reference's rule, in the input's own dtype:
+ * for every column c of w[rows, cols] (dtype F16/BF16/F32, ld ldw) and every
+ * group of group_rows consecutive rows (group_rows <= 0: the whole column),
+ *   scale = dtype(dtype(max|w|.clamp_min(1e-12)) / qmax),  qmax = 2^(bits-1) - 1
+ *   out   = dtype(clamp(round(dtype(w / scale)), -qmax, qmax) * scale)
+ * each step computed in fp32 and rounded to the dtype as torch does (so an
+ * fp16 group of zeros gets scale 0 and NaN outputs, as in the reference).
+ * bits in [2, 8]. out[rows, cols] has the same dtype (ld ldo).
+ * Replaces quantize.quantize_col on a column (quantize.py:42-60) and, on a
+ * layer's fp32 copy w[out, in], the column walk of quantize.rtn_layer
+ * (quantize.py:63-68). */
+PK_API int pk_fake_quant_groups(const void* w, int dtype, int64_t rows, int64_t cols, int64_t ldw,
+                                int64_t group_rows, int bits, void* out, int64_t ldo,
+                                void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* W4A16 GEMM                                                              */
 /* ---------------------------------------------------------------------- */
@@ -183,6 +198,30 @@ PK_API int pk_w4a16_gemm_host(const void* a_host, int a_dtype, int64_t lda, cons
                               void* y_dev, void* workspace, size_t workspace_bytes,
                               void* stream);
 
+/* Weight staging of the M = 1 decode GEMVs (process-wide, default 0).
+ * mode 0: a GEMV prefetches its weights and scales into L2 before the
+ *   kernel ahead of it in the stream has finished (a hint that never returns
+ *   stale data), and loads them into shared memory only after it has.
+ * mode 1: the GEMV loads its first weights and scales into shared memory
+ *   before that kernel has finished; only the activations wait for it. The
+ *   caller guarantees that no kernel which lets its dependents start early
+ *   (programmatic dependent launch) writes the weights or scales of the
+ *   GEMV that follows it. Kernels that do not (every kernel launched without
+ *   that trigger, including this library's quantizers) are safe.
+ * Applies to calls made after it. No counterpart in the reference (Triton
+ * launches have no such overlap). */
+PK_API int pk_set_weight_staging(int mode);
+
+/* Profiling aid: while dev_buf is set (NULL turns it off), each CTA of the
+ * M = 1 decode GEMVs launched afterwards writes 8 uint64 words at
+ * dev_buf[8 * cta]: %globaltimer at entry, after griddepcontrol.wait, when
+ * its first weights landed, when its arithmetic ended and when its output
+ * was stored, then its SM id, its unit count and a kernel-specific word.
+ * Launches whose grid needs more than `bytes` record nothing. Kernels
+ * captured in a CUDA graph keep the setting they were captured with. No
+ * counterpart in the reference. */
+PK_API int pk_debug_phase_stamps(void* dev_buf, size_t bytes);
+
 /* ---------------------------------------------------------------------- */
 /* N-sharded W4A16 layer with the output exchange fused into the GEMV      */
 /* ---------------------------------------------------------------------- */
@@ -242,6 +281,20 @@ PK_API int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const 
 PK_API int pk_gptq_int4(float* wt, const float* h_inv, int64_t K, int64_t N, int group_size,
                  uint8_t* packed, void* scales, int scale_dtype, float* err_scratch,
                  void* stream);
+
+/* The GPTQ walk of quantize.gptq_layer itself (quantize.py:95-104) on the
+ * GPU, with the reference's quantize_col rule: wt[K, N] fp32 (K = input
+ * features, N = outputs: the layer's weight transposed, already permuted by
+ * the caller for act_order, quantize.py:97-98) is overwritten with the
+ * fake-quant weights. Input feature j in order: scales over groups of
+ * out_group consecutive outputs (<= 0: all N; quantize.py:100 with
+ * group_size), q = clamp(round(w / scale), -qmax, qmax), err = w - q * scale,
+ * and every later feature k receives w[k] -= err * (h_inv[j, k] / h_inv[j, j]),
+ * products and differences rounded separately as torch does. h_inv[K, K] is
+ * the inverse damped Hessian (quantize.py:88-93). bits in [2, 8]; N <= 16384;
+ * err_scratch holds 32 * N floats. */
+PK_API int pk_gptq_ref(float* wt, const float* h_inv, int64_t K, int64_t N, int out_group,
+                       int bits, float* err_scratch, void* stream);
 
 /* ---------------------------------------------------------------------- */
 /* fp8 (e4m3) GEMM                                                         */

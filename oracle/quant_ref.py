@@ -23,7 +23,7 @@ __all__ = [
     "E4M3_MAX",
     "f32_to_bf16_bits", "bf16_bits_to_f32", "round_to_bf16", "round_to_dtype",
     "f32_to_e4m3_bits", "e4m3_bits_to_f32",
-    "group_quant_codes", "store_scales", "quantize_col_fake",
+    "group_quant_codes", "store_scales", "quantize_col_fake", "rtn_layer_fake",
     "quantize_int4_per_tensor", "pack_int4_n", "unpack_int4_n",
     "dequant_weight", "w4a16_reference", "int4_gemm_per_tensor_reference",
     "fp8_quantize", "fp8_gemm_reference", "dense_gemm_reference",
@@ -154,19 +154,44 @@ def store_scales(scales_f32: np.ndarray, dtype: str) -> np.ndarray:
     return round_to_dtype(scales_f32, dtype)
 
 
-def quantize_col_fake(w_col: np.ndarray, bits: int, group_size: int | None = None):
-    """``quantize.quantize_col`` (quantize.py:42-60): fake-quant fp32 output."""
-    w_col = np.asarray(w_col, dtype=np.float32)
+def quantize_col_fake(w_col: np.ndarray, bits: int, group_size: int | None = None,
+                      dtype: str = "f32"):
+    """``quantize.quantize_col`` (quantize.py:42-60) on a column of ``dtype``
+    ("f16", "bf16" or "f32"; values given as fp32): fake-quant output as fp32
+    values of that dtype.
+
+    Each step of quantize.py:58-59 (``.clamp_min(1e-12)``, ``/ qmax``,
+    ``w / scale``, ``round``, ``clamp``, ``* scale``) is computed in fp32 and
+    rounded to the dtype, as torch evaluates it on a half tensor; in fp16 the
+    1e-12 floor rounds to 0, so a zero group gets NaN outputs, as upstream."""
+    rt = lambda v: round_to_dtype(v, dtype)  # noqa: E731
+    w_col = rt(np.asarray(w_col, dtype=np.float32))
     if bits >= 16:
         return w_col.copy()
     qmax = np.float32(2 ** (bits - 1) - 1)
     gs = w_col.size if group_size is None else group_size
     out = np.empty_like(w_col)
-    for g in range(0, w_col.size, gs):
-        blk = w_col[g:g + gs]
-        s = np.maximum(np.abs(blk).max(), np.float32(1e-12)) / qmax
-        out[g:g + gs] = np.clip(np.rint(blk / s), -qmax, qmax) * s
+    with np.errstate(divide="ignore", invalid="ignore"):
+        for g in range(0, w_col.size, gs):
+            blk = w_col[g:g + gs]
+            s = rt(rt(np.maximum(np.abs(blk).max(), np.float32(1e-12))) / qmax)
+            q = np.clip(np.rint(rt(blk / s)), -qmax, qmax)
+            out[g:g + gs] = rt(q * s)
     return out
+
+
+def rtn_layer_fake(w: np.ndarray, bits: int, group_size: int | None = None,
+                   dtype: str = "f32") -> np.ndarray:
+    """``quantize.rtn_layer`` (quantize.py:63-68): every input column of
+    ``w[out, in]`` (values of ``dtype``) quantized in fp32 (``w.float()``),
+    the result rounded back to ``dtype``."""
+    wf = round_to_dtype(np.asarray(w, dtype=np.float32), dtype)
+    if bits >= 16:
+        return wf.copy()
+    out = np.empty_like(wf)
+    for j in range(wf.shape[1]):
+        out[:, j] = quantize_col_fake(wf[:, j], bits, group_size, "f32")
+    return round_to_dtype(out, dtype)
 
 
 # ---------------------------------------------------------------------------
@@ -287,18 +312,26 @@ def gptq_inverse_hessian_inputs(x: np.ndarray, damp: float = 0.01):
 
 
 def gptq_fake_quant_columns(w: np.ndarray, h_inv: np.ndarray, bits: int,
-                            group_size: int | None = None) -> np.ndarray:
+                            group_size: int | None = None,
+                            act_mag: np.ndarray | None = None) -> np.ndarray:
     """``gptq_layer(w, x, bits, act_order=False, group_size)`` (quantize.py:71-115).
 
     Walks the input columns j of ``w[out, in]`` in order (quantize.py:99):
     ``q = quantize_col(w[:, j])`` with its groups along the OUTPUT rows
     (quantize.py:100), ``err = w[:, j] - q``, ratio ``h_inv[j, j+1:] /
     h_inv[j, j]`` and ``w[:, j+1:] -= outer(err, ratio)`` (quantize.py:101-104),
-    each product and difference rounded to fp32 on its own."""
+    each product and difference rounded to fp32 on its own. With ``act_mag``
+    (act_order=True, quantize.py:97-101) the columns of ``w`` and the rows and
+    columns of ``h_inv`` are first put in order of decreasing ``act_mag``
+    (distinct values: the order is unique) and the result is put back."""
     wq = np.array(w, dtype=np.float32, copy=True)
     h_inv = np.asarray(h_inv, dtype=np.float32)
     if bits >= 16:
         return wq
+    if act_mag is not None:
+        order = np.argsort(-np.asarray(act_mag, dtype=np.float32), kind="stable")
+        res = gptq_fake_quant_columns(wq[:, order], h_inv[order][:, order], bits, group_size)
+        return res[:, np.argsort(order, kind="stable")]
     d = wq.shape[1]
     for j in range(d):
         col = wq[:, j].copy()

@@ -77,6 +77,10 @@ SIGNATURES = {
     "pk_ipc_close": (_int, [_vp]),
     "pk_w4a16_gemm_sharded": (_int, [_vp, _int, _i64, _vp, _vp, _f32, _int, _i64, _i64, _i64,
                                      _int, _i64, _i64, _int, _int, _vp, _vp, _vp, _sz, _vp]),
+    "pk_fake_quant_groups": (_int, [_vp, _int, _i64, _i64, _i64, _i64, _int, _vp, _i64, _vp]),
+    "pk_gptq_ref": (_int, [_vp, _vp, _i64, _i64, _int, _int, _vp, _vp]),
+    "pk_set_weight_staging": (_int, [_int]),
+    "pk_debug_phase_stamps": (_int, [_vp, _sz]),
 }
 
 _lib = None

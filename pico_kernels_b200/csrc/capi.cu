@@ -322,8 +322,36 @@ int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t* wp, co
   if (split_k < 0) return fail(PK_ERR_SHAPE, "split_k must be >= 0");
   cudaStream_t s = as_stream(stream);
 
-  // Decode shapes where it is faster, with the automatic split: the CUDA-core
-  // GEMV (a weight stream).
+  // M = 1 on layers that fit one wave: the CUDA-core GEMV whose K splits
+  // reduce inside thread-block clusters (no workspace).
+  if (split_k == 0 && gemv_cluster_preferred(M, N, K) &&
+      gemv_cluster_supported(M, N, K, group_size, scales, lda, a, wp)) {
+    DecodeArgs p{};
+    p.a = a;
+    p.lda = lda;
+    p.wp = wp;
+    p.scales = scales;
+    p.group = group_size;
+    p.scalar_scale = scales ? 1.0f : scalar_scale;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.out = out;
+    p.out_dtype = out_dtype;
+    p.ldo = ldo;
+    p.a_dtype = a_dtype;
+    p.split = 1;
+    p.status = device_status_ptr();
+    const char* why = "";
+    cudaError_t e = launch_w4a16_gemv_cluster(p, s, &why);
+    if (e == cudaErrorInvalidValue && why[0] != '\0') return fail(PK_ERR_ALIGN, "%s", why);
+    if (e != cudaSuccess) return cuda_fail(e, "w4a16 cluster gemv launch");
+    ok();
+    return PK_OK;
+  }
+
+  // Other decode shapes where it is faster, with the automatic split: the
+  // stream-K CUDA-core GEMV (a weight stream).
   if (split_k == 0 && gemv_preferred(M, N, K) &&
       gemv_supported(M, N, K, group_size, scales, lda, a, wp)) {
     const size_t need = gemv_workspace_bytes(M, N, K);
@@ -825,9 +853,13 @@ int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t
     return fail(PK_ERR_ALIGN,
                 "sharded W4A16: A, the packed weights and the scales must be 16-byte aligned "
                 "with lda a multiple of 8");
+  // M = 1 layers that fill one wave run the cluster form, which needs only
+  // the completion counter from the workspace
+  const bool cluster = path == kPathGemv && gemv_cluster_preferred(M, N, K) &&
+                       gemv_cluster_supported(M, N, K, group_size, scales, lda, a, wp);
   int split = 1;
   size_t need = kCounterBytes;
-  if (path == kPathGemv) {
+  if (path == kPathGemv && !cluster) {
     need = gemv_workspace_bytes(M, N, K);
   } else if (path == kPathDecode) {
     split = decode_pick_split(M, N, K);
@@ -873,11 +905,54 @@ int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t
   }
   sh.done = ws_counters(workspace) + (kMaxCounters - 1);
   const char* why = "";
-  cudaError_t e = path == kPathGemv     ? launch_w4a16_gemv(p, as_stream(stream), &why, &sh)
+  cudaError_t e = cluster ? launch_w4a16_gemv_cluster(p, as_stream(stream), &why, &sh)
+                  : path == kPathGemv     ? launch_w4a16_gemv(p, as_stream(stream), &why, &sh)
                   : path == kPathDecode ? launch_w4a16_decode(p, as_stream(stream), &why, &sh)
                                     : launch_w4a16_skinny(p, as_stream(stream), &why, &sh);
   if (e == cudaErrorInvalidValue && why[0] != '\0') return fail(PK_ERR_ALIGN, "%s", why);
   if (e != cudaSuccess) return cuda_fail(e, "sharded w4a16 gemm launch");
+  ok();
+  return PK_OK;
+}
+
+int pk_fake_quant_groups(const void* w, int dtype, int64_t rows, int64_t cols, int64_t ldw,
+                         int64_t group_rows, int bits, void* out, int64_t ldo, void* stream) {
+  if (!w || !out) return fail(PK_ERR_SHAPE, "null pointer");
+  if (rows <= 0 || cols <= 0 || ldw < cols || ldo < cols)
+    return fail(PK_ERR_SHAPE, "need rows, cols > 0 and leading dimensions >= cols");
+  if (bits < 2 || bits > 8) return fail(PK_ERR_SHAPE, "bits must be in [2, 8] (got %d)", bits);
+  if (dtype != PK_F16 && dtype != PK_BF16 && dtype != PK_F32)
+    return fail(PK_ERR_DTYPE, "fake quantization runs on f16, bf16 or f32");
+  cudaError_t e = launch_fake_quant_groups(w, dtype, rows, cols, ldw, group_rows, bits, out, ldo,
+                                           as_stream(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fake quantization launch");
+  ok();
+  return PK_OK;
+}
+
+int pk_gptq_ref(float* wt, const float* h_inv, int64_t K, int64_t N, int out_group, int bits,
+                float* err_scratch, void* stream) {
+  if (!wt || !h_inv || !err_scratch) return fail(PK_ERR_SHAPE, "null pointer");
+  if (K <= 0 || N <= 0) return fail(PK_ERR_SHAPE, "need K, N > 0");
+  if (N > gptq_ref_max_out())
+    return fail(PK_ERR_UNSUPPORTED, "the walk holds at most %d outputs per feature (got %lld)",
+                gptq_ref_max_out(), (long long)N);
+  if (bits < 2 || bits > 8) return fail(PK_ERR_SHAPE, "bits must be in [2, 8] (got %d)", bits);
+  cudaError_t e = launch_gptq_ref(wt, h_inv, K, N, out_group, bits, err_scratch, as_stream(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gptq (reference rule) launch");
+  ok();
+  return PK_OK;
+}
+
+int pk_set_weight_staging(int mode) {
+  if (mode != 0 && mode != 1) return fail(PK_ERR_SHAPE, "weight staging mode must be 0 or 1");
+  set_weight_staging(mode);
+  ok();
+  return PK_OK;
+}
+
+int pk_debug_phase_stamps(void* dev_buf, size_t bytes) {
+  set_phase_stamps(dev_buf, bytes);
   ok();
   return PK_OK;
 }

@@ -128,6 +128,64 @@ __global__ void __launch_bounds__(kTrailTN * 8)
   }
 }
 
+// ---------------------------------------------------------------------------
+// The reference's own rule (gptq_layer's quantize_col, quantize.py:100): each
+// input feature j is one column of outputs, quantized with scales over groups
+// of `out_group` consecutive OUTPUTS (<= 0: the whole column), and replaced by
+// its fake-quant values. One CTA walks a block of kRefBlock features in order:
+// per feature, the group absmax (shared memory, one warp per group), the
+// fp32 scale max.clamp_min(1e-12) / qmax, then per output its code, fake
+// value q * s and error (quantize.py:58-59, 101), and the update of the
+// block's later features (quantize.py:102-104). The trailing kernel above
+// applies the block's updates to the features after it, in feature order.
+// ---------------------------------------------------------------------------
+constexpr int kRefThreads = 1024;
+constexpr int kRefBlock = 32;
+constexpr int kRefMaxOut = 16384;
+
+__global__ void __launch_bounds__(kRefThreads)
+    gptq_ref_block_kernel(float* __restrict__ wt, int64_t K, int64_t N, int64_t j0, int gb,
+                          const float* __restrict__ h_inv, float* __restrict__ err,
+                          int64_t out_group, float qmax) {
+  extern __shared__ float sm[];
+  float* absb = sm;       // [N] |w| of the current feature
+  float* sc = sm + N;     // [G] its group scales
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t G = (N + out_group - 1) / out_group;
+  for (int k = 0; k < gb; ++k) {
+    const int64_t j = j0 + k;
+    float* row = wt + j * N;
+    for (int64_t n = tid; n < N; n += kRefThreads) absb[n] = fabsf(row[n]);
+    __syncthreads();
+    for (int64_t g = warp; g < G; g += kRefThreads / 32) {
+      const int64_t a = g * out_group, b = a + out_group < N ? a + out_group : N;
+      float m = 0.0f;
+      for (int64_t n = a + lane; n < b; n += 32) m = fmaxf(m, absb[n]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0) sc[g] = __fdiv_rn(fmaxf(m, 1e-12f), qmax);   // quantize.py:58
+    }
+    __syncthreads();
+    const float hjj = h_inv[j * K + j];
+    for (int64_t n = tid; n < N; n += kRefThreads) {
+      const float v = row[n];
+      const float s = sc[n / out_group];
+      float q = rintf(__fdiv_rn(v, s));                                // quantize.py:59
+      q = q < -qmax ? -qmax : (q > qmax ? qmax : q);
+      const float fq = __fmul_rn(q, s);
+      const float e = __fsub_rn(v, fq);                                // quantize.py:101
+      row[n] = fq;                                                     // quantize.py:104
+      err[static_cast<int64_t>(k) * N + n] = e;
+      for (int kk = k + 1; kk < gb; ++kk) {
+        const float r = __fdiv_rn(h_inv[j * K + j0 + kk], hjj);        // quantize.py:102
+        float* x = wt + (j0 + kk) * N + n;
+        *x = __fsub_rn(*x, __fmul_rn(e, r));                           // quantize.py:103
+      }
+    }
+    __syncthreads();  // absb and sc are rewritten for the next feature
+  }
+}
+
 template <typename S>
 cudaError_t gptq_run(float* wt, const float* h_inv, int64_t K, int64_t N, int group,
                      uint8_t* packed, S* scales, float* err, cudaStream_t s) {
@@ -157,6 +215,32 @@ cudaError_t gptq_run(float* wt, const float* h_inv, int64_t K, int64_t N, int gr
 }  // namespace
 
 int gptq_max_group() { return kGptqMaxGroup; }
+int gptq_ref_max_out() { return kRefMaxOut; }
+
+cudaError_t launch_gptq_ref(float* wt, const float* h_inv, int64_t K, int64_t N, int out_group,
+                            int bits, float* err, cudaStream_t s) {
+  const int64_t og = out_group <= 0 || out_group > N ? N : out_group;
+  const int64_t G = (N + og - 1) / og;
+  const size_t smem = static_cast<size_t>(N + G) * sizeof(float);
+  cudaError_t e = cudaFuncSetAttribute(gptq_ref_block_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  const float qmax = static_cast<float>((1ll << (bits - 1)) - 1);
+  const unsigned tx = static_cast<unsigned>((N + kTrailTN - 1) / kTrailTN);
+  for (int64_t j0 = 0; j0 < K; j0 += kRefBlock) {
+    const int gb = static_cast<int>(K - j0 < kRefBlock ? K - j0 : kRefBlock);
+    gptq_ref_block_kernel<<<1, kRefThreads, smem, s>>>(wt, K, N, j0, gb, h_inv, err, og, qmax);
+    const int64_t rest = K - (j0 + gb);
+    if (rest > 0) {
+      const dim3 grid(tx, static_cast<unsigned>((rest + kTrailTK - 1) / kTrailTK));
+      gptq_trailing_kernel<<<grid, dim3(kTrailTN, 8), 0, s>>>(wt, K, N, j0, gb, h_inv, err);
+    }
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
 
 cudaError_t launch_gptq_int4(float* wt, const float* h_inv, int64_t K, int64_t N, int group,
                              uint8_t* packed, void* scales, int scale_dtype, float* err,

@@ -76,11 +76,22 @@ cudaError_t launch_quant_int4_tensor(const void* w, int dtype, int64_t n, float 
 cudaError_t launch_pack_int4(const int8_t* q, int64_t K, int64_t N, uint8_t* p, cudaStream_t s);
 cudaError_t launch_unpack_int4(const uint8_t* p, int64_t K, int64_t N, int8_t* q,
                                cudaStream_t s);
+// reference-rule fake quantization of every column of w[rows, cols], groups of
+// `group` rows (<= 0: whole columns), arithmetic rounded to dtype per step
+cudaError_t launch_fake_quant_groups(const void* w, int dtype, int64_t rows, int64_t cols,
+                                     int64_t ldw, int64_t group, int bits, void* out, int64_t ldo,
+                                     cudaStream_t s);
 // ---- gptq.cu (GPTQ producer of packed int4 weights) ----------------------
 int gptq_max_group();
 cudaError_t launch_gptq_int4(float* wt, const float* h_inv, int64_t K, int64_t N, int group,
                              uint8_t* packed, void* scales, int scale_dtype, float* err,
                              cudaStream_t s);
+// The reference's own walk (quantize.py:95-104): wt[K = in, N = out] fp32 is
+// overwritten with the fake-quant weights, each input feature quantized with
+// quantize_col's rule (groups of `out_group` outputs, <= 0: the whole column)
+int gptq_ref_max_out();
+cudaError_t launch_gptq_ref(float* wt, const float* h_inv, int64_t K, int64_t N, int out_group,
+                            int bits, float* err, cudaStream_t s);
 
 // absmax into amax, then the cast with scale = 448 / amax computed on the
 // device and stored to `scale` (gemm_fp8.quantize without the host sync)
@@ -150,6 +161,22 @@ bool gemv_supported(int64_t M, int64_t N, int64_t K, int group, const void* scal
 size_t gemv_workspace_bytes(int64_t M, int64_t N, int64_t K);  // 0: no split-K fixup needed
 cudaError_t launch_w4a16_gemv(const DecodeArgs& args, cudaStream_t s, const char** why,
                               const OutputShard* shard = nullptr);
+
+// ---- w4a16_gemv_cluster.cu (M = 1 in one wave, K split reduced in clusters)
+bool gemv_cluster_supported(int64_t M, int64_t N, int64_t K, int group, const void* scales,
+                            int64_t lda, const void* a, const void* wp);
+bool gemv_cluster_preferred(int64_t M, int64_t N, int64_t K);
+int gemv_cluster_split(int64_t N, int64_t K);
+cudaError_t launch_w4a16_gemv_cluster(const DecodeArgs& args, cudaStream_t s, const char** why,
+                                      const OutputShard* shard = nullptr);
+// Weight staging (pk_set_weight_staging): 1 = decode GEMVs load weights and
+// scales into shared memory before the previous kernel in the stream ends.
+void set_weight_staging(int mode);
+int weight_staging();
+// Phase stamps (pk_debug_phase_stamps): the buffer, when set and at least
+// `need` bytes long, else nullptr.
+void set_phase_stamps(void* buf, size_t bytes);
+uint64_t* phase_stamps(size_t need);
 
 // ---- gemm_tc.cu (persistent tcgen05 GEMM: fp8, dense split-K, W4A16 prefill)
 struct GemmArgs {

@@ -374,6 +374,42 @@ cudaError_t quant_group_dispatch_scale(const void* w, int64_t K, int64_t N, int6
   }
 }
 
+// Fake quantization with the reference's group rule, in the input's dtype:
+// quantize.quantize_col (quantize.py:42-60) on every column of w[rows, cols]
+// (groups of `group` consecutive rows; group <= 0: the whole column), the
+// column walk of rtn_layer (quantize.py:63-68) when w is that layer's fp32
+// copy. torch evaluates each step of
+//   scale = w.abs().max().clamp_min(1e-12) / qmax
+//   out   = clamp(round(w / scale), -qmax, qmax) * scale
+// in fp32 and rounds the result to the tensor's dtype; each step here does
+// the same, so fp16 columns keep the reference's behaviour where its 1e-12
+// floor underflows (a zero scale: inf / NaN quotients, NaN out where w = 0).
+// The clamp propagates NaN like torch.clamp. One thread per (column, group);
+// consecutive threads take consecutive columns (coalesced rows).
+template <typename T>
+__global__ void fake_quant_groups_kernel(const T* __restrict__ w, int64_t rows, int64_t cols,
+                                         int64_t ldw, int64_t group, float qmax,
+                                         T* __restrict__ out, int64_t ldo) {
+  const int64_t G = (rows + group - 1) / group;
+  const int64_t total = G * cols;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t c = t % cols, g = t / cols;
+    const int64_t r0 = g * group;
+    const int64_t r1 = r0 + group < rows ? r0 + group : rows;
+    float m = 0.0f;
+    for (int64_t r = r0; r < r1; ++r) m = fmaxf(m, fabsf(to_f32<T>(w[r * ldw + c])));
+    const float floor_ = round_through<T>(fmaxf(m, 1e-12f));   // .clamp_min(1e-12)
+    const float s = round_through<T>(floor_ / qmax);           // / qmax
+    for (int64_t r = r0; r < r1; ++r) {
+      const float x = round_through<T>(to_f32<T>(w[r * ldw + c]) / s);  // w / scale
+      float q = rintf(x);                                                // torch.round
+      q = q < -qmax ? -qmax : (q > qmax ? qmax : q);                     // clamp, NaN kept
+      out[r * ldo + c] = from_f32<T>(q * s);                             // * scale
+    }
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_quant_int4_group(const void* w, int w_dtype, int64_t K, int64_t N, int64_t ldw,
@@ -521,6 +557,41 @@ cudaError_t launch_dequant_int4(const uint8_t* wp, const void* scales, int group
     else dequant_int4_kernel<__half, false><<<grid, threads, 0, s>>>(wp, sp, group, K, N, op);
   } else {
     return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace pk
+
+namespace pk {
+
+cudaError_t launch_fake_quant_groups(const void* w, int dtype, int64_t rows, int64_t cols,
+                                     int64_t ldw, int64_t group, int bits, void* out, int64_t ldo,
+                                     cudaStream_t s) {
+  if (group <= 0 || group > rows) group = rows;
+  const float qmax = static_cast<float>((1ll << (bits - 1)) - 1);
+  const int64_t total = ((rows + group - 1) / group) * cols;
+  const int threads = 256;
+  int64_t blocks = (total + threads - 1) / threads;
+  if (blocks > 65535ll * 16) blocks = 65535ll * 16;
+  const dim3 grid(static_cast<unsigned>(blocks));
+  switch (dtype) {
+    case PK_F32:
+      fake_quant_groups_kernel<float><<<grid, threads, 0, s>>>(
+          static_cast<const float*>(w), rows, cols, ldw, group, qmax, static_cast<float*>(out), ldo);
+      break;
+    case PK_F16:
+      fake_quant_groups_kernel<__half><<<grid, threads, 0, s>>>(
+          static_cast<const __half*>(w), rows, cols, ldw, group, qmax, static_cast<__half*>(out),
+          ldo);
+      break;
+    case PK_BF16:
+      fake_quant_groups_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(w), rows, cols, ldw, group, qmax,
+          static_cast<__nv_bfloat16*>(out), ldo);
+      break;
+    default:
+      return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
 }

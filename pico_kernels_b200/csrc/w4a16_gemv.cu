@@ -191,6 +191,7 @@ struct GemvParams {
   float* partials;
   unsigned* sems;
   int* status;
+  uint64_t* stamps;    // optional per-CTA phase times (pk_debug_phase_stamps)
 };
 
 // Write column `col` of output row m into every copy of the output.
@@ -240,6 +241,10 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
   const int64_t u1 = U * (cta + 1) / G;
   const int n_units = static_cast<int>(u1 - u0);
   bool stored = false;  // this thread wrote output (sharded exchange: fence before arriving)
+  uint64_t t_entry = 0, t_wait = 0, t_first = 0, t_comp = 0;
+  bool was_last = false;
+  const bool stamp = p.stamps != nullptr && threadIdx.x == 0;
+  if (stamp) t_entry = globaltimer();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -306,6 +311,7 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
   } else {
     // ---------------- dequant / FMA warps ----------------
     griddep_wait();
+    if (stamp) t_wait = globaltimer();
     // -8 * 16^p * 2^-149 for the column pairs' positions (2,3) and (4,5): the
     // same bit patterns as the sign flips, negated
     const uint64_t off23 = pack2(__uint_as_float(0x80000800u), __uint_as_float(0x80008000u));
@@ -326,6 +332,7 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
       const int k0 = kb * kRows;
       if (!failed && !mbar_wait_sleep(&full[slot * kSub], round & 1, p.status, kSiteGemvConsumer))
         failed = true;
+      if (stamp && i == 0) t_first = globaltimer();
       const uint8_t* base = smem + slot * C::kSlotBytes;
 
       // Activations: lane l converts row 32*warp + l of every output row m.
@@ -415,6 +422,7 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
       if (!seg_end) continue;
 
       // ---- end of a segment: reduce over warps, one output row at a time ----
+      if (stamp) t_comp = globaltimer();
       named_bar_sync(1, kWarps * 32);  // every warp is done with its pairs
       const int t = threadIdx.x;       // column within the slice
       float v[M];
@@ -459,6 +467,7 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
       }
       named_bar_sync(1, kWarps * 32);
       if (*last_flag) {
+        was_last = true;
         float sum[M];
 #pragma unroll
         for (int m = 0; m < M; ++m) sum[m] = 0.0f;
@@ -490,6 +499,19 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
     }
   }
 
+  if (stamp) {
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    uint64_t* st = p.stamps + static_cast<int64_t>(blockIdx.x) * 8;
+    st[0] = t_entry;
+    st[1] = t_wait;
+    st[2] = t_first;
+    st[3] = t_comp;
+    st[4] = globaltimer();
+    st[5] = smid;
+    st[6] = static_cast<uint64_t>(n_units);
+    st[7] = was_last ? 1u : 0u;  // this CTA summed a slice's partials
+  }
   if (p.world > 1) sharded_finish(p, stored);
 }
 
@@ -591,6 +613,7 @@ cudaError_t launch_w4a16_gemv(const DecodeArgs& a, cudaStream_t s, const char** 
   p.partials = a.partials;
   p.sems = a.sems;
   p.status = a.status;
+  p.stamps = phase_stamps(static_cast<size_t>(gemv_grid(a.N, a.K)) * 64);
   if (grouped) {
     const int64_t groups = (a.K + a.group - 1) / a.group;
     if (!encode_tmap_2d(&tmS, dt, a.scales, a.N, groups, a.N * 2, kCols,

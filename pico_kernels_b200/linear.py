@@ -59,18 +59,23 @@ class W4A16Linear(nn.Module):
                                                      device=device))
         else:
             self.bias = None
+        # act_order GPTQ: the packed rows follow this order of the input features
+        self.register_buffer("perm", None)
 
     @classmethod
     def from_linear(cls, linear: nn.Linear, group_size: int = 128,
                     dtype: torch.dtype | None = None, calib: torch.Tensor | None = None,
-                    damp: float = 0.01) -> "W4A16Linear":
+                    damp: float = 0.01, act_order: bool = False) -> "W4A16Linear":
         """Quantize ``linear.weight`` (on a CUDA device) into a new layer.
 
         Round-to-nearest per group by default; with calibration inputs
         ``calib[..., in]`` (this layer's inputs) the GPTQ producer
         (``gptq.gptq_quantize_int4``) chooses the codes. ``dtype``
         (activations and stored scales) defaults to the weight's dtype when
-        that is fp16/bf16, else bf16. The bias is kept in fp32.
+        that is fp16/bf16, else bf16. The bias is kept in fp32. With
+        ``act_order`` (GPTQ only) the input features are quantized in order of
+        decreasing activation energy (quantize.py:97-101) and stored in that
+        order; ``forward`` gathers its inputs with the same permutation.
         """
         w = linear.weight.detach()
         _lib.require_cuda(w)
@@ -82,8 +87,13 @@ class W4A16Linear(nn.Module):
         # to the activation dtype as the GEMM reads them
         if calib is not None:
             from .gptq import gptq_quantize_int4
-            packed, scales = gptq_quantize_int4(w, calib, group_size=group_size, damp=damp,
-                                                scale_dtype=dtype)
+            res = gptq_quantize_int4(w, calib, group_size=group_size, damp=damp,
+                                     scale_dtype=dtype, act_order=act_order)
+            packed, scales = res[0], res[1]
+            if act_order:
+                layer.perm = res[2]
+        elif act_order:
+            raise _lib.ShapeError("act_order needs calibration inputs (GPTQ)")
         else:
             packed, scales = quantize_int4_grouped(w.t(), group_size, scale_dtype=dtype)
         layer.w_packed.copy_(packed)
@@ -99,6 +109,8 @@ class W4A16Linear(nn.Module):
         x2 = x.reshape(-1, self.in_features)
         if x2.dtype != self.dtype:
             x2 = x2.to(self.dtype)
+        if self.perm is not None:
+            x2 = x2.index_select(1, self.perm)
         out_dtype = x.dtype if (self.bias is None and x.dtype == torch.bfloat16) else torch.float32
         y = int4_gemm(x2, self.w_packed, self.scales, group_size=self.group_size,
                       out_dtype=out_dtype)
@@ -111,7 +123,10 @@ class W4A16Linear(nn.Module):
         from .gemm_int4 import unpack_int4_n
         q = unpack_int4_n(self.w_packed).float()
         s = self.scales.float().repeat_interleave(self.group_size, dim=0)[: self.in_features]
-        return (q * s).t().contiguous()
+        w = (q * s).t()
+        if self.perm is not None:
+            w = w[:, torch.argsort(self.perm)]
+        return w.contiguous()
 
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, "
@@ -139,7 +154,7 @@ def _capture_inputs(model: nn.Module, module: nn.Module, calib) -> torch.Tensor:
 def quantize_linear_layers(model: nn.Module, group_size: int = 128,
                            select: Callable[[str, nn.Linear], bool] | None = None,
                            dtype: torch.dtype | None = None, calib=None,
-                           damp: float = 0.01) -> nn.Module:
+                           damp: float = 0.01, act_order: bool = False) -> nn.Module:
     """Replace ``nn.Linear`` children in place with ``W4A16Linear``.
 
     ``select(name, module)`` picks the layers (default: every ``nn.Linear``
@@ -161,5 +176,6 @@ def quantize_linear_layers(model: nn.Module, group_size: int = 128,
             parent = getattr(parent, p)
         mod = getattr(parent, leaf)
         x = _capture_inputs(model, mod, calib) if calib is not None else None
-        setattr(parent, leaf, W4A16Linear.from_linear(mod, group_size, dtype, calib=x, damp=damp))
+        setattr(parent, leaf, W4A16Linear.from_linear(mod, group_size, dtype, calib=x, damp=damp,
+                                                      act_order=act_order and x is not None))
     return model

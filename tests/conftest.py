@@ -31,3 +31,25 @@ def config1():
 def gptq_golden():
     with np.load(GOLDEN / "gptq_small.npz") as z:
         return {k: z[k] for k in z.files}
+
+
+@pytest.fixture(scope="session")
+def qcol_golden():
+    with np.load(GOLDEN / "quantize_col.npz") as z:
+        return {k: z[k] for k in z.files}
+
+
+@pytest.fixture(scope="session")
+def gptq_ao_golden():
+    with np.load(GOLDEN / "gptq_act_order.npz") as z:
+        return {k: z[k] for k in z.files}
+
+
+def golden_values(arr: np.ndarray, dtype: str) -> np.ndarray:
+    """fp32 values of a golden array stored by make_golden._np (bf16 as uint16 bits)."""
+    if dtype == "bfloat16":
+        return (arr.astype(np.uint32) << 16).view(np.float32)
+    return arr.astype(np.float32)
+
+
+SHORT = {"float16": "f16", "bfloat16": "bf16", "float32": "f32"}

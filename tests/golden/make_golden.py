@@ -9,7 +9,10 @@ It imports ``quantize.quantize_col``, ``gemm_int4.quantize_int4``,
 runs them on CPU torch tensors (the Triton kernels are never launched), then
 writes ``golden_small.npz``, ``config1.npz`` and ``gptq_small.npz`` beside
 this script (``quantize.gptq_layer`` with act_order=False, the inverse Hessian
-it builds, and its fake-quant output). The GPU box
+it builds, and its fake-quant output), ``quantize_col.npz``
+(``quantize.quantize_col`` on fp16 / bf16 / fp32 columns at 2-8 bits and
+``quantize.rtn_layer``) and ``gptq_act_order.npz`` (``quantize.gptq_layer``
+with its default act_order=True; ``--only`` writes a subset). The GPU box
 has no reference checkout: the tests only read the committed ``.npz`` files.
 
 Derived quantities:
@@ -219,16 +222,106 @@ def make_gptq(ref: Path) -> dict[str, np.ndarray]:
     return out
 
 
+def make_quantize_col(ref: Path) -> dict[str, np.ndarray]:
+    """``quantize.quantize_col`` (quantize.py:42-60) on fp16 / bf16 / fp32
+    columns at 2, 3, 4 and 8 bits, with and without groups (a ragged last
+    group included), and ``quantize.rtn_layer`` (quantize.py:63-68) on small
+    layers; edge columns: a group of zeros, values below the 1e-12 floor (it
+    underflows to 0 in fp16), ties at x.5 of the scale, and large magnitudes."""
+    sys.path.insert(0, str(ref))
+    import quantize  # noqa: E402
+
+    out: dict[str, np.ndarray] = {}
+    torch.manual_seed(31)
+    base = torch.randn(100) * 0.05
+    edge = torch.randn(64) * 0.02
+    edge[:16] = 0.0                                       # a group of zeros
+    edge[16:32] = torch.randn(16) * 1e-9                  # below fp16's subnormals
+    edge[32:48] = torch.tensor([7.0, 0.5, 1.5, 2.5, -3.5, 4.5, -5.5, 6.5] * 2)  # scale 1, ties
+    edge[48:64] = torch.randn(16) * 3e3
+    cols = {"rand": base, "edge": edge}
+    i = 0
+    for dt in (torch.float16, torch.bfloat16, torch.float32):
+        for cname, col in cols.items():
+            w = col.to(dt)
+            for bits in (2, 3, 4, 8):
+                for gs in (None, 16):
+                    key = f"qcol/{i:03d}"
+                    i += 1
+                    out[f"{key}/w"] = _np(w)
+                    out[f"{key}/out"] = _np(quantize.quantize_col(w, bits, gs))
+                    out[f"{key}/dtype"] = np.array(str(dt)[6:])
+                    out[f"{key}/bits"] = np.array(bits)
+                    out[f"{key}/group"] = np.array(gs or 0)
+                    out[f"{key}/name"] = np.array(cname)
+    torch.manual_seed(32)
+    j = 0
+    for dt in (torch.float16, torch.bfloat16, torch.float32):
+        w = (torch.randn(48, 24) * 0.02).to(dt)
+        for bits, gs in ((4, None), (4, 8), (3, 16), (8, None)):
+            key = f"rtn/{j:03d}"
+            j += 1
+            out[f"{key}/w"] = _np(w)
+            out[f"{key}/out"] = _np(quantize.rtn_layer(w, bits, gs))
+            out[f"{key}/dtype"] = np.array(str(dt)[6:])
+            out[f"{key}/bits"] = np.array(bits)
+            out[f"{key}/group"] = np.array(gs or 0)
+    return out
+
+
+def make_gptq_act_order(ref: Path) -> dict[str, np.ndarray]:
+    """``quantize.gptq_layer`` (quantize.py:71-115) with its default
+    act_order=True (and a 3-bit case without it), plus the inverse Hessian and
+    the activation energies it computed with the reference's own expressions
+    (quantize.py:86-93), which the GPU walk takes as inputs."""
+    sys.path.insert(0, str(ref))
+    import quantize  # noqa: E402
+
+    out: dict[str, np.ndarray] = {}
+    torch.manual_seed(41)
+    cases = ((32, 64, 256, None, 4, True), (48, 40, 128, 8, 4, True), (16, 96, 512, 16, 4, True),
+             (40, 48, 192, 8, 3, True), (24, 32, 128, None, 3, False))
+    for (o_dim, i_dim, n, gs, bits, ao) in cases:
+        w = torch.randn(o_dim, i_dim) * 0.02
+        x = torch.randn(n, i_dim) * torch.linspace(0.2, 3.0, i_dim)[torch.randperm(i_dim)]
+        xf = x.float()
+        H = (xf.t() @ xf) / n
+        act_mag = torch.diag(H).clone()
+        H = H + 0.01 * act_mag.mean() * torch.eye(i_dim)
+        h_inv = torch.linalg.inv(H)
+        wq = quantize.gptq_layer(w, x, bits, damp=0.01, act_order=ao, group_size=gs)
+        key = f"gptq/o{o_dim}_i{i_dim}_g{gs or 0}_b{bits}_ao{int(ao)}"
+        out[f"{key}/w"] = _np(w)
+        out[f"{key}/x"] = _np(x)
+        out[f"{key}/h_inv"] = _np(h_inv)
+        out[f"{key}/act_mag"] = _np(act_mag)
+        out[f"{key}/group"] = np.array(gs or 0)
+        out[f"{key}/bits"] = np.array(bits)
+        out[f"{key}/act_order"] = np.array(int(ao))
+        out[f"{key}/wq"] = _np(wq)
+    return out
+
+
+FILES = {
+    "golden_small.npz": make_small,
+    "config1.npz": make_config1,
+    "gptq_small.npz": make_gptq,
+    "quantize_col.npz": make_quantize_col,
+    "gptq_act_order.npz": make_gptq_act_order,
+}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
+    ap.add_argument("--only", nargs="*", choices=sorted(FILES), default=None,
+                    help="write only these files (default: all)")
     args = ap.parse_args()
     torch.set_num_threads(8)
-    small = make_small(args.reference)
-    np.savez_compressed(HERE / "golden_small.npz", **small)
-    np.savez_compressed(HERE / "config1.npz", **make_config1(args.reference))
-    np.savez_compressed(HERE / "gptq_small.npz", **make_gptq(args.reference))
-    print("wrote", HERE / "golden_small.npz", len(small), "arrays")
+    for name in args.only or sorted(FILES):
+        arrays = FILES[name](args.reference)
+        np.savez_compressed(HERE / name, **arrays)
+        print("wrote", HERE / name, len(arrays), "arrays")
 
 
 if __name__ == "__main__":

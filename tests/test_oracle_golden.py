@@ -190,3 +190,60 @@ def test_group_rtn_properties_random_shapes():
             blk = np.abs(codes[gi:gi + g])
             assert np.all(blk.max(axis=0) == 7)
         assert np.array_equal(o.unpack_int4_n(o.pack_int4_n(codes)), codes)
+
+
+def _cases(z, prefix):
+    keys = sorted({k.rsplit("/", 1)[0] for k in z if k.startswith(prefix)})
+    assert keys, prefix
+    return keys
+
+
+def test_oracle_quantize_col_all_dtypes_and_widths(qcol_golden):
+    """quantize.quantize_col on fp16 / bf16 / fp32 columns at 2, 3, 4 and 8
+    bits (quantize.py:42-60), bit for bit, NaN where the reference gives NaN."""
+    from conftest import SHORT, golden_values
+    z = qcol_golden
+    for key in _cases(z, "qcol/"):
+        dt = str(z[f"{key}/dtype"])
+        w = golden_values(z[f"{key}/w"], dt)
+        want = golden_values(z[f"{key}/out"], dt)
+        g = int(z[f"{key}/group"])
+        got = o.quantize_col_fake(w, int(z[f"{key}/bits"]), g or None, SHORT[dt])
+        assert np.array_equal(np.isnan(got), np.isnan(want)), key
+        assert np.array_equal(got[~np.isnan(got)], want[~np.isnan(want)]), key
+
+
+def test_oracle_fp16_zero_group_is_nan(qcol_golden):
+    # the reference's 1e-12 floor underflows in fp16: the zero group is NaN
+    from conftest import golden_values
+    z = qcol_golden
+    hits = [k for k in _cases(z, "qcol/") if str(z[f"{k}/name"]) == "edge"
+            and str(z[f"{k}/dtype"]) == "float16" and int(z[f"{k}/group"]) == 16]
+    assert hits
+    for k in hits:
+        out = golden_values(z[f"{k}/out"], "float16")
+        assert np.isnan(out[:16]).all() and not np.isnan(out[32:]).any()
+
+
+def test_oracle_rtn_layer(qcol_golden):
+    from conftest import SHORT, golden_values
+    z = qcol_golden
+    for key in _cases(z, "rtn/"):
+        dt = str(z[f"{key}/dtype"])
+        w = golden_values(z[f"{key}/w"], dt)
+        g = int(z[f"{key}/group"])
+        got = o.rtn_layer_fake(w, int(z[f"{key}/bits"]), g or None, SHORT[dt])
+        assert np.array_equal(got, golden_values(z[f"{key}/out"], dt)), key
+
+
+def test_oracle_gptq_act_order(gptq_ao_golden):
+    """quantize.gptq_layer with its default act_order=True (quantize.py:97-107),
+    and a 3-bit case without it, given the reference's inverse Hessian and
+    activation energies: bit for bit."""
+    z = gptq_ao_golden
+    for key in _cases(z, "gptq/"):
+        g = int(z[f"{key}/group"])
+        ao = int(z[f"{key}/act_order"])
+        got = o.gptq_fake_quant_columns(z[f"{key}/w"], z[f"{key}/h_inv"], int(z[f"{key}/bits"]),
+                                        g or None, z[f"{key}/act_mag"] if ao else None)
+        assert np.array_equal(got, z[f"{key}/wq"]), key
