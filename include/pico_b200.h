@@ -66,6 +66,14 @@ PK_API const char* pk_last_error_string(void);
  * site that recorded it; reset != 0 clears it. */
 PK_API int pk_device_status(int* code, int* where, int reset);
 
+/* Limit of every device-side wait of this library on the current device
+ * (mbarrier phases, the sharded layers' peer flags), in nanoseconds at the
+ * highest SM clock; 0 restores the built-in ~2 s. A wait that runs out
+ * records PK_ERR_TIMEOUT and its site in the device status word and the
+ * kernel returns without its result (pk_device_status reads it). Synchronous.
+ * No counterpart in the reference (Triton kernels have no bounded waits). */
+PK_API int pk_set_wait_limit_ns(int64_t ns);
+
 /* ---------------------------------------------------------------------- */
 /* int4 quantization and packing                                           */
 /* ---------------------------------------------------------------------- */

@@ -79,6 +79,7 @@ SIGNATURES = {
                                      _int, _i64, _i64, _int, _int, _vp, _vp, _vp, _sz, _vp]),
     "pk_fake_quant_groups": (_int, [_vp, _int, _i64, _i64, _i64, _i64, _int, _vp, _i64, _vp]),
     "pk_gptq_ref": (_int, [_vp, _vp, _i64, _i64, _int, _int, _vp, _vp]),
+    "pk_set_wait_limit_ns": (_int, [_i64]),
     "pk_set_weight_staging": (_int, [_int]),
     "pk_debug_phase_stamps": (_int, [_vp, _sz]),
 }
@@ -184,6 +185,13 @@ def workspace(device: torch.device, nbytes: int, tag: str = "splitk",
         buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
         _workspaces[key] = buf
     return buf
+
+
+def set_wait_limit(seconds: float | None) -> None:
+    """Limit of the kernels' device-side waits on the current device (None:
+    the built-in ~2 s); a wait that runs out is reported by device_status()."""
+    ns = 0 if seconds is None else max(1, int(seconds * 1e9))
+    check(load().pk_set_wait_limit_ns(ns), "pk_set_wait_limit_ns")
 
 
 def reset_workspaces() -> None:

@@ -29,8 +29,9 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 void ok() { g_msg[0] = '\0'; }
 
-// First error code recorded by a device-side bounded wait, and where.
-__device__ int g_device_status[2];
+// First error code recorded by a device-side bounded wait, and where; then
+// the wait limit in SM cycles as a 64-bit word (0: the built-in default).
+__device__ __align__(8) int g_device_status[4];
 
 constexpr int kMaxDevices = 64;
 int* g_status_ptr[kMaxDevices] = {};
@@ -940,6 +941,23 @@ int pk_gptq_ref(float* wt, const float* h_inv, int64_t K, int64_t N, int out_gro
   if (bits < 2 || bits > 8) return fail(PK_ERR_SHAPE, "bits must be in [2, 8] (got %d)", bits);
   cudaError_t e = launch_gptq_ref(wt, h_inv, K, N, out_group, bits, err_scratch, as_stream(stream));
   if (e != cudaSuccess) return cuda_fail(e, "gptq (reference rule) launch");
+  ok();
+  return PK_OK;
+}
+
+int pk_set_wait_limit_ns(int64_t ns) {
+  if (ns < 0) return fail(PK_ERR_SHAPE, "the wait limit must be >= 0 ns (0: default)");
+  int* p = device_status_ptr();
+  if (p == nullptr) return fail(PK_ERR_CUDA, "device status word unavailable");
+  int dev = 0, khz = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "SM clock rate");
+  // SM cycles at the highest clock: the limit is at least `ns` at any clock
+  long long cycles = ns == 0 ? 0 : ns / 1000000 * khz + (ns % 1000000) * khz / 1000000;
+  if (ns > 0 && cycles < 1) cycles = 1;
+  e = cudaMemcpy(p + 2, &cycles, sizeof(cycles), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(e, "set the wait limit");
   ok();
   return PK_OK;
 }

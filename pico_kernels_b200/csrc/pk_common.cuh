@@ -3,9 +3,9 @@
 // and the smem matrix descriptors the tensor core reads.
 //
 // Every wait in this library is bounded: a wait that does not complete within
-// PK_WAIT_CYCLES SM cycles records PK_ERR_TIMEOUT in the device status word and
-// returns false, and the caller unwinds (frees TMEM, returns) instead of
-// spinning forever.
+// the wait limit (pk_set_wait_limit_ns; by default PK_WAIT_CYCLES SM cycles,
+// ~2 s) records PK_ERR_TIMEOUT in the device status word and returns false,
+// and the caller unwinds (frees TMEM, returns) instead of spinning forever.
 #pragma once
 
 #include <cstdint>
@@ -29,6 +29,17 @@ __device__ __forceinline__ void record_error(int* status, int code, int where) {
   if (status != nullptr) {
     if (atomicCAS(status, 0, code) == 0) status[1] = where;
   }
+}
+
+// Wait limit in SM cycles: the 64-bit word after the status code and site
+// (pk_set_wait_limit_ns), or PK_WAIT_CYCLES when it is 0 or there is no
+// status word. Read only once a wait did not complete on its first probe.
+__device__ __forceinline__ long long wait_limit(const int* status) {
+  if (status != nullptr) {
+    const long long v = *reinterpret_cast<const volatile long long*>(status + 2);
+    if (v > 0) return v;
+  }
+  return PK_WAIT_CYCLES;
 }
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -74,18 +85,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return ok != 0;
 }
 
-// Wait for phase `parity` of `bar` to complete, for at most PK_WAIT_CYCLES SM
-// clock cycles (about 2 s at full clock). The bound is checked on the SM's
+// Wait for phase `parity` of `bar` to complete, for at most the wait limit
+// (SM clock cycles; about 2 s at full clock by default). The bound is checked on the SM's
 // own cycle counter: cheap to read, unlike the global timer.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int where) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const long long t0 = clock64();
+  const long long limit = wait_limit(status);
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(a, parity)) return true;
-    if (clock64() - t0 > PK_WAIT_CYCLES) {
+    if (clock64() - t0 > limit) {
       record_error(status, PK_ERR_TIMEOUT, where);
       return false;
     }
@@ -113,9 +125,10 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, 
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const long long t0 = clock64();
+  const long long limit = wait_limit(status);
   while (true) {
     if (mbar_try_wait_hint(a, parity, hint_ns)) return true;
-    if (clock64() - t0 > PK_WAIT_CYCLES) {
+    if (clock64() - t0 > limit) {
       record_error(status, PK_ERR_TIMEOUT, where);
       return false;
     }
@@ -381,6 +394,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
                                                   int where) {
   const uint32_t a = smem_u32(bar);
   const long long t0 = clock64();
+  const long long limit = wait_limit(status);
   while (true) {
     uint32_t ok;
     asm volatile(
@@ -391,7 +405,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
         : "r"(a), "r"(parity)
         : "memory");
     if (ok) return true;
-    if (clock64() - t0 > PK_WAIT_CYCLES) {
+    if (clock64() - t0 > limit) {
       record_error(status, PK_ERR_TIMEOUT, where);
       return false;
     }
@@ -661,11 +675,12 @@ __device__ __forceinline__ void peer_exchange_finish(const P& p, bool stored, in
   *expected = target;
   const unsigned* own = reinterpret_cast<const unsigned*>(p.peer_flag[p.rank]);
   const long long t0 = clock64();
+  const long long limit = wait_limit(status);
   while (true) {
     unsigned v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(own) : "memory");
     if (static_cast<int>(v - target) >= 0) break;
-    if (clock64() - t0 > PK_WAIT_CYCLES) {
+    if (clock64() - t0 > limit) {
       record_error(status, PK_ERR_TIMEOUT, where);
       break;
     }
