@@ -585,24 +585,31 @@ def phase_leg(work, chunk: int) -> dict:
         torch.cuda.synchronize()
     finally:
         lib.pk_debug_phase_stamps(None, 0)
-    st = buf.cpu()
-    st = st[st[:, 0] > 0].double()
-    if len(st) == 0:
+    # rows [half][cta]: launches alternate between the halves, so they hold
+    # the last launch and the one before it (the later entries: the last)
+    raw = buf.cpu().view(2, rows // 2, 8)
+    ctas = int((raw[0, :, 0] > 0).sum())
+    if ctas == 0:
         return {"ctas": 0}
+    h0, h1 = raw[0, :ctas].double(), raw[1, :ctas].double()
+    prev, st = (h0, h1) if h1[:, 1].min() > h0[:, 1].min() else (h1, h0)
     t0 = st[:, 0].min()
 
     def stat(x):
         x = x / 1e3
         return {"median": round(float(x.median()), 3), "max": round(float(x.max()), 3)}
     return {
-        "ctas": len(st), "sms": int(st[:, 5].unique().numel()),
+        "ctas": ctas, "sms": int(st[:, 5].unique().numel()),
+        "gap_after_previous_launch_us": round(float((st[:, 1].min() - prev[:, 4].max()) / 1e3), 3),
         "entry_us": stat(st[:, 0] - t0),
         "wait_released_us": stat(st[:, 1] - t0),
         "first_weights_after_wait_us": stat(st[:, 2] - st[:, 1]),
         "arithmetic_us": stat(st[:, 3] - st[:, 2]),
         "reduction_and_store_us": stat(st[:, 4] - st[:, 3]),
         "end_us": stat(st[:, 4] - t0),
-        "note": "last launch of a 64-step chain; times from its first CTA's entry (%globaltimer)",
+        "note": ("last launch of a 64-step chain; times from its first CTA's entry "
+                 "(%globaltimer); the gap runs from the previous launch's last CTA end to "
+                 "this launch's dependency wait returning"),
     }
 
 

@@ -222,12 +222,15 @@ PK_API int pk_set_weight_staging(int mode);
 
 /* Profiling aid: while dev_buf is set (NULL turns it off), each CTA of the
  * M = 1 decode GEMVs launched afterwards writes 8 uint64 words at
- * dev_buf[8 * cta]: %globaltimer at entry, after griddepcontrol.wait, when
- * its first weights landed, when its arithmetic ended and when its output
- * was stored, then its SM id, its unit count and a kernel-specific word.
- * Launches whose grid needs more than `bytes` record nothing. Kernels
- * captured in a CUDA graph keep the setting they were captured with. No
- * counterpart in the reference. */
+ * dev_buf[slot * bytes / 16 + 8 * cta]: %globaltimer at entry, after
+ * griddepcontrol.wait, when its first weights landed, when its arithmetic
+ * ended and when its output was stored, then its SM id, its unit count and
+ * a kernel-specific word. `slot` alternates 0, 1 from launch to launch (the
+ * two halves of the buffer), so the last two launches of a chain are both
+ * kept. Launches whose grid needs more than `bytes` (grid * 128) record
+ * nothing. Kernels captured in a CUDA
+ * graph keep the setting they were captured with. No counterpart in the
+ * reference. */
 PK_API int pk_debug_phase_stamps(void* dev_buf, size_t bytes);
 
 /* ---------------------------------------------------------------------- */
@@ -247,24 +250,26 @@ PK_API int pk_ipc_close(void* ptr);
 
 /* One rank's slice of an N-sharded W4A16 layer, y[M, N_full] = A @ dequant(W),
  * where this rank holds columns [n_offset, n_offset + N) (Wp [K, N/2],
- * scales [K/g, N]). The local kernel (the one pk_w4a16_gemm picks with
- * split_k = 0: GEMV, decode or skinny) writes its columns straight into every
- * rank's output buffer peer_out[r] (fp32 or bf16 [M, ldo] with ldo >= N_full, mapped
- * with pk_ipc_open), then its last CTA adds 1 to every peer's arrival count
- * peer_flag[r] (release, system scope) and waits, at most ~2 s, until its own
- * count reaches the next multiple of world - 1: on return every rank's
- * columns are in peer_out[rank]. Each peer_flag[r] is 8 zero-initialised,
- * 8-byte aligned bytes in rank r's memory (the count, then rank r's own
- * expected count, advanced by the kernel, so CUDA graph replays stay in
- * step). All ranks call it in the same order; a buffer must not be
- * rewritten by the next call before its reader is done (alternate two
- * buffers). Needs a workspace of
- * pk_w4a16_workspace_size bytes (at least 64 KB). Covers the GEMV's shapes
- * (M = 1, and M = 2 on slices of 16 MB or more), the decode kernel's (M <= 32,
- * K % 128 == 0, N % 128 == 0, group 128) and the skinny kernel's where
- * pk_w4a16_gemm would pick it (32 < M <= 256); world <= 8. Returns
- * PK_ERR_UNSUPPORTED otherwise (the fused prefill kernel has no exchange), so
- * the caller can exchange with NCCL instead.
+ * scales [K/g, N]). The local kernel (the one pk_w4a16_gemm picks without a
+ * workspace and with split_k = 0: the GEMV, the decode kernel, the skinny
+ * kernel, or the fused tcgen05 prefill) writes its columns straight into
+ * every rank's output buffer peer_out[r] (fp32 or bf16 [M, ldo] with ldo >=
+ * N_full, mapped with pk_ipc_open), then its last CTA adds 1 to every peer's
+ * arrival count peer_flag[r] (release, system scope) and waits, bounded (the
+ * wait limit, pk_set_wait_limit_ns), until its own count reaches the next
+ * multiple of world - 1: on return every rank's columns are in
+ * peer_out[rank]. Each peer_flag[r] is 8 zero-initialised, 8-byte aligned
+ * bytes in rank r's memory (the count, then rank r's own expected count,
+ * advanced by the kernel, so CUDA graph replays stay in step). All ranks call
+ * it in the same order; a buffer must not be rewritten by the next call
+ * before its reader is done (alternate two buffers). Needs a workspace of
+ * pk_w4a16_workspace_size bytes (at least 64 KB); world <= 8. The kernel is
+ * chosen from the shape alone, so every rank of a layer takes the same path:
+ * shapes no kernel with the exchange serves (K or N not a multiple of 64, or
+ * a group size not a multiple of 64 on the prefill) return
+ * PK_ERR_UNSUPPORTED on every rank, and the caller can exchange with NCCL
+ * instead; a rank whose A, Wp or scales are not 16-byte aligned (or lda not a
+ * multiple of 8) gets PK_ERR_ALIGN, an error rather than a fallback.
  * Replaces the all-gather that gemm_int4.int4_gemm's callers would need on a
  * sharded layer (no counterpart in the reference). */
 PK_API int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t* wp,

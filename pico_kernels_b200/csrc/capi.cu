@@ -657,7 +657,13 @@ int fp8_gemm_impl(const uint8_t* a8, const uint8_t* b8, int64_t M, int64_t N, in
 // Kernel of the fused exchange for a shape, or -1 when none has one: decided
 // from the shape alone (aligned stand-in pointers, lda = K), so that every
 // rank of an N-sharded layer reaches the same answer.
-enum { kPathGemv = 0, kPathDecode = 1, kPathSkinny = 2 };
+enum { kPathGemv = 0, kPathDecode = 1, kPathSkinny = 2, kPathPrefill = 3 };
+// The fused tcgen05 W4A16 prefill: 64-row K stages, scales on 64-row
+// boundaries (the shapes pk_w4a16_gemm sends to it without a workspace).
+bool prefill_shape_ok(int64_t M, int64_t N, int64_t K, int group, bool grouped) {
+  return K % 64 == 0 && N % 64 == 0 && (!grouped || group % 64 == 0) && M < (1ll << 31) &&
+         N < (1ll << 31) && K < (1ll << 31);
+}
 int sharded_path(int64_t M, int64_t N, int64_t K, int group, bool grouped) {
   const void* aligned = reinterpret_cast<const void*>(256);
   const void* sc = grouped ? aligned : nullptr;
@@ -666,6 +672,7 @@ int sharded_path(int64_t M, int64_t N, int64_t K, int group, bool grouped) {
   if (decode_supported(M, N, K, group, sc, K, aligned)) return kPathDecode;
   if (skinny_supported(M, N, K, group, sc, K, aligned) && skinny_preferred(M, N, K))
     return kPathSkinny;
+  if (prefill_shape_ok(M, N, K, group, grouped)) return kPathPrefill;
   return -1;
 }
 
@@ -845,11 +852,15 @@ int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t
   if (path < 0)
     return fail(PK_ERR_UNSUPPORTED,
                 "the fused exchange covers the GEMV, decode and skinny kernels' shapes only");
+  const bool aligned16 = (reinterpret_cast<uintptr_t>(wp) & 15) == 0;
   const bool readable =
       path == kPathGemv     ? gemv_supported(M, N, K, group_size, scales, lda, a, wp)
       : path == kPathDecode ? decode_supported(M, N, K, group_size, scales, lda, a)
-                            : skinny_supported(M, N, K, group_size, scales, lda, a) &&
-                                  (reinterpret_cast<uintptr_t>(wp) & 15) == 0;
+      : path == kPathSkinny ? skinny_supported(M, N, K, group_size, scales, lda, a) && aligned16
+                            : lda % 8 == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
+                                  aligned16 &&
+                                  (scales == nullptr ||
+                                   (reinterpret_cast<uintptr_t>(scales) & 15) == 0);
   if (!readable)
     return fail(PK_ERR_ALIGN,
                 "sharded W4A16: A, the packed weights and the scales must be 16-byte aligned "
@@ -906,6 +917,32 @@ int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t
   }
   sh.done = ws_counters(workspace) + (kMaxCounters - 1);
   const char* why = "";
+  if (path == kPathPrefill) {
+    GemmArgs g{};
+    g.kind = GemmArgs::kW4A16;
+    g.a = a;
+    g.a_dtype = a_dtype;
+    g.lda = lda;
+    g.b = wp;
+    g.ldb = N / 2;
+    g.scales = scales;
+    g.group = group_size;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.split = 1;
+    g.out = reinterpret_cast<void*>(peer_out[rank]);
+    g.out_dtype = out_dtype;
+    g.ldc = ldo;
+    g.out_scale = scales ? 1.0f : scalar_scale;
+    g.status = device_status_ptr();
+    g.peers = sh;
+    cudaError_t e = launch_gemm_tc(g, as_stream(stream), &why);
+    if (e == cudaErrorInvalidValue && why[0] != '\0') return fail(PK_ERR_ALIGN, "%s", why);
+    if (e != cudaSuccess) return cuda_fail(e, "sharded w4a16 prefill launch");
+    ok();
+    return PK_OK;
+  }
   cudaError_t e = cluster ? launch_w4a16_gemv_cluster(p, as_stream(stream), &why, &sh)
                   : path == kPathGemv     ? launch_w4a16_gemv(p, as_stream(stream), &why, &sh)
                   : path == kPathDecode ? launch_w4a16_decode(p, as_stream(stream), &why, &sh)

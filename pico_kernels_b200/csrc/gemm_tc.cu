@@ -91,6 +91,8 @@ struct Params {
   const float* scale_b;
   int whole;             // pair kernel: units that are whole tiles; each later tile is two
                          // units of half its columns (the last wave's tail), 16-bit kinds
+  OutputShard peers;     // one-CTA kernel without split-K: world > 0 stores every output
+                         // into all ranks' buffers and ends with the flag barrier
 };
 
 // The epilogue multiplier: the host's out_scale, or, for scales that live on
@@ -203,6 +205,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int k_tiles_total = (p.K + C::kBK - 1) / C::kBK;
   const int num_units = p.num_m * p.num_n * p.split;
+  bool stored = false;  // this thread wrote output (sharded exchange: fence before arriving)
 
   if (warp == kTmaWarp && lane == 0) {
     for (int i = 0; i < C::kStages; ++i) {
@@ -361,8 +364,17 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
               for (int e = 0; e < 8; ++e)
                 v[e] = __uint_as_float(raw[i + (kInt4 ? ((e & 3) * 2 + (e >> 2)) : e)]) * out_scale;
               const int col = col0 + c * 32 + i;
-              if (col < p.N)
-                store8(p.out, p.out_dtype, row * p.ldc + col, v, col + 8 <= p.N, min(8, p.N - col));
+              if (col < p.N) {
+                if (p.peers.world == 0) {
+                  store8(p.out, p.out_dtype, row * p.ldc + col, v, col + 8 <= p.N, min(8, p.N - col));
+                } else {
+                  for (int r = 0; r < p.peers.world; ++r)
+                    store8(reinterpret_cast<void*>(p.peers.peer_out[r]), p.out_dtype,
+                           row * p.ldc + p.peers.n_offset + col, v, col + 8 <= p.N,
+                           min(8, p.N - col));
+                  stored = true;
+                }
+              }
             }
           }
         }
@@ -495,6 +507,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
+  if (p.peers.world > 1) peer_exchange_finish(p.peers, stored, p.status, kSiteGemmPeers);
 }
 
 // ---------------------------------------------------------------------------
@@ -765,6 +778,7 @@ cudaError_t launch_typed(const GemmArgs& g, cudaStream_t s, const char** why) {
   p.grouped = g.scales != nullptr;
   p.a_is_f16 = g.a_dtype == PK_F16;
   p.status = g.status;
+  p.peers = g.peers;
   const int units = p.num_m * p.num_n * p.split;
   const int grid = units < num_sms() ? units : num_sms();
   auto kernel = gemm_tc_kernel<kKind, kInt4>;
@@ -878,6 +892,10 @@ size_t gemm_splitk_workspace_bytes(int64_t M, int64_t N, int split) {
 }
 
 cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t s, const char** why) {
+  if (g.peers.world > 0 && (g.kind != GemmArgs::kW4A16 || g.split > 1)) {
+    *why = "the output exchange covers the fused W4A16 prefill without split-K only";
+    return cudaErrorInvalidValue;
+  }
   // Pair tiles for dense / fp8 products without split-K that have rows for both
   // halves of a pair, unless the pair tiles make at most one wave: then
   // one-CTA tiles keep at least as many SMs busy and start sooner (fp8

@@ -28,6 +28,7 @@ enum WaitSite : int {
   kSiteGemmMma = 202,
   kSiteGemmEpilogue = 203,
   kSiteGemmDequant = 204,
+  kSiteGemmPeers = 205,
   kSiteGemvProducer = 301,
   kSiteGemvConsumer = 302,
   kSiteGemvPeers = 303,
@@ -173,10 +174,11 @@ cudaError_t launch_w4a16_gemv_cluster(const DecodeArgs& args, cudaStream_t s, co
 // scales into shared memory before the previous kernel in the stream ends.
 void set_weight_staging(int mode);
 int weight_staging();
-// Phase stamps (pk_debug_phase_stamps): the buffer, when set and at least
-// `need` bytes long, else nullptr.
+// Phase stamps (pk_debug_phase_stamps): for a launch of `grid` CTAs, the
+// half of the buffer this launch writes (halves alternate launch by launch,
+// so the last two are kept), or nullptr when unset or too small.
 void set_phase_stamps(void* buf, size_t bytes);
-uint64_t* phase_stamps(size_t need);
+uint64_t* phase_stamps(size_t grid);
 
 // ---- gemm_tc.cu (persistent tcgen05 GEMM: fp8, dense split-K, W4A16 prefill)
 struct GemmArgs {
@@ -199,6 +201,7 @@ struct GemmArgs {
   float* partials;      // split-K workspace
   unsigned* sems;
   int* status;
+  OutputShard peers;    // W4A16 prefill of an N-sharded layer (world 0: unsharded)
 };
 int64_t gemm_tiles(int64_t M, int64_t N);
 size_t gemm_splitk_workspace_bytes(int64_t M, int64_t N, int split);

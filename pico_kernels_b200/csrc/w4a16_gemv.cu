@@ -613,7 +613,7 @@ cudaError_t launch_w4a16_gemv(const DecodeArgs& a, cudaStream_t s, const char** 
   p.partials = a.partials;
   p.sems = a.sems;
   p.status = a.status;
-  p.stamps = phase_stamps(static_cast<size_t>(gemv_grid(a.N, a.K)) * 64);
+  p.stamps = phase_stamps(static_cast<size_t>(gemv_grid(a.N, a.K)));
   if (grouped) {
     const int64_t groups = (a.K + a.group - 1) / a.group;
     if (!encode_tmap_2d(&tmS, dt, a.scales, a.N, groups, a.N * 2, kCols,

@@ -10,33 +10,50 @@
 // itself; what decides the time per GEMM is how much of each launch's work
 // overlaps the launch before it, and how short its own critical path is.
 //
-//  * Partition. The columns are cut into strips of 256 (128 packed bytes per
-//    row); each strip's K rows are split over `split` CTAs, which form one
-//    thread-block cluster (split <= 8). CTA r of a strip owns units
-//    [U*r/split, U*(r+1)/split) of 256 rows (U = K/256). strips * split <=
-//    the SM count, so each CTA owns one SM and never waits for a second wave.
-//  * Footprint. ~104 KB of shared memory and 288 threads, so that the next
-//    launch's CTA (started early by programmatic dependent launch) fits on
-//    the same SM and issues its weight traffic while this one computes.
-//  * Loads. Warp 8 (one thread) is the TMA producer of a 3-slot ring: per
-//    unit four 64-row weight boxes (each with its own mbarrier, so a warp
-//    starts when the box holding its rows lands), the unit's two group-scale
-//    rows, and, on a separate barrier, the unit's 256 activations. Before
+//  * Partition. The columns are cut into strips of 128 (64 packed bytes per
+//    row); each strip's K rows are split over `split` CTAs (split <= 4),
+//    which form one thread-block cluster. CTA r of a strip owns units
+//    [U*r/split, U*(r+1)/split) of 512 rows (U = K/512). strips * split <=
+//    the SM count, so the grid is one wave of one CTA per SM.
+//  * Footprint. ~145 KB of shared memory (a 4-slot ring), so that no SM
+//    holds two CTAs of one grid: with room for two, CTAs started early by
+//    programmatic dependent launch were packed two to an SM on ~12 SMs, whose
+//    doubled arithmetic then set every launch's critical path. Clusters of 4:
+//    at one CTA per SM a B200 holds 33 of them at once but only 15 clusters
+//    of 8, which left a sixteenth waiting for the first ones to finish.
+//  * Loads. Warp 8 (one thread) is the TMA producer of a 4-slot ring: per
+//    unit four 128-row weight boxes (each with its own mbarrier, so a warp
+//    starts when the box holding its rows lands), the unit's four group-scale
+//    rows, and, on a separate barrier, the unit's 512 activations. Before
 //    griddepcontrol.wait it prefetches the CTA's weights into L2 (a hint that
 //    cannot return stale data); with weight staging on (pk_set_weight_staging)
 //    it loads the first units' weights and scales into shared memory there
 //    instead, and only the activations wait for the previous kernel.
-//  * Arithmetic: exactly the CUDA-core GEMV's (w4a16_gemv.cu). Warp w takes
-//    rows [32w, 32w + 32) of every unit (one scale group), lane l columns
-//    [8l, 8l + 8); one LOP3 per nibble makes the fp32 pattern of
-//    (q + 8) * 16^p * 2^-149, activations are pre-scaled by 2^S, one packed
-//    fma.rn.f32x2 per two weights accumulates exact products, and per unit
-//    the +8 offset is removed, 2^(149 - S - 4p) undone and the fp32 group
-//    scale applied. All shared-memory traffic uses explicit ld/st.shared.
-//  * Reduction. The 8 warps' column sums meet in shared memory; then, after
-//    a cluster barrier, CTA r of the strip reads its share of the columns
-//    from all `split` CTAs' shared memory (distributed shared memory) and
-//    sums them in CTA order: deterministic, no global workspace, no atomics.
+//  * Arithmetic (the CUDA-core GEMV's exact-product scheme, w4a16_gemv.cu,
+//    with fewer instructions per word). Warp w takes rows [64w, 64w + 64) of
+//    every unit (within one scale group); lane l the word of columns
+//    [8(l % 16), 8(l % 16) + 8) in the rows of parity l / 16: one 32-bit word
+//    per row, two rows per warp instruction (128 contiguous bytes). XOR-ing the word with 0x88888888 turns every nibble into
+//    q + 8 (0..15); nibbles 0-5 are then masked in place (one AND each) and
+//    nibbles 6-7 after one right shift by 8, each read as an fp32 bit pattern
+//    worth (q + 8) * 16^p * 2^-149 (p = 0..5: subnormal, or the lowest normal
+//    binade, exact). Activations are pre-scaled by 2^S with S = clamp(248 -
+//    e_max, 30, 127) over the warp's 64 rows, so every product with a
+//    non-negligible activation is a normal fp32 number and exact; one packed
+//    fma.rn.f32x2 per two weights accumulates them. Per unit the +8 offset is
+//    removed with the sum of the scaled activations, 2^(149 - S - 4p) undone
+//    (exact) and the fp32 group scale applied: 1 XOR, 1 shift, 8 AND and 4
+//    FMA2 per 8 weights. The two row parities of a column meet by a shuffle. All shared-memory traffic uses explicit ld/st.shared.
+//  * Reduction. The 8 warps' column sums meet in shared memory; each other
+//    CTA of the cluster then pushes its 128 sums into the leader's (rank 0)
+//    shared memory with st.async, which completes bytes on the leader's
+//    mbarrier, and exits; the leader waits for them (bounded), sums the
+//    strip's columns in CTA order and stores them: deterministic, no global
+//    workspace, no atomics, and only one CTA per cluster waits or stores
+//    (in the sharded exchange, one system-scope fence per cluster).
+//  * Placement. Launched with the spread cluster scheduling policy, so a
+//    cluster's CTAs go to different SMs (a packed placement put two CTAs of
+//    the grid on some SMs and doubled their time).
 #include "pk_common.cuh"
 
 #include <cstring>
@@ -48,39 +65,42 @@
 namespace pk {
 namespace {
 
-constexpr int kRows = 256;              // K rows per unit
-constexpr int kCols = 256;              // columns per strip
-constexpr int kRowBytes = kCols / 2;    // packed bytes per row of a strip
+constexpr int kRows = 512;              // K rows per unit
+constexpr int kCols = 128;              // columns per strip
+constexpr int kRowBytes = kCols / 2;    // packed bytes per row of a strip (64)
 constexpr int kWarps = 8;               // dequant/FMA warps
 constexpr int kProducerWarp = kWarps;
 constexpr int kThreads = (kWarps + 1) * 32;
-constexpr int kRowsPerWarp = kRows / kWarps;  // 32
+constexpr int kRowsPerWarp = kRows / kWarps;  // 64: half a scale group
 constexpr int kGroup = 128;
 constexpr int kSub = 4;
-constexpr int kSubRows = kRows / kSub;            // 64
+constexpr int kSubRows = kRows / kSub;            // 128
 constexpr int kSubWBytes = kSubRows * kRowBytes;  // 8192
-constexpr int kMaxSplit = 8;
-constexpr int kStages = 3;
+constexpr int kABox = 256;                        // activations per TMA box (box limit 256)
+constexpr int kMaxSplit = 4;
+constexpr int kStages = 4;
 constexpr int kWBytes = kRows * kRowBytes;              // 32768
-constexpr int kSBytes = (kRows / kGroup) * kCols * 2;   // 1024: two 16-bit scale rows
-constexpr int kABytes = kRows * 2;                      // 512
-constexpr int kSlotBytes = kWBytes + kSBytes + kABytes;  // 34304 = 268 * 128
+constexpr int kSBytes = (kRows / kGroup) * kCols * 2;   // 1024: four 16-bit scale rows
+constexpr int kABytes = kRows * 2;                      // 1024
+constexpr int kSlotBytes = kWBytes + kSBytes + kABytes;  // 34816 = 272 * 128
 constexpr int kRingBytes = kStages * kSlotBytes;
 constexpr int kPairOff = kRingBytes;                     // per-warp activation pairs
 constexpr int kPairBytes = kWarps * kRowsPerWarp * 8;
-constexpr int kBarOff = kPairOff + kPairBytes;
-constexpr int kNumBars = kStages * (kSub + 2);           // full[kSub], afull, empty per slot
+constexpr int kInOff = kPairOff + kPairBytes;             // leader: [kMaxSplit][kCols] pushed sums
+constexpr int kInBytes = kMaxSplit * kCols * 4;
+constexpr int kBarOff = kInOff + kInBytes;
+constexpr int kNumBars = kStages * (kSub + 2) + 1;       // full[kSub], afull, empty per slot; pushed
 constexpr int kSmemBytes = kBarOff + kNumBars * 8 + 128;  // + 128 for the alignment fix-up
-// At the end the ring is free: the cross-warp sums and the CTA's column sums
-// (read by the cluster) reuse its first bytes.
+// At the end the ring is free: the cross-warp sums reuse its first bytes.
 constexpr int kRedOff = 0;                               // [kWarps][kCols] floats
-constexpr int kSumOff = kWarps * kCols * 4;              // [kCols] floats
-static_assert(kSumOff + kCols * 4 <= kRingBytes, "reduction buffers fit the ring");
-static_assert(kSmemBytes <= 115712, "two CTAs (this launch and the next) must fit an SM");
+static_assert(kWarps * kCols * 4 <= kRingBytes, "reduction buffer fits the ring");
+static_assert(kSmemBytes > 116 * 1024 && kSmemBytes <= 227 * 1024,
+              "one CTA per SM: more than half of the SM's shared memory");
 static_assert(kSlotBytes % 128 == 0, "slots stay 128-byte aligned");
 
+// The nibble flip as a kernel parameter (a constant-bank operand of the XOR).
 struct DecodeConsts {
-  uint32_t x[4];
+  uint32_t flip;
 };
 
 struct ClusterParams {
@@ -149,11 +169,21 @@ __device__ __forceinline__ void scales8(uint4 raw, uint64_t (&s)[4]) {
   }
 }
 
-__device__ __forceinline__ void cluster_arrive_release() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait_acquire() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 4 bytes into CTA `rank`'s shared memory at the same offset as `local`,
+// counted as completed transaction bytes on that CTA's mbarrier at the same
+// offset as `bar`.
+__device__ __forceinline__ void st_async_f32(uint32_t local, uint32_t bar, uint32_t rank, float v) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(
+          cluster_map(local, rank)),
+      "f"(v), "r"(cluster_map(bar, rank))
+      : "memory");
 }
 
 template <typename T, bool kGrouped>
@@ -169,6 +199,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOff);  // [slot][sub-box]
   uint64_t* afull = full + kStages * kSub;                        // [slot]
   uint64_t* empty = afull + kStages;                              // [slot]
+  uint64_t* pushed = empty + kStages;  // leader: the other CTAs' sums have landed
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -186,9 +217,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&afull[s], 1);
       mbar_init(&empty[s], kWarps);
     }
+    mbar_init(pushed, 1);
+    if (rank == 0 && p.split > 1)
+      mbar_arrive_expect_tx(pushed, static_cast<uint32_t>((p.split - 1) * kCols * 4));
     fence_barrier_init();
   }
   __syncthreads();
+  // Every CTA's barriers are initialised before any other CTA of the cluster
+  // pushes to them: arrive now, wait before the push.
+  if (p.split > 1) cluster_arrive_relaxed();
   // The next launch may start its prologue (weight prefetch) now; it waits
   // for this grid before reading activations or writing anything.
   griddep_launch_dependents();
@@ -215,19 +252,25 @@ __global__ void __launch_bounds__(kThreads, 2)
       };
       auto issue_a = [&](int i, int slot) {
         mbar_arrive_expect_tx(&afull[slot], kABytes);
-        tma_load_2d(smem + slot * kSlotBytes + kWBytes + kSBytes, &tmA, &afull[slot],
-                    (u0 + i) * kRows, 0);
+        for (int h = 0; h < kRows / kABox; ++h)
+          tma_load_2d(smem + slot * kSlotBytes + kWBytes + kSBytes + h * kABox * 2, &tmA,
+                      &afull[slot], (u0 + i) * kRows + h * kABox, 0);
       };
       const int pre = n_units < kStages ? n_units : kStages;
       if (p.early) {
         for (int i = 0; i < pre; ++i) issue_w(i, i);
       }
-      // the rest of the CTA's weights (all of them without staging) into L2
+      // the rest of the CTA's weights (all of them without staging) into L2,
+      // and the activations of the first units: L2 is coherent, so a line the
+      // previous kernel is still writing cannot come back stale
       for (int i = p.early ? pre : 0; i < n_units && i < pre + 4 * kStages; ++i) {
         const int k0 = (u0 + i) * kRows;
         for (int j = 0; j < kSub; ++j) tma_prefetch_l2_2d(&tmW, strip * kRowBytes, k0 + j * kSubRows);
         if constexpr (kGrouped) tma_prefetch_l2_2d(&tmS, strip * kCols, k0 / kGroup);
       }
+      for (int i = 0; i < pre; ++i)
+        for (int h = 0; h < kRows / kABox; ++h)
+          tma_prefetch_l2_2d(&tmA, (u0 + i) * kRows + h * kABox, 0);
       griddep_wait();
       if (!p.early) {
         for (int i = 0; i < pre; ++i) issue_w(i, i);
@@ -260,7 +303,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---------------- dequant / FMA warps ----------------
     griddep_wait();
     if (stamp) t_wait = globaltimer();
-    // -8 * 16^p * 2^-149 for the column pairs' positions (2,3) and (4,5)
+    // -8 * 16^p * 2^-149 for the column pairs' positions (0,1), (2,3), (4,5)
+    const uint64_t off01 = pack2(__uint_as_float(0x80000008u), __uint_as_float(0x80000080u));
     const uint64_t off23 = pack2(__uint_as_float(0x80000800u), __uint_as_float(0x80008000u));
     const uint64_t off45 = pack2(__uint_as_float(0x80080000u), __uint_as_float(0x80800000u));
     const uint32_t pairs = sbase + kPairOff + warp * kRowsPerWarp * 8;
@@ -269,20 +313,29 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t base = sbase + slot * kSlotBytes;
       if (!failed && !mbar_wait_sleep(&afull[slot], round & 1, p.status, kSiteGemvConsumer))
         failed = true;
-      // Activations: lane l scales row 32w + l; S = clamp(248 - e_max, 30, 127)
-      // from the largest exponent among the warp's rows.
-      const float av = lds_act<T>(base + kWBytes + kSBytes + (warp * kRowsPerWarp + lane) * 2);
-      uint32_t emax = (__float_as_uint(av) >> 23) & 0xFFu;
-      emax = __reduce_max_sync(0xffffffffu, emax);
+      // Activations: lane l scales rows 64w + l and 64w + 32 + l; S = clamp(248 -
+      // e_max, 30, 127) from the largest exponent among the warp's 64 rows.
+      const uint32_t abase = base + kWBytes + kSBytes + warp * kRowsPerWarp * 2;
+      const float av0 = lds_act<T>(abase + lane * 2);
+      const float av1 = lds_act<T>(abase + (32 + lane) * 2);
+      uint32_t emax = (__float_as_uint(av0) >> 23) & 0xFFu;
+      const uint32_t e1 = (__float_as_uint(av1) >> 23) & 0xFFu;
+      emax = __reduce_max_sync(0xffffffffu, emax > e1 ? emax : e1);
       int S = 248 - static_cast<int>(emax);
       S = S < 30 ? 30 : (S > 127 ? 127 : S);
-      const float as = av * exp2i(S);
-      sts_u64(pairs + lane * 8, pack2(as, as));
-      float t = as;
+      const float as0 = av0 * exp2i(S), as1 = av1 * exp2i(S);
+      sts_u64(pairs + lane * 8, pack2(as0, as0));
+      sts_u64(pairs + (32 + lane) * 8, pack2(as1, as1));
+      // A lane walks the rows of one parity (lane / 16): the sum of the scaled
+      // activations of that parity removes its +8 offsets. Rows 64w + l and
+      // 64w + 32 + l have the parity of l, so sum over lanes of equal l % 2.
+      float t = as0 + as1;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+      for (int o = 16; o > 1; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+      t = __shfl_sync(0xffffffffu, t, lane >> 4);
       const uint64_t asum = pack2(t, t);
-      // 2^(149 - S - 4p) for the pairs' positions (2,3) and (4,5)
+      // 2^(149 - S - 4p) for the pairs' positions (0,1), (2,3) and (4,5)
+      const uint64_t pw01 = pack2(exp2i(149 - S), exp2i(145 - S));
       const uint64_t pw23 = pack2(exp2i(141 - S), exp2i(137 - S));
       const uint64_t pw45 = pack2(exp2i(133 - S), exp2i(129 - S));
       // sub-box 0 carries the unit's scales; the warp's rows are in sub-box w/2
@@ -296,32 +349,35 @@ __global__ void __launch_bounds__(kThreads, 2)
       uint64_t sc[4];
       if constexpr (kGrouped) {
         const int srow = (warp * kRowsPerWarp) / kGroup;
-        scales8<T>(lds_v4(base + kWBytes + srow * kCols * 2 + lane * 16), sc);
+        scales8<T>(lds_v4(base + kWBytes + srow * kCols * 2 + (lane & 15) * 16), sc);
       } else {
 #pragma unroll
         for (int q = 0; q < 4; ++q) sc[q] = pack2(p.scalar_scale, p.scalar_scale);
       }
       __syncwarp();
 
+      // lane l: word l % 16 (columns 8(l%16) .. +8) of rows 64w + 2i + l / 16
       uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-      const uint32_t wrow = base + warp * kRowsPerWarp * kRowBytes + lane * 4;
+      const uint32_t wrow =
+          base + (warp * kRowsPerWarp + (lane >> 4)) * kRowBytes + (lane & 15) * 4;
+      const uint32_t prow = pairs + (lane >> 4) * 8;
 #pragma unroll
-      for (int b = 0; b < kRowsPerWarp / 8; ++b) {
+      for (int b = 0; b < kRowsPerWarp / 16; ++b) {
         uint32_t wv[8];
         uint64_t a2[8];
 #pragma unroll
-        for (int r = 0; r < 8; ++r) wv[r] = lds_u32(wrow + (b * 8 + r) * kRowBytes);
+        for (int r = 0; r < 8; ++r) wv[r] = lds_u32(wrow + (b * 8 + r) * 2 * kRowBytes);
 #pragma unroll
-        for (int r = 0; r < 8; ++r) a2[r] = lds_u64(pairs + (b * 8 + r) * 8);
+        for (int r = 0; r < 8; ++r) a2[r] = lds_u64(prow + (b * 8 + r) * 16);
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
-          const uint32_t w = wv[r];
-          const uint32_t lo = w << 8, hi = w >> 8;
+          const uint32_t w = wv[r] ^ dc.flip;  // every nibble q -> q + 8
+          const uint32_t hi = w >> 8;          // nibbles 6, 7 at positions 4, 5
           uint64_t d[4];
-          d[0] = pack2(__uint_as_float((lo & 0xF00u) ^ dc.x[0]), __uint_as_float((lo & 0xF000u) ^ dc.x[1]));
-          d[1] = pack2(__uint_as_float((w & 0xF00u) ^ dc.x[0]), __uint_as_float((w & 0xF000u) ^ dc.x[1]));
-          d[2] = pack2(__uint_as_float((w & 0xF0000u) ^ dc.x[2]), __uint_as_float((w & 0xF00000u) ^ dc.x[3]));
-          d[3] = pack2(__uint_as_float((hi & 0xF0000u) ^ dc.x[2]), __uint_as_float((hi & 0xF00000u) ^ dc.x[3]));
+          d[0] = pack2(__uint_as_float(w & 0xFu), __uint_as_float(w & 0xF0u));
+          d[1] = pack2(__uint_as_float(w & 0xF00u), __uint_as_float(w & 0xF000u));
+          d[2] = pack2(__uint_as_float(w & 0xF0000u), __uint_as_float(w & 0xF00000u));
+          d[3] = pack2(__uint_as_float(hi & 0xF0000u), __uint_as_float(hi & 0xF00000u));
 #pragma unroll
           for (int q = 0; q < 4; ++q) acc[q] = fma2(d[q], a2[r], acc[q]);
         }
@@ -329,8 +385,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       // fold the unit: remove the +8 offset, undo 2^S * 16^p, apply the scale
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const uint64_t c = fma2(q < 2 ? off23 : off45, asum, acc[q]);
-        tot[q] = fma2(mul2(c, q < 2 ? pw23 : pw45), sc[q], tot[q]);
+        const uint64_t off = q == 0 ? off01 : (q == 1 ? off23 : off45);
+        const uint64_t pw = q == 0 ? pw01 : (q == 1 ? pw23 : pw45);
+        const uint64_t c = fma2(off, asum, acc[q]);
+        tot[q] = fma2(mul2(c, pw), sc[q], tot[q]);
       }
       __syncwarp();  // every lane is done with the slot and the pairs
       if (lane == 0) mbar_arrive(&empty[slot]);
@@ -342,43 +400,46 @@ __global__ void __launch_bounds__(kThreads, 2)
   // ---------------- reduction: warps, then the cluster ----------------
   failed = __syncthreads_or(failed) != 0;  // every warp is done with the ring
   if (warp < kWarps) {
-    const float2 a0 = unpack2(tot[0]), a1 = unpack2(tot[1]);
-    const float2 a2 = unpack2(tot[2]), a3 = unpack2(tot[3]);
-    const uint32_t dst = sbase + kRedOff + (warp * kCols + lane * 8) * 4;
-    sts_v4f(dst, a0.x, a0.y, a1.x, a1.y);
-    sts_v4f(dst + 16, a2.x, a2.y, a3.x, a3.y);
+    // lanes l and l + 16 hold the two row parities of the same columns
+    float2 v[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      v[q] = unpack2(tot[q]);
+      v[q].x += __shfl_xor_sync(0xffffffffu, v[q].x, 16);
+      v[q].y += __shfl_xor_sync(0xffffffffu, v[q].y, 16);
+    }
+    if (lane < 16) {
+      const uint32_t dst = sbase + kRedOff + (warp * kCols + lane * 8) * 4;
+      sts_v4f(dst, v[0].x, v[0].y, v[1].x, v[1].y);
+      sts_v4f(dst + 16, v[2].x, v[2].y, v[3].x, v[3].y);
+    }
   }
   __syncthreads();
+  float colsum = 0.0f;
   if (threadIdx.x < kCols) {
-    float s = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) s += lds_f32(sbase + kRedOff + (w * kCols + threadIdx.x) * 4);
-    sts_f32(sbase + kSumOff + threadIdx.x * 4, s);
+    for (int w = 0; w < kWarps; ++w)
+      colsum += lds_f32(sbase + kRedOff + (w * kCols + threadIdx.x) * 4);
   }
-  cluster_arrive_release();
-  cluster_wait_acquire();  // every CTA of the strip has its column sums in place
+  if (p.split > 1) cluster_wait_acquire();  // the leader's barrier is initialised
   bool stored = false;
-  if (!failed) {
-    // CTA `rank` sums its share of the strip's columns over the cluster, in
-    // CTA order
-    const int c0 = kCols * rank / p.split, c1 = kCols * (rank + 1) / p.split;
-    const int col = c0 + static_cast<int>(threadIdx.x);
-    if (col < c1) {
-      const uint32_t addr = sbase + kSumOff + col * 4;
-      float x[kMaxSplit];
-#pragma unroll
-      for (int j = 0; j < kMaxSplit; ++j)
-        if (j < p.split) x[j] = ld_cluster_f32(cluster_map(addr, static_cast<uint32_t>(j)));
-      float v = 0.0f;
-#pragma unroll
-      for (int j = 0; j < kMaxSplit; ++j)
-        if (j < p.split) v += x[j];
-      emit_out(p.out, p.peers, p.out_dtype, static_cast<int64_t>(strip) * kCols + col, v);
+  const uint32_t in_base = sbase + kInOff;
+  if (rank != 0) {
+    // push this CTA's column sums into slot `rank` of the leader's buffer
+    if (threadIdx.x < kCols)
+      st_async_f32(in_base + (rank * kCols + threadIdx.x) * 4, smem_u32(pushed), 0u, colsum);
+  } else {
+    if (p.split > 1 &&
+        !mbar_wait(pushed, 0, p.status, kSiteGemvConsumer))  // the others' sums have landed
+      failed = true;
+    failed = __syncthreads_or(failed) != 0;
+    if (!failed && threadIdx.x < kCols) {
+      float v = colsum;  // in CTA order: rank 0 first, then ranks 1 .. split-1
+      for (int j = 1; j < p.split; ++j) v += lds_f32(in_base + (j * kCols + threadIdx.x) * 4);
+      emit_out(p.out, p.peers, p.out_dtype, static_cast<int64_t>(strip) * kCols + threadIdx.x, v);
       stored = true;
     }
   }
-  cluster_arrive_release();
-  cluster_wait_acquire();  // keep every CTA's shared memory alive until all reads are done
   if (stamp) {
     t_red = globaltimer();
     uint32_t smid;
@@ -441,12 +502,17 @@ void set_phase_stamps(void* buf, size_t bytes) {
   g_phase_stamps = static_cast<uint64_t*>(buf);
   g_phase_stamp_bytes = buf != nullptr ? bytes : 0;
 }
-uint64_t* phase_stamps(size_t need) {
-  return g_phase_stamps != nullptr && g_phase_stamp_bytes >= need ? g_phase_stamps : nullptr;
+uint64_t* phase_stamps(size_t grid) {
+  // two halves of the buffer, alternating launch by launch
+  if (g_phase_stamps == nullptr || g_phase_stamp_bytes < grid * 128) return nullptr;
+  static int calls = 0;
+  return g_phase_stamps + (calls++ & 1) * (g_phase_stamp_bytes / 16);
 }
 
 // CTAs per strip: as many as keep strips * split within one CTA per SM, at
-// most 8 (a portable cluster) and at most one per 256-row unit.
+// most 4 (clusters of 4 at one CTA per SM: 33 fit a B200 at once, clusters of
+// 8 only 15, which left a sixteenth cluster waiting for a second wave) and at
+// most one per 512-row unit.
 int gemv_cluster_split(int64_t N, int64_t K) {
   const int64_t strips = N / kCols;
   if (strips <= 0) return 0;
@@ -469,12 +535,15 @@ bool gemv_cluster_supported(int64_t M, int64_t N, int64_t K, int group, const vo
   return true;
 }
 
-// The cluster form wherever its grid keeps at least 3/4 of the SMs busy with
-// at least two CTAs per strip (below that the stream-K GEMV balances better).
+// The cluster form for small layers: its grid keeps at least 3/4 of the SMs
+// busy with at least two CTAs per strip, and each CTA has at most 4 units
+// (the ring holds them all). Longer K ranges stream better through the
+// stream-K GEMV's two CTAs per SM (Llama-70B down_proj: 35 vs 59 us).
 bool gemv_cluster_preferred(int64_t M, int64_t N, int64_t K) {
-  if (M != 1 || N % kCols != 0) return false;
+  if (M != 1 || N % kCols != 0 || K % kRows != 0) return false;
   const int split = gemv_cluster_split(N, K);
-  return split >= 2 && (N / kCols) * split * 4 >= 3ll * num_sms();
+  if (split < 2 || (N / kCols) * split * 4 < 3ll * num_sms()) return false;
+  return (K / kRows + split - 1) / split <= kStages;
 }
 
 cudaError_t launch_w4a16_gemv_cluster(const DecodeArgs& a, cudaStream_t s, const char** why,
@@ -484,7 +553,7 @@ cudaError_t launch_w4a16_gemv_cluster(const DecodeArgs& a, cudaStream_t s, const
   if (!encode_tmap_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.wp, a.N / 2, a.K, a.N / 2, kRowBytes,
                       kSubRows, CU_TENSOR_MAP_SWIZZLE_NONE, why))
     return cudaErrorInvalidValue;
-  if (!encode_tmap_2d(&tmA, dt, a.a, a.K, 1, a.lda * 2, kRows, 1, CU_TENSOR_MAP_SWIZZLE_NONE, why))
+  if (!encode_tmap_2d(&tmA, dt, a.a, a.K, 1, a.lda * 2, kABox, 1, CU_TENSOR_MAP_SWIZZLE_NONE, why))
     return cudaErrorInvalidValue;
   const bool grouped = a.scales != nullptr;
   if (grouped) {
@@ -506,7 +575,7 @@ cudaError_t launch_w4a16_gemv_cluster(const DecodeArgs& a, cudaStream_t s, const
   p.out = a.out;
   p.status = a.status;
   const int64_t grid = (a.N / kCols) * p.split;
-  p.stamps = phase_stamps(static_cast<size_t>(grid) * 64);
+  p.stamps = phase_stamps(static_cast<size_t>(grid));
   if (shard != nullptr) {
     if (shard->world < 1 || shard->world > kMaxPeers || shard->done == nullptr) {
       *why = "sharded GEMV: 1 <= world <= 8 and a workspace are required";
@@ -514,7 +583,7 @@ cudaError_t launch_w4a16_gemv_cluster(const DecodeArgs& a, cudaStream_t s, const
     }
     p.peers = *shard;
   }
-  const DecodeConsts dc{{0x800u, 0x8000u, 0x80000u, 0x800000u}};
+  const DecodeConsts dc{0x88888888u};
 
   auto launch = [&](auto kernel) -> cudaError_t {
     cudaError_t e = set_max_smem(reinterpret_cast<const void*>(kernel), kSmemBytes);
@@ -528,15 +597,17 @@ cudaError_t launch_w4a16_gemv_cluster(const DecodeArgs& a, cudaStream_t s, const
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = kSmemBytes;
     cfg.stream = s;
-    cudaLaunchAttribute attrs[2];
+    cudaLaunchAttribute attrs[3];
     attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attrs[0].val.programmaticStreamSerializationAllowed = 1;
     attrs[1].id = cudaLaunchAttributeClusterDimension;
     attrs[1].val.clusterDim.x = static_cast<unsigned>(p.split);
     attrs[1].val.clusterDim.y = 1;
     attrs[1].val.clusterDim.z = 1;
+    attrs[2].id = cudaLaunchAttributeClusterSchedulingPolicyPreference;
+    attrs[2].val.clusterSchedulingPolicyPreference = cudaClusterSchedulingPolicySpread;
     cfg.attrs = attrs;
-    cfg.numAttrs = 2;
+    cfg.numAttrs = 3;
     return cudaLaunchKernelEx(&cfg, kernel, tmW, tmA, tmS, p, dc);
   };
   if (a.a_dtype == PK_BF16)

@@ -72,8 +72,8 @@ def test_host_only_calls_work_without_gpu():
     assert host_call(a_dtype=_lib.PK_F32) == _lib.PK_ERR_DTYPE
     assert host_call(out_dtype=_lib.PK_I8) == _lib.PK_ERR_DTYPE
     # sharded W4A16: bad world / rank / slice are shape errors; shapes no kernel
-    # with the fused exchange serves (M > 256) report PK_ERR_UNSUPPORTED so the
-    # caller falls back to NCCL
+    # with the fused exchange serves (K not a multiple of 64) report
+    # PK_ERR_UNSUPPORTED so the caller falls back to NCCL
     outs = (ctypes.c_uint64 * 2)(4096, 8192)
     flags = (ctypes.c_uint64 * 2)(4096, 8192)
     sh = dict(a=4096, a_dtype=_lib.PK_BF16, lda=1024, wp=4096, scales=4096, scalar=1.0,
@@ -87,7 +87,7 @@ def test_host_only_calls_work_without_gpu():
     assert sharded_call(world=9) == _lib.PK_ERR_SHAPE
     assert sharded_call(rank=2) == _lib.PK_ERR_SHAPE
     assert sharded_call(n_offset=1536) == _lib.PK_ERR_SHAPE
-    assert sharded_call(M=300) == _lib.PK_ERR_UNSUPPORTED
+    assert sharded_call(M=300, K=1000, lda=1000) == _lib.PK_ERR_UNSUPPORTED
     # the fused-or-NCCL choice depends on the shape only: a misaligned A or
     # leading dimension on a covered shape is an error (never UNSUPPORTED,
     # which would send this rank alone to the all-gather), and an uncovered
@@ -95,7 +95,9 @@ def test_host_only_calls_work_without_gpu():
     assert sharded_call(a=4098) == _lib.PK_ERR_ALIGN
     assert sharded_call(lda=1025) == _lib.PK_ERR_ALIGN
     assert sharded_call(wp=4100) == _lib.PK_ERR_ALIGN
-    assert sharded_call(M=300, a=4098) == _lib.PK_ERR_UNSUPPORTED
+    assert sharded_call(M=300, K=1000, lda=1000, a=4098) == _lib.PK_ERR_UNSUPPORTED
+    # the fused prefill serves the other shapes: misaligned operands are errors there too
+    assert sharded_call(M=300, a=4098) == _lib.PK_ERR_ALIGN
     assert sharded_call(M=64, N=256, K=256, ldo=512, a=4098) in (_lib.PK_ERR_UNSUPPORTED,
                                                                  _lib.PK_ERR_ALIGN)
     assert sharded_call(M=64, N=256, K=256, ldo=512, a=4098) == \

@@ -127,7 +127,7 @@ def _decision_worker(rank, world, port, q):
         outs = (ctypes.c_uint64 * world)(*[4096 * (r + 1) for r in range(world)])
         flags = (ctypes.c_uint64 * world)(*[1 << 20 + r for r in range(world)])
         codes = {}
-        for M, N, K in ((1, 3584, 8192), (32, 1024, 28672), (300, 1024, 1024)):
+        for M, N, K in ((1, 3584, 8192), (32, 1024, 28672), (300, 1024, 1000)):
             a = 4096 + (2 if rank == 1 else 0)
             codes[M] = lib.pk_w4a16_gemm_sharded(
                 a, _lib.PK_BF16, K, 8192, 16384, 1.0, 128, M, N, K, _lib.PK_F32, N * world,

@@ -87,12 +87,15 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 1024, 2048), (16, 1024, 2048), (32, 1024, 1024),
-                                   (64, 1024, 1024), (200, 20480, 512)])
+@pytest.mark.parametrize("M,N,K", [(1, 1024, 2048), (1, 4096, 4096), (16, 1024, 2048),
+                                   (32, 1024, 1024), (64, 1024, 1024), (200, 20480, 512),
+                                   (300, 2048, 1024), (512, 1024, 2048)])
 def test_sharded_entry_one_rank(M, N, K):
     """pk_w4a16_gemm_sharded at world = 1 (no flag barrier): each kernel with
-    the exchange epilogue writes exactly its column slice of the full-width
-    buffer, bit-identical to the unsharded call (same kernel, same split)."""
+    the exchange epilogue (the stream-K and cluster GEMVs, the decode, skinny
+    and fused prefill kernels) writes exactly its column slice of the
+    full-width buffer, bit-identical to the unsharded call (same kernel, same
+    split)."""
     import ctypes
     from pico_kernels_b200 import _lib
     dev = torch.device("cuda")
