@@ -528,11 +528,17 @@ def _prime(runner_out) -> None:
     torch.cuda.synchronize()
 
 
-def _gate() -> None:
+def _gate(dist=None) -> None:
     """Hold the stream for ~0.1 ms before the start event, so that the graph
     launches behind it are already queued when timing starts: the timed
-    region then holds the steps' device time, not the host's submission."""
+    region then holds the steps' device time, not the host's submission.
+    With several ranks a one-element NCCL all-reduce follows on the stream:
+    it ends on every GPU at about the same time, so the ranks' timed regions
+    start together instead of one host's lag each (sharded steps wait for
+    each other, and a late rank would count its lag into the others' time)."""
     torch.cuda._sleep(200_000)
+    if dist is not None:
+        dist.all_reduce(torch.zeros(1, device="cuda"))
 
 
 def _time_graphs(runner_out, dist) -> float:
@@ -541,7 +547,7 @@ def _time_graphs(runner_out, dist) -> float:
     barrier(dist)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    _gate()
+    _gate(dist)
     e0.record()
     _replay(runner_out)
     e1.record()
@@ -642,7 +648,7 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
-    _gate()
+    _gate(dist)
     ev0.record()
     _replay(timed)
     ev1.record()
@@ -695,6 +701,8 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
     torch.cuda.synchronize()
     barrier(dist)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist is not None:
+        dist.all_reduce(torch.zeros(1, device="cuda"))  # start the ranks together
     e0.record()
     for i in range(e2e_steps):
         e2e_fn(i)

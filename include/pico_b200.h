@@ -265,8 +265,9 @@ PK_API int pk_ipc_close(void* ptr);
  * before its reader is done (alternate two buffers). Needs a workspace of
  * pk_w4a16_workspace_size bytes (at least 64 KB); world <= 8. The kernel is
  * chosen from the shape alone, so every rank of a layer takes the same path:
- * shapes no kernel with the exchange serves (K or N not a multiple of 64, or
- * a group size not a multiple of 64 on the prefill) return
+ * shapes no kernel with the exchange serves (K or N not a multiple of 64, a
+ * group size not a multiple of 64 on the prefill, or a prefill-sized call
+ * whose output slice is over 8 MB, where NCCL's all-gather is faster) return
  * PK_ERR_UNSUPPORTED on every rank, and the caller can exchange with NCCL
  * instead; a rank whose A, Wp or scales are not 16-byte aligned (or lda not a
  * multiple of 8) gets PK_ERR_ALIGN, an error rather than a fallback.

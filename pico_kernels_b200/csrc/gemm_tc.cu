@@ -507,7 +507,8 @@ __global__ void __launch_bounds__(Cfg<kKind, kInt4>::kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
-  if (p.peers.world > 1) peer_exchange_finish(p.peers, stored, p.status, kSiteGemmPeers);
+  if (p.peers.world > 1)
+    peer_exchange_finish(p.peers, stored, p.status, kSiteGemmPeers, gridDim.x * gridDim.y);
 }
 
 // ---------------------------------------------------------------------------

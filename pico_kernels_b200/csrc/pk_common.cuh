@@ -649,19 +649,22 @@ __device__ __forceinline__ void emit_out(void* out, const OutputShard& x, int ou
     store_elem(reinterpret_cast<void*>(x.peer_out[r]), out_dtype, idx + x.n_offset, v);
 }
 
-// Called by every thread of every CTA after its output stores. The CTA's
-// peer stores are ordered before one system-scope fence by thread 0 through
-// the barrier (the grid-synchronisation pattern), taken only by CTAs that
-// stored; the grid's last CTA adds 1 to each peer's flag (release, system
-// scope) and waits, bounded, until its own flag reaches its next expected
-// count, advanced in device memory so CUDA graph replays stay in step.
+// Called by every thread of each CTA that arrives, after its output stores;
+// `arrivals` CTAs of the grid arrive in all (every CTA, or one per cluster
+// when a cluster barrier has already ordered its CTAs' stores before the
+// leader's). The CTA's peer stores are ordered before one system-scope fence
+// by thread 0 through the barrier (the grid-synchronisation pattern), taken
+// only by CTAs that stored; the last of the `arrivals` CTAs adds 1 to each
+// peer's flag (release, system scope) and waits, bounded, until its own flag
+// reaches its next expected count, advanced in device memory so CUDA graph
+// replays stay in step.
 template <typename P>
 __device__ __forceinline__ void peer_exchange_finish(const P& p, bool stored, int* status,
-                                                     int where) {
+                                                     int where, unsigned arrivals) {
   const bool any = __syncthreads_or(stored) != 0;
   if (threadIdx.x + threadIdx.y + threadIdx.z != 0) return;
   if (any) __threadfence_system();
-  const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+  const unsigned total = arrivals;
   unsigned prev;
   asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p.done) : "memory");
   if (prev != total - 1) return;

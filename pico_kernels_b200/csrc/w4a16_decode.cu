@@ -369,7 +369,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) tmem_dealloc(tmem, C::kTmemCols);
-  if (peers.world > 1) peer_exchange_finish(peers, stored, status, kSiteDecodePeers);
+  if (peers.world > 1) {
+    if (use_cluster) {
+      // every CTA of the cluster has stored its share of the columns: one
+      // system-scope fence and one arrival per cluster (by its rank 0)
+      cluster_sync();
+      if (cluster_ctarank() == 0)
+        peer_exchange_finish(peers, true, status, kSiteDecodePeers, gridDim.x);
+    } else {
+      peer_exchange_finish(peers, stored, status, kSiteDecodePeers, gridDim.x * gridDim.y);
+    }
+  }
 }
 
 CUtensorMapDataType tmap_type(int dt) {

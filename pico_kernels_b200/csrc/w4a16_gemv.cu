@@ -207,7 +207,7 @@ __device__ __forceinline__ void store_col(const GemvParams& p, int m, int64_t co
 
 // After every CTA's stores: the shared flag barrier of the fused exchange.
 __device__ __forceinline__ void sharded_finish(const GemvParams& p, bool stored) {
-  peer_exchange_finish(p, stored, p.status, kSiteGemvPeers);
+  peer_exchange_finish(p, stored, p.status, kSiteGemvPeers, gridDim.x);
 }
 
 // Index of the scale group holding K row `row` (a shift for power-of-two groups).

@@ -454,7 +454,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     st[6] = static_cast<uint64_t>(n_units);
     st[7] = 0;
   }
-  if (p.peers.world > 1) peer_exchange_finish(p.peers, stored, p.status, kSiteGemvPeers);
+  // only the leaders stored: one fence and one arrival per cluster
+  if (p.peers.world > 1 && rank == 0)
+    peer_exchange_finish(p.peers, stored, p.status, kSiteGemvPeers, gridDim.x / p.split);
 }
 
 CUtensorMapDataType tmap_type16(int dt) {

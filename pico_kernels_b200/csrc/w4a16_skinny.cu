@@ -236,7 +236,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) tmem_dealloc(tmem, C::kTmemCols);
-  if (peers.world > 1) peer_exchange_finish(peers, stored, status, kSiteSkinnyPeers);
+  if (peers.world > 1)
+    peer_exchange_finish(peers, stored, status, kSiteSkinnyPeers, gridDim.x * gridDim.y);
 }
 
 CUtensorMapDataType sk_tmap_type(int dt) {
