@@ -509,6 +509,40 @@ def capture_runner(step_fn, n_sets: int, steps: int, chunk: int = 1000):
     return (graph_for(chunk) if full else None), full, (graph_for(rem) if rem else None)
 
 
+def capture_timed(step_fn, n_sets: int, steps: int, chunk: int, ev0, ev1) -> list:
+    """CUDA graphs covering exactly `steps` steps, replayed in list order, with
+    the start event recorded as the first node of the first graph and the stop
+    event as the last node of the last (events created with external=True):
+    the events then bracket the steps' device time alone, not the launch of
+    the first graph."""
+    chunk = max(1, min(chunk, steps))
+    full, rem = divmod(steps, chunk)
+    counts = [chunk] * full + ([rem] if rem else [])
+    graphs: dict = {}
+
+    def graph(n, first, last):
+        key = (n, first, last)
+        if key not in graphs:
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                step_fn(0)  # lazily created state exists before capture
+                torch.cuda.synchronize()
+                with torch.cuda.graph(g, stream=s):
+                    if first:
+                        ev0.record()
+                    for i in range(n):
+                        step_fn(i % n_sets)
+                    if last:
+                        ev1.record()
+            torch.cuda.current_stream().wait_stream(s)
+            graphs[key] = g
+        return graphs[key]
+
+    return [graph(n, i == 0, i == len(counts) - 1) for i, n in enumerate(counts)]
+
+
 def _replay(runner_out) -> None:
     g, n, grem = runner_out
     for _ in range(n):
@@ -638,20 +672,22 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
 
     warm = capture_runner(work.step, work.n_sets, args.warmup, chunk)
     _replay(warm)
-    timed = capture_runner(work.step, work.n_sets, args.steps, chunk)
-    _prime(timed)  # exactly `steps` GEMMs are timed below, from warm graphs
+    ev0 = torch.cuda.Event(enable_timing=True, external=True)
+    ev1 = torch.cuda.Event(enable_timing=True, external=True)
+    timed = capture_timed(work.step, work.n_sets, args.steps, chunk, ev0, ev1)
+    for g in dict.fromkeys(timed):  # each graph's first launch uploads it: untimed
+        g.replay()
+    torch.cuda.synchronize()
 
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.05)
     barrier(dist)
     torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
     _gate(dist)
-    ev0.record()
-    _replay(timed)
-    ev1.record()
+    for g in timed:  # exactly `steps` GEMMs between the in-graph events
+        g.replay()
     torch.cuda.synchronize()
     t1 = time.perf_counter()
     barrier(dist)
