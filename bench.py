@@ -640,13 +640,14 @@ def phase_leg(work, chunk: int) -> dict:
         return {"median": round(float(x.median()), 3), "max": round(float(x.max()), 3)}
     return {
         "ctas": ctas, "sms": int(st[:, 5].unique().numel()),
-        "gap_after_previous_launch_us": round(float((st[:, 1].min() - prev[:, 4].max()) / 1e3), 3),
+        "gap_after_previous_launch_us": round(float((st[:, 1].min() - prev[:, 7].max()) / 1e3), 3),
         "entry_us": stat(st[:, 0] - t0),
         "wait_released_us": stat(st[:, 1] - t0),
         "first_weights_after_wait_us": stat(st[:, 2] - st[:, 1]),
         "arithmetic_us": stat(st[:, 3] - st[:, 2]),
         "reduction_and_store_us": stat(st[:, 4] - st[:, 3]),
-        "end_us": stat(st[:, 4] - t0),
+        "after_store_to_exit_us": stat(st[:, 7] - st[:, 4]),
+        "end_us": stat(st[:, 7] - t0),
         "note": ("last launch of a 64-step chain; times from its first CTA's entry "
                  "(%globaltimer); the gap runs from the previous launch's last CTA end to "
                  "this launch's dependency wait returning"),

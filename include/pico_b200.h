@@ -224,8 +224,9 @@ PK_API int pk_set_weight_staging(int mode);
  * M = 1 decode GEMVs launched afterwards writes 8 uint64 words at
  * dev_buf[slot * bytes / 16 + 8 * cta]: %globaltimer at entry, after
  * griddepcontrol.wait, when its first weights landed, when its arithmetic
- * ended and when its output was stored, then its SM id, its unit count and
- * a kernel-specific word. `slot` alternates 0, 1 from launch to launch (the
+ * ended and when its output was stored, then its SM id, its unit count (the
+ * stream-K GEMV sets bit 32 in CTAs that summed a slice's partials) and the
+ * time it finished, after the sharded exchange's flag barrier if any. `slot` alternates 0, 1 from launch to launch (the
  * two halves of the buffer), so the last two launches of a chain are both
  * kept. Launches whose grid needs more than `bytes` (grid * 128) record
  * nothing. Kernels captured in a CUDA

@@ -509,10 +509,10 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
     st[3] = t_comp;
     st[4] = globaltimer();
     st[5] = smid;
-    st[6] = static_cast<uint64_t>(n_units);
-    st[7] = was_last ? 1u : 0u;  // this CTA summed a slice's partials
+    st[6] = static_cast<uint64_t>(n_units) | (was_last ? (1ull << 32) : 0ull);  // summed a slice
   }
   if (p.world > 1) sharded_finish(p, stored);
+  if (stamp) p.stamps[static_cast<int64_t>(blockIdx.x) * 8 + 7] = globaltimer();
 }
 
 CUtensorMapDataType tmap_type16(int dt) {

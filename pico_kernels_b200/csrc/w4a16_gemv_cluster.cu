@@ -33,8 +33,8 @@
 //    with fewer instructions per word). Warp w takes rows [64w, 64w + 64) of
 //    every unit (within one scale group); lane l the word of columns
 //    [8(l % 16), 8(l % 16) + 8) in the rows of parity l / 16: one 32-bit word
-//    per row, two rows per warp instruction (128 contiguous bytes). XOR-ing the word with 0x88888888 turns every nibble into
-//    q + 8 (0..15); nibbles 0-5 are then masked in place (one AND each) and
+//    per row, two rows per warp instruction (128 contiguous bytes).
+//    XOR-ing the word with 0x88888888 turns every nibble into q + 8 (0..15); nibbles 0-5 are then masked in place (one AND each) and
 //    nibbles 6-7 after one right shift by 8, each read as an fp32 bit pattern
 //    worth (q + 8) * 16^p * 2^-149 (p = 0..5: subnormal, or the lowest normal
 //    binade, exact). Activations are pre-scaled by 2^S with S = clamp(248 -
@@ -43,7 +43,8 @@
 //    fma.rn.f32x2 per two weights accumulates them. Per unit the +8 offset is
 //    removed with the sum of the scaled activations, 2^(149 - S - 4p) undone
 //    (exact) and the fp32 group scale applied: 1 XOR, 1 shift, 8 AND and 4
-//    FMA2 per 8 weights. The two row parities of a column meet by a shuffle. All shared-memory traffic uses explicit ld/st.shared.
+//    FMA2 per 8 weights. The two row parities of a column meet by a shuffle.
+//    All shared-memory traffic uses explicit ld/st.shared.
 //  * Reduction. The 8 warps' column sums meet in shared memory; each other
 //    CTA of the cluster then pushes its 128 sums into the leader's (rank 0)
 //    shared memory with st.async, which completes bytes on the leader's
@@ -51,9 +52,9 @@
 //    strip's columns in CTA order and stores them: deterministic, no global
 //    workspace, no atomics, and only one CTA per cluster waits or stores
 //    (in the sharded exchange, one system-scope fence per cluster).
-//  * Placement. Launched with the spread cluster scheduling policy, so a
-//    cluster's CTAs go to different SMs (a packed placement put two CTAs of
-//    the grid on some SMs and doubled their time).
+//  * Placement. The launch also asks for the spread cluster scheduling
+//    policy; on its own that did not keep two CTAs off one SM (the shared-
+//    memory footprint does).
 #include "pk_common.cuh"
 
 #include <cstring>
@@ -106,7 +107,7 @@ struct DecodeConsts {
 struct ClusterParams {
   int N, K;
   int split;            // CTAs per strip = cluster size
-  int units;            // units per strip (K / 256)
+  int units;            // units per strip (K / 512)
   int early;            // weights and scales loaded before griddepcontrol.wait
   float scalar_scale;   // per-tensor mode (no group scales)
   int out_dtype;
@@ -452,11 +453,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     st[4] = t_red;
     st[5] = smid;
     st[6] = static_cast<uint64_t>(n_units);
-    st[7] = 0;
+    st[7] = t_red;  // overwritten with the exchange's end below
   }
   // only the leaders stored: one fence and one arrival per cluster
   if (p.peers.world > 1 && rank == 0)
     peer_exchange_finish(p.peers, stored, p.status, kSiteGemvPeers, gridDim.x / p.split);
+  if (stamp) p.stamps[static_cast<int64_t>(blockIdx.x) * 8 + 7] = globaltimer();
 }
 
 CUtensorMapDataType tmap_type16(int dt) {
