@@ -35,12 +35,12 @@
 //    comes after the wait.
 //  * Dequant. Warps 0-7 each take 32 consecutive rows of every unit (inside
 //    one scale group); lane l owns columns [8l, 8l+8) of the slice, one
-//    32-bit word per row (nibble j = column 8l+j). Each nibble n = q & 15 is
-//    moved to bit position 4p (p = 2..5: the word itself for nibbles 2-5,
-//    w << 8 for 0-1, w >> 8 for 6-7) and its sign bit flipped with one LOP3,
-//    (src & (15 << 4p)) ^ (8 << 4p). Read as an fp32 bit pattern below 2^24
-//    that is exactly the number (q + 8) * 16^p * 2^-149 (a subnormal, or the
-//    smallest normal binade). The activations are pre-scaled by 2^S, so one
+//    32-bit word per row (nibble j = column 8l+j), read with explicit
+//    ld.shared. One XOR with 0x88888888 turns every nibble into q + 8;
+//    nibbles 0-5 are masked in place (one AND each, bit position 4p, p =
+//    0..5) and nibbles 6-7 after a right shift by 8 (positions 4, 5). Read as
+//    an fp32 bit pattern below 2^24 that is exactly the number (q + 8) * 16^p
+//    * 2^-149 (a subnormal, or the smallest normal binade). The activations are pre-scaled by 2^S, so one
 //    packed FMA per two weights accumulates a' * (q + 8) * 16^p * 2^-149 with
 //    the product exact and one fp32 rounding, as a plain fp32 dot product
 //    would. At the end of each unit the warp removes the +8 offset with the
@@ -102,12 +102,10 @@ struct GemvCfg {
   static_assert(kSmemBytes <= kSmemTwoPerSm, "two CTAs must fit an SM");
 };
 
-// Bit patterns 8 << 4p for p = 2..5 (the flipped sign bit of a nibble at
-// position p). Passed as kernel parameters so that (w & mask) ^ x compiles to
-// one LOP3: an instruction takes at most one 32-bit immediate, and a
-// constant-bank operand is free.
+// The nibble flip 0x88888888 (every nibble q -> q + 8), as a kernel parameter
+// (a constant-bank operand of the XOR).
 struct DecodeConsts {
-  uint32_t x[4];
+  uint32_t flip;
 };
 
 // fp32 pair helpers (packed f32x2 arithmetic, sm_100)
@@ -314,6 +312,7 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
     if (stamp) t_wait = globaltimer();
     // -8 * 16^p * 2^-149 for the column pairs' positions (2,3) and (4,5): the
     // same bit patterns as the sign flips, negated
+    const uint64_t off01 = pack2(__uint_as_float(0x80000008u), __uint_as_float(0x80000080u));
     const uint64_t off23 = pack2(__uint_as_float(0x80000800u), __uint_as_float(0x80008000u));
     const uint64_t off45 = pack2(__uint_as_float(0x80080000u), __uint_as_float(0x80800000u));
     uint64_t acc[M][4], tot[M][4];
@@ -363,6 +362,7 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
         asum[m] = pack2(t, t);
       }
       // 2^(149 - S - 4p) for the pairs' positions (2,3) and (4,5)
+      const uint64_t pw01 = pack2(exp2i(149 - S), exp2i(145 - S));
       const uint64_t pw23 = pack2(exp2i(141 - S), exp2i(137 - S));
       const uint64_t pw45 = pack2(exp2i(133 - S), exp2i(129 - S));
       uint64_t sc[4];
@@ -382,25 +382,25 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
                            kSiteGemvConsumer))
         failed = true;
 
-      const uint32_t* wrow =
-          reinterpret_cast<const uint32_t*>(base) + warp * kRowsPerWarp * 32 + lane;
+      const uint32_t wrow = smem_u32(base) + (warp * kRowsPerWarp * 32 + lane) * 4;
+      const uint32_t pairs_s = smem_u32(pairs);
 #pragma unroll
       for (int b = 0; b < kRowsPerWarp / 8; ++b) {
         uint32_t wv[8];
 #pragma unroll
-        for (int r = 0; r < 8; ++r) wv[r] = wrow[(b * 8 + r) * 32];
+        for (int r = 0; r < 8; ++r) wv[r] = lds_u32(wrow + (b * 8 + r) * 128);
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
-          const uint32_t w = wv[r];
-          const uint32_t lo = w << 8, hi = w >> 8;
+          const uint32_t w = wv[r] ^ dc.flip;  // every nibble q -> q + 8
+          const uint32_t hi = w >> 8;          // nibbles 6, 7 at positions 4, 5
           uint64_t d[4];
-          d[0] = pack2(__uint_as_float((lo & 0xF00u) ^ dc.x[0]), __uint_as_float((lo & 0xF000u) ^ dc.x[1]));
-          d[1] = pack2(__uint_as_float((w & 0xF00u) ^ dc.x[0]), __uint_as_float((w & 0xF000u) ^ dc.x[1]));
-          d[2] = pack2(__uint_as_float((w & 0xF0000u) ^ dc.x[2]), __uint_as_float((w & 0xF00000u) ^ dc.x[3]));
-          d[3] = pack2(__uint_as_float((hi & 0xF0000u) ^ dc.x[2]), __uint_as_float((hi & 0xF00000u) ^ dc.x[3]));
+          d[0] = pack2(__uint_as_float(w & 0xFu), __uint_as_float(w & 0xF0u));
+          d[1] = pack2(__uint_as_float(w & 0xF00u), __uint_as_float(w & 0xF000u));
+          d[2] = pack2(__uint_as_float(w & 0xF0000u), __uint_as_float(w & 0xF00000u));
+          d[3] = pack2(__uint_as_float(hi & 0xF0000u), __uint_as_float(hi & 0xF00000u));
 #pragma unroll
           for (int m = 0; m < M; ++m) {
-            const uint64_t a2 = pairs[(b * 8 + r) * M + m];
+            const uint64_t a2 = lds_u64(pairs_s + ((b * 8 + r) * M + m) * 8);
 #pragma unroll
             for (int q = 0; q < 4; ++q) acc[m][q] = fma2(d[q], a2, acc[m][q]);
           }
@@ -411,8 +411,10 @@ __global__ void __launch_bounds__(kThreads, GemvCfg<M>::kCtasPerSm)
       for (int m = 0; m < M; ++m)
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const uint64_t c = fma2(q < 2 ? off23 : off45, asum[m], acc[m][q]);
-          tot[m][q] = fma2(mul2(c, q < 2 ? pw23 : pw45), sc[q], tot[m][q]);
+          const uint64_t off = q == 0 ? off01 : (q == 1 ? off23 : off45);
+          const uint64_t pw = q == 0 ? pw01 : (q == 1 ? pw23 : pw45);
+          const uint64_t c = fma2(off, asum[m], acc[m][q]);
+          tot[m][q] = fma2(mul2(c, pw), sc[q], tot[m][q]);
           acc[m][q] = 0ull;
         }
       __syncwarp();
@@ -627,7 +629,7 @@ cudaError_t launch_w4a16_gemv(const DecodeArgs& a, cudaStream_t s, const char** 
     *why = "the split-K GEMV needs a workspace";
     return cudaErrorInvalidValue;
   }
-  const DecodeConsts dc{{0x800u, 0x8000u, 0x80000u, 0x800000u}};
+  const DecodeConsts dc{0x88888888u};
 
   auto launch = [&](auto kernel, int smem_bytes) -> cudaError_t {
     cudaError_t e =
