@@ -45,6 +45,8 @@ L2_BYTES = 126 * 2 ** 20
 WORKLOADS = {
     # HBM-bound decode GEMMs: metric GB/s of algorithmic bytes
     "w4a16_decode_m1": dict(kind="w4a16", M=1, N=4096, K=4096, ncu_traffic=8.71e6),
+    "w4a16_decode_m2": dict(kind="w4a16", M=2, N=4096, K=4096),
+    "w4a16_decode_m3": dict(kind="w4a16", M=3, N=4096, K=4096),
     "w4a16_decode_m4": dict(kind="w4a16", M=4, N=4096, K=4096),
     "w4a16_decode_m16": dict(kind="w4a16", M=16, N=4096, K=4096),
     # tensor-bound prefill GEMM: metric TFLOP/s

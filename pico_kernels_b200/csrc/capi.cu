@@ -657,7 +657,7 @@ int fp8_gemm_impl(const uint8_t* a8, const uint8_t* b8, int64_t M, int64_t N, in
 // Kernel of the fused exchange for a shape, or -1 when none has one: decided
 // from the shape alone (aligned stand-in pointers, lda = K), so that every
 // rank of an N-sharded layer reaches the same answer.
-enum { kPathGemv = 0, kPathDecode = 1, kPathSkinny = 2, kPathPrefill = 3 };
+enum { kPathGemv = 0, kPathDecode = 1, kPathSkinny = 2, kPathPrefill = 3, kPathCluster = 4 };
 // The fused tcgen05 W4A16 prefill: 64-row K stages, scales on 64-row
 // boundaries (the shapes pk_w4a16_gemm sends to it without a workspace).
 bool prefill_shape_ok(int64_t M, int64_t N, int64_t K, int group, bool grouped) {
@@ -673,6 +673,9 @@ constexpr int64_t kPrefillExchangeMaxBytes = int64_t(8) << 20;
 int sharded_path(int64_t M, int64_t N, int64_t K, int group, bool grouped, int out_dtype) {
   const void* aligned = reinterpret_cast<const void*>(256);
   const void* sc = grouped ? aligned : nullptr;
+  if (gemv_cluster_preferred(M, N, K) &&
+      gemv_cluster_supported(M, N, K, group, sc, K, aligned, aligned))
+    return kPathCluster;
   if (gemv_preferred(M, N, K) && gemv_supported(M, N, K, group, sc, K, aligned, aligned))
     return kPathGemv;
   if (decode_supported(M, N, K, group, sc, K, aligned)) return kPathDecode;
@@ -862,7 +865,8 @@ int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t
                 "the fused exchange covers the GEMV, decode and skinny kernels' shapes only");
   const bool aligned16 = (reinterpret_cast<uintptr_t>(wp) & 15) == 0;
   const bool readable =
-      path == kPathGemv     ? gemv_supported(M, N, K, group_size, scales, lda, a, wp)
+      path == kPathCluster  ? gemv_cluster_supported(M, N, K, group_size, scales, lda, a, wp)
+      : path == kPathGemv   ? gemv_supported(M, N, K, group_size, scales, lda, a, wp)
       : path == kPathDecode ? decode_supported(M, N, K, group_size, scales, lda, a)
       : path == kPathSkinny ? skinny_supported(M, N, K, group_size, scales, lda, a) && aligned16
                             : lda % 8 == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
@@ -875,8 +879,7 @@ int pk_w4a16_gemm_sharded(const void* a, int a_dtype, int64_t lda, const uint8_t
                 "with lda a multiple of 8");
   // M = 1 layers that fill one wave run the cluster form, which needs only
   // the completion counter from the workspace
-  const bool cluster = path == kPathGemv && gemv_cluster_preferred(M, N, K) &&
-                       gemv_cluster_supported(M, N, K, group_size, scales, lda, a, wp);
+  const bool cluster = path == kPathCluster;
   int split = 1;
   size_t need = kCounterBytes;
   if (path == kPathGemv && !cluster) {
