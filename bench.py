@@ -48,6 +48,7 @@ WORKLOADS = {
     "w4a16_decode_m2": dict(kind="w4a16", M=2, N=4096, K=4096),
     "w4a16_decode_m3": dict(kind="w4a16", M=3, N=4096, K=4096),
     "w4a16_decode_m4": dict(kind="w4a16", M=4, N=4096, K=4096),
+    "w4a16_decode_m8": dict(kind="w4a16", M=8, N=4096, K=4096),
     "w4a16_decode_m16": dict(kind="w4a16", M=16, N=4096, K=4096),
     # tensor-bound prefill GEMM: metric TFLOP/s
     "w4a16_prefill": dict(kind="w4a16", M=4096, N=11008, K=4096, ncu_traffic=368e6),
@@ -730,7 +731,7 @@ def run_ours(args, wl: dict, world: int, rank: int, local: int) -> None:
             breakdown["step"] = "the local GEMM, then an NCCL all-gather of its output"
         del g_gemm, g_gath
 
-    phases = phase_leg(work, chunk) if args.phases and work.kind == "w4a16" and work.M == 1 else None
+    phases = phase_leg(work, chunk) if args.phases and work.kind == "w4a16" and work.M <= 8 else None
 
     # end to end through the public API, host buffers in and out every step
     e2e_fn, h2d, d2h = work.e2e_step_fn()

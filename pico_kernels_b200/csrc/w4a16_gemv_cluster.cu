@@ -1,7 +1,8 @@
-// W4A16 decode GEMV (M = 1..3) for layers that fit one wave of the SMs, on the
-// CUDA cores, with the K split reduced inside thread-block clusters.
+// W4A16 decode GEMM (M = 1..8) for layers that fit one wave of the SMs: the
+// nibbles are decoded in registers into exact fp16 operands of mma.sync
+// tiles, and the K split is reduced inside thread-block clusters.
 //
-// out[1, N] = A[1, K] @ (q[K, N] * s[K/128, N])  -- gemm_int4.int4_gemm
+// out[M, N] = A[M, K] @ (q[K, N] * s[K/128, N])  -- gemm_int4.int4_gemm
 // (gemm_int4.py:75-92) with group scales, q unpacked from Wp[K, N/2] in the
 // reference's nibble order (gemm_int4.py:43-50, pack_int4_n at :65-72).
 //
@@ -13,53 +14,53 @@
 //  * Partition. The columns are cut into strips of 128 (64 packed bytes per
 //    row); each strip's K rows are split over `split` CTAs (split <= 4),
 //    which form one thread-block cluster. CTA r of a strip owns units
-//    [U*r/split, U*(r+1)/split) of 512 rows (U = K/512). strips * split <=
-//    the SM count, so the grid is one wave of one CTA per SM.
-//  * Footprint. ~145 KB of shared memory (a 4-slot ring), so that no SM
-//    holds two CTAs of one grid: with room for two, CTAs started early by
-//    programmatic dependent launch were packed two to an SM on ~12 SMs, whose
-//    doubled arithmetic then set every launch's critical path. Clusters of 4:
-//    at one CTA per SM a B200 holds 33 of them at once but only 15 clusters
-//    of 8, which left a sixteenth waiting for the first ones to finish.
-//  * Loads. Warp 8 (one thread) is the TMA producer of a 4-slot ring: per
-//    unit four 128-row weight boxes (each with its own mbarrier, so a warp
-//    starts when the box holding its rows lands), the unit's four group-scale
-//    rows, and, on a separate barrier, the unit's 512 activations. Before
-//    griddepcontrol.wait it prefetches the CTA's weights into L2 (a hint that
-//    cannot return stale data); with weight staging on (pk_set_weight_staging)
-//    it loads the first units' weights and scales into shared memory there
-//    instead, and only the activations wait for the previous kernel.
-//  * Arithmetic (the CUDA-core GEMV's exact-product scheme, w4a16_gemv.cu,
-//    with fewer instructions per word). Warp w takes rows [64w, 64w + 64) of
-//    every unit (within one scale group); lane l the word of columns
-//    [8(l % 16), 8(l % 16) + 8) in the rows of parity l / 16: one 32-bit word
-//    per row, two rows per warp instruction (128 contiguous bytes).
-//    XOR-ing the word with 0x88888888 turns every nibble into q + 8 (0..15); nibbles 0-5 are then masked in place (one AND each) and
-//    nibbles 6-7 after one right shift by 8, each read as an fp32 bit pattern
-//    worth (q + 8) * 16^p * 2^-149 (p = 0..5: subnormal, or the lowest normal
-//    binade, exact). Activations are pre-scaled by 2^S with S = clamp(248 -
-//    e_max, 30, 127) over the warp's 64 rows, so every product with a
-//    non-negligible activation is a normal fp32 number and exact; one packed
-//    fma.rn.f32x2 per two weights accumulates them. Per unit the +8 offset is
-//    removed with the sum of the scaled activations, 2^(149 - S - 4p) undone
-//    (exact) and the fp32 group scale applied: 1 XOR, 1 shift, 8 AND and 4
-//    FMA2 per 8 weights. The two row parities of a column meet by a shuffle.
-//    All shared-memory traffic uses explicit ld/st.shared.
-//  * M > 1. The nibble decode is shared by the M activation rows: per 8
-//    weights the XOR, shift and 8 ANDs are done once and 4 FMA2 per row
-//    follow, with S, the +8 offset sum and the group fold per row. Measured
-//    at 4096^2 against the tensor-core decode kernel: M = 2 6.58 vs 8.39 us,
-//    M = 3 7.79 vs 8.49 us, M = 4 9.23 vs 8.49 us (so M <= 3 here).
-//  * Reduction. The 8 warps' column sums meet in shared memory; each other
-//    CTA of the cluster then pushes its 128 sums into the leader's (rank 0)
-//    shared memory with st.async, which completes bytes on the leader's
-//    mbarrier, and exits; the leader waits for them (bounded), sums the
-//    strip's columns in CTA order and stores them: deterministic, no global
-//    workspace, no atomics, and only one CTA per cluster waits or stores
-//    (in the sharded exchange, one system-scope fence per cluster).
+//    [U*r/split, U*(r+1)/split) of 512 rows (U = K/512), at most 4 (the
+//    ring holds them all). strips * split <= the SM count, so the grid is one
+//    wave of one CTA per SM.
+//  * Footprint. More than 116 KB of shared memory, so that no SM holds two
+//    CTAs of one grid: with room for two, CTAs started early by programmatic
+//    dependent launch were packed two to an SM on ~12 SMs, whose doubled
+//    work then set every launch's critical path. Clusters of 4: at one CTA
+//    per SM a B200 holds 33 of them at once but only 15 clusters of 8.
+//  * Loads. Warp 8 (one thread) is the TMA producer: per unit four 128-row
+//    weight boxes (64-byte swizzled; each with its own mbarrier, so a warp
+//    starts when the box holding its rows lands) and the unit's four group-
+//    scale rows. Before griddepcontrol.wait it prefetches the CTA's weights
+//    into L2 (a hint that cannot return stale data); with weight staging on
+//    (pk_set_weight_staging) it loads them into shared memory there instead.
+//    The activations, which the previous kernel may have written, are read
+//    by the mma warps themselves after the wait (L2-coherent loads), so the
+//    wait-to-first-use chain is one load round trip.
+//  * Activations -> B fragments. Each warp converts its rows of every unit
+//    into fp16 mma B fragments once (bf16 rows scaled by 2^S_m per output row
+//    m, so the largest is in [2^14, 2^15): exact; fp16 rows as they are).
+//  * Weights -> A fragments. The tiles are swap-AB: the mma's M dimension is
+//    16 output columns, N the (up to 8) output rows, K 16 weight rows. A lane
+//    loads 8 bytes (16 columns) of 4 rows per k-step; one PRMT puts byte b of
+//    two rows into the two fp16 halves of a word, and one mask-and-flip LOP3
+//    leaves (q + 8) * 2^-24 (low nibble) or (q + 8) * 16 * 2^-24 (high nibble)
+//    in each half: exact subnormal fp16 values. So every product in the fp32
+//    accumulator is exact: 2 PRMT + 4 LOP3 + 1 mma per 8 weights and lane.
+//    The +8 offsets enter each unit's tiles as their starting value: one mma
+//    of the constant -8 * 2^-24 (or -128 * 2^-24) with the activations.
+//  * Fold. Per unit the tiles' sums take the fp32 group scales; at the end
+//    2^24 (2^20 for high nibbles) and 2^-S_m are undone exactly.
+//  * Reduction. The 8 warps' sums meet in shared memory; each other CTA of
+//    the cluster then pushes its sums into the leader's (rank 0) shared
+//    memory with st.async, which completes bytes on the leader's mbarrier,
+//    and exits; the leader waits for them (bounded), sums the strip's columns
+//    in CTA order and stores them: deterministic, no global workspace, no
+//    atomics, and only one CTA per cluster waits or stores (in the sharded
+//    exchange, one system-scope fence per cluster).
 //  * Placement. The launch also asks for the spread cluster scheduling
 //    policy; on its own that did not keep two CTAs off one SM (the shared-
 //    memory footprint does).
+//
+// mma.sync rather than tcgen05: the operands are produced in registers and
+// consumed there; the decode (6 ALU instructions per 8 weights) sets the
+// pace, and the legacy tensor path's rate (measured ~2.3 SM cycles per
+// m16n8k16) keeps up with it. A tcgen05 tile would take its A operand from
+// shared or tensor memory, a store and a barrier per tile more.
 #include "pk_common.cuh"
 
 #include <cstring>
@@ -67,52 +68,43 @@
 #include <type_traits>
 
 #include "pk_internal.h"
+#include "w4a16_mma.cuh"
 
 namespace pk {
 namespace {
 
-constexpr int kRows = 512;              // K rows per unit
-constexpr int kCols = 128;              // columns per strip
-constexpr int kRowBytes = kCols / 2;    // packed bytes per row of a strip (64)
-constexpr int kWarps = 8;               // dequant/FMA warps
+using namespace w4mma;  // units of 512 rows x 128 columns, 8 mma warps, tile decode
+
 constexpr int kProducerWarp = kWarps;
 constexpr int kThreads = (kWarps + 1) * 32;
-constexpr int kRowsPerWarp = kRows / kWarps;  // 64: half a scale group
+constexpr int kMmaThreads = kWarps * 32;
 constexpr int kGroup = 128;
-constexpr int kSub = 4;
-constexpr int kSubRows = kRows / kSub;            // 128
-constexpr int kSubWBytes = kSubRows * kRowBytes;  // 8192
-constexpr int kABox = 256;                        // activations per TMA box (box limit 256)
 constexpr int kMaxSplit = 4;
-constexpr int kStages = 4;
-constexpr int kWBytes = kRows * kRowBytes;              // 32768
+constexpr int kStages = 4;                              // units per CTA, all resident
 constexpr int kSBytes = (kRows / kGroup) * kCols * 2;   // 1024: four 16-bit scale rows
-constexpr int kMaxM = 3;  // M = 4: the tensor-core decode kernel is faster (8.5 vs 9.2 us)
-constexpr int kNumBars = kStages * (kSub + 2) + 1;       // full[kSub], afull, empty per slot; pushed
+constexpr int kNumBars = kStages * kSub + 1;            // full[slot][sub-box]; pushed
 
-// Shared-memory layout for M activation rows.
+// Shared-memory layout for M output rows. The ring's weight boxes are
+// 64-byte swizzled, so slots are 1024-byte aligned (the pattern's period).
 template <int M>
 struct Lay {
-  static constexpr int kABytes = kRows * 2 * M;          // [box][m][256] activations
-  static constexpr int kSlotBytes = kWBytes + kSBytes + kABytes;
+  static constexpr int kSlotBytes = (kWBytes + kSBytes + 1023) / 1024 * 1024;
   static constexpr int kRingBytes = kStages * kSlotBytes;
-  static constexpr int kPairOff = kRingBytes;            // per warp: [64 rows][M] pairs
-  static constexpr int kPairBytes = kWarps * kRowsPerWarp * M * 8;
-  static constexpr int kInOff = kPairOff + kPairBytes;   // leader: [kMaxSplit][M][kCols] sums
+  // B fragments per warp: [unit][k-step] blocks (blk_words<M>() words)
+  static constexpr int kBlkWords = blk_words<M>();
+  static constexpr int kFragOff = kRingBytes;
+  static constexpr int kFragWarpBytes = kStages * kKSteps * kBlkWords * 4;
+  static constexpr int kFragBytes = kWarps * kFragWarpBytes;
+  static constexpr int kInOff = kFragOff + kFragBytes;   // leader: [kMaxSplit][M][kCols] sums
   static constexpr int kInBytes = kMaxSplit * M * kCols * 4;
   static constexpr int kBarOff = kInOff + kInBytes;
-  static constexpr int kSmemBytes = kBarOff + kNumBars * 8 + 128;  // + alignment fix-up
+  static constexpr int kSmemBytes = kBarOff + kNumBars * 8 + 1024;  // + alignment fix-up
   // At the end the ring is free: the cross-warp sums [kWarps][M][kCols] reuse it.
   static constexpr int kRedOff = 0;
   static_assert(kWarps * M * kCols * 4 <= kRingBytes, "reduction buffer fits the ring");
   static_assert(kSmemBytes > 116 * 1024 && kSmemBytes <= 227 * 1024,
                 "one CTA per SM: more than half of the SM's shared memory");
-  static_assert(kSlotBytes % 128 == 0, "slots stay 128-byte aligned");
-};
-
-// The nibble flip as a kernel parameter (a constant-bank operand of the XOR).
-struct DecodeConsts {
-  uint32_t flip;
+  static_assert(kBlkWords % 32 == 8 || kBlkWords % 32 == 24, "k-step blocks on distinct banks");
 };
 
 struct ClusterParams {
@@ -124,61 +116,19 @@ struct ClusterParams {
   int out_dtype;
   int64_t ldo;
   void* out;
+  const uint16_t* a;    // [M][lda] activations
+  int64_t lda;
   OutputShard peers;    // world == 0: unsharded
   int* status;
   uint64_t* stamps;     // optional per-CTA phase times (pk_debug_phase_stamps)
 };
 
-__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ float2 unpack2(uint64_t v) {
-  float2 r;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
-  return r;
-}
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ float exp2i(int e) {
-  return __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
-}
-
-// 16-bit activation at shared address `addr` as fp32.
-template <typename T>
-__device__ __forceinline__ float lds_act(uint32_t addr) {
-  uint16_t h;
-  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(addr));
-  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-    return __uint_as_float(static_cast<uint32_t>(h) << 16);
-  } else {
-    return __half2float(__ushort_as_half(h));
-  }
-}
-
-// Eight 16-bit scales (one uint4) -> four fp32 pairs.
-template <typename T>
-__device__ __forceinline__ void scales8(uint4 raw, uint64_t (&s)[4]) {
-  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-      s[i] = pack2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u));
-    } else {
-      const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
-      const float2 f = __half22float2(h);
-      s[i] = pack2(f.x, f.y);
-    }
-  }
+// A global load cached in L2 only: after griddepcontrol.wait it sees the
+// previous kernel's writes, and no L1 line of this SM can be stale.
+__device__ __forceinline__ uint32_t ldg_cg_u32(const void* p) {
+  uint32_t v;
+  asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void cluster_arrive_relaxed() {
@@ -201,35 +151,29 @@ __device__ __forceinline__ void st_async_f32(uint32_t local, uint32_t bar, uint3
 template <int M, typename T, bool kGrouped>
 __global__ void __launch_bounds__(kThreads, 1)
     w4a16_gemv_cluster_kernel(const __grid_constant__ CUtensorMap tmW,
-                              const __grid_constant__ CUtensorMap tmA,
                               const __grid_constant__ CUtensorMap tmS,
-                              const __grid_constant__ ClusterParams p, const DecodeConsts dc) {
+                              const __grid_constant__ ClusterParams p, const Consts dc) {
   using L = Lay<M>;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
-                                             ~static_cast<uintptr_t>(127));
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = smem_u32(smem);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);  // [slot][sub-box]
-  uint64_t* afull = full + kStages * kSub;                        // [slot]
-  uint64_t* empty = afull + kStages;                              // [slot]
-  uint64_t* pushed = empty + kStages;  // leader: the other CTAs' sums have landed
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);  // [unit][sub-box]
+  uint64_t* pushed = full + kStages * kSub;  // leader: the other CTAs' sums have landed
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int strip = blockIdx.x / p.split;
   const int rank = blockIdx.x % p.split;  // the CTA's rank in its cluster
   const int u0 = p.units * rank / p.split;
-  const int n_units = p.units * (rank + 1) / p.split - u0;
+  const int n_units = p.units * (rank + 1) / p.split - u0;  // <= kStages (host-checked)
   uint64_t t_entry = 0, t_wait = 0, t_first = 0, t_comp = 0, t_red = 0;
   const bool stamp = p.stamps != nullptr && threadIdx.x == 0;
   if (stamp) t_entry = globaltimer();
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      for (int j = 0; j < kSub; ++j) mbar_init(&full[s * kSub + j], 1);
-      mbar_init(&afull[s], 1);
-      mbar_init(&empty[s], kWarps);
-    }
+    for (int j = 0; j < kStages * kSub; ++j) mbar_init(&full[j], 1);
     mbar_init(pushed, 1);
     if (rank == 0 && p.split > 1)
       mbar_arrive_expect_tx(pushed, static_cast<uint32_t>((p.split - 1) * M * kCols * 4));
@@ -244,22 +188,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   griddep_launch_dependents();
 
   bool failed = false;
-  uint64_t tot[M][4];
+  float tot[8][4];  // tile j: columns 16g + 2j ([0], [1]) and + 1 ([2], [3]); rows 2t, 2t + 1
 #pragma unroll
-  for (int m = 0; m < M; ++m)
+  for (int j = 0; j < 8; ++j)
 #pragma unroll
-    for (int q = 0; q < 4; ++q) tot[m][q] = 0ull;
+    for (int e = 0; e < 4; ++e) tot[j][e] = 0.0f;
+  float pw0 = 1.0f, pw1 = 1.0f;  // 2^-S of the lane's tokens 2t, 2t + 1
   if (warp == kProducerWarp) {
     if (lane == 0) {
       tma_prefetch_desc(&tmW);
-      tma_prefetch_desc(&tmA);
       if constexpr (kGrouped) tma_prefetch_desc(&tmS);
-      const uint32_t tx0 = kSubWBytes + (kGrouped ? kSBytes : 0);
-      auto issue_w = [&](int i, int slot) {
+      auto issue_w = [&](int i) {
         const int k0 = (u0 + i) * kRows;
-        uint8_t* base = smem + slot * L::kSlotBytes;
-        uint64_t* fb = &full[slot * kSub];
-        mbar_arrive_expect_tx(&fb[0], tx0);
+        uint8_t* base = smem + i * L::kSlotBytes;
+        uint64_t* fb = &full[i * kSub];
+        mbar_arrive_expect_tx(&fb[0], kSubWBytes + (kGrouped ? kSBytes : 0));
         tma_load_2d(base, &tmW, &fb[0], strip * kRowBytes, k0);
         if constexpr (kGrouped) tma_load_2d(base + kWBytes, &tmS, &fb[0], strip * kCols, k0 / kGroup);
         for (int j = 1; j < kSub; ++j) {
@@ -267,231 +210,127 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(base + j * kSubWBytes, &tmW, &fb[j], strip * kRowBytes, k0 + j * kSubRows);
         }
       };
-      auto issue_a = [&](int i, int slot) {
-        mbar_arrive_expect_tx(&afull[slot], L::kABytes);
-        for (int h = 0; h < kRows / kABox; ++h)  // box h: [m][256] activations
-          tma_load_2d(smem + slot * L::kSlotBytes + kWBytes + kSBytes + h * M * kABox * 2, &tmA,
-                      &afull[slot], (u0 + i) * kRows + h * kABox, 0);
-      };
-      const int pre = n_units < kStages ? n_units : kStages;
       if (p.early) {
-        for (int i = 0; i < pre; ++i) issue_w(i, i);
+        for (int i = 0; i < n_units; ++i) issue_w(i);
+      } else {
+        // into L2 while the previous kernel runs: L2 is coherent, so a line
+        // that kernel is still writing cannot come back stale
+        for (int i = 0; i < n_units; ++i) {
+          const int k0 = (u0 + i) * kRows;
+          for (int j = 0; j < kSub; ++j)
+            tma_prefetch_l2_2d(&tmW, strip * kRowBytes, k0 + j * kSubRows);
+          if constexpr (kGrouped) tma_prefetch_l2_2d(&tmS, strip * kCols, k0 / kGroup);
+        }
       }
-      // the rest of the CTA's weights (all of them without staging) into L2,
-      // and the activations of the first units: L2 is coherent, so a line the
-      // previous kernel is still writing cannot come back stale
-      for (int i = p.early ? pre : 0; i < n_units && i < pre + 4 * kStages; ++i) {
-        const int k0 = (u0 + i) * kRows;
-        for (int j = 0; j < kSub; ++j) tma_prefetch_l2_2d(&tmW, strip * kRowBytes, k0 + j * kSubRows);
-        if constexpr (kGrouped) tma_prefetch_l2_2d(&tmS, strip * kCols, k0 / kGroup);
-      }
-      for (int i = 0; i < pre; ++i)
-        for (int h = 0; h < kRows / kABox; ++h)
-          tma_prefetch_l2_2d(&tmA, (u0 + i) * kRows + h * kABox, 0);
       griddep_wait();
       if (!p.early) {
-        for (int i = 0; i < pre; ++i) issue_w(i, i);
-      }
-      for (int i = 0; i < pre; ++i) issue_a(i, i);
-      int issued = pre;
-      bool ok = true;
-      for (int i = pre, slot = pre % kStages, round = pre / kStages; i < n_units; ++i) {
-        if (!mbar_wait(&empty[slot], (round - 1) & 1, p.status, kSiteGemvProducer)) {
-          ok = false;
-          break;
-        }
-        issue_w(i, slot);
-        issue_a(i, slot);
-        issued = i + 1;
-        if (++slot == kStages) slot = 0, ++round;
-      }
-      if (!ok) {
-        // let copies already issued land before the CTA's shared memory is released
-        const int first = issued > kStages ? issued - kStages : 0;
-        for (int i = first; i < issued; ++i) {
-          for (int j = 0; j < kSub; ++j)
-            mbar_wait(&full[(i % kStages) * kSub + j], (i / kStages) & 1, nullptr, 0);
-          mbar_wait(&afull[i % kStages], (i / kStages) & 1, nullptr, 0);
-        }
+        for (int i = 0; i < n_units; ++i) issue_w(i);
       }
     }
     __syncwarp();
   } else {
-    // ---------------- dequant / FMA warps ----------------
+    // ---------------- mma warps ----------------
     griddep_wait();
     if (stamp) t_wait = globaltimer();
-    // -8 * 16^p * 2^-149 for the column pairs' positions (0,1), (2,3), (4,5)
-    const uint64_t off01 = pack2(__uint_as_float(0x80000008u), __uint_as_float(0x80000080u));
-    const uint64_t off23 = pack2(__uint_as_float(0x80000800u), __uint_as_float(0x80008000u));
-    const uint64_t off45 = pack2(__uint_as_float(0x80080000u), __uint_as_float(0x80800000u));
-    const uint32_t pairs = sbase + L::kPairOff + warp * kRowsPerWarp * M * 8;
-    constexpr int kWarpsPerSub = kSubRows / kRowsPerWarp;  // 2
-    for (int i = 0, slot = 0, round = 0; i < n_units; ++i) {
-      const uint32_t base = sbase + slot * L::kSlotBytes;
-      if (!failed && !mbar_wait_sleep(&afull[slot], round & 1, p.status, kSiteGemvConsumer))
-        failed = true;
-      // Activations ([box of 256 rows][m][256] in the slot): lane l scales rows
-      // 64w + l and 64w + 32 + l of every output row m; S_m = clamp(248 -
-      // e_max, 30, 127) from the largest exponent among the warp's 64 rows.
-      // A lane walks the rows of one parity (lane / 16): the sum of the scaled
-      // activations of that parity removes its +8 offsets. Rows 64w + l and
-      // 64w + 32 + l have the parity of l, so sum over lanes of equal l % 2.
-      uint64_t asum[M], pw01[M], pw23[M], pw45[M];
-      {
-        const int r0 = warp * kRowsPerWarp;  // the warp's 64 rows lie in one box
-        const uint32_t abase =
-            base + kWBytes + kSBytes + (r0 / kABox) * M * kABox * 2 + (r0 % kABox) * 2;
+    const LaneMap lm = lane_map(lane);
+    const uint32_t frag = sbase + L::kFragOff + warp * L::kFragWarpBytes;
+    constexpr uint32_t kUnitFragBytes = kKSteps * L::kBlkWords * 4;
+    // Activations of every unit -> fp16 B fragments, with one scale 2^S_m per
+    // output row over the warp's rows of all its units (bf16; fp16 as is).
+    {
+      const int rho = warp * kRowsPerWarp + 2 * lane;
+      const uint8_t* a_lane = reinterpret_cast<const uint8_t*>(p.a) +
+                              (static_cast<int64_t>(u0) * kRows + rho) * 2;
+      uint32_t raw[M][kStages];
 #pragma unroll
-        for (int m = 0; m < M; ++m) {
-          const float av0 = lds_act<T>(abase + (m * kABox + lane) * 2);
-          const float av1 = lds_act<T>(abase + (m * kABox + 32 + lane) * 2);
-          uint32_t emax = (__float_as_uint(av0) >> 23) & 0xFFu;
-          const uint32_t e1 = (__float_as_uint(av1) >> 23) & 0xFFu;
-          emax = __reduce_max_sync(0xffffffffu, emax > e1 ? emax : e1);
-          int S = 248 - static_cast<int>(emax);
-          S = S < 30 ? 30 : (S > 127 ? 127 : S);
-          const float as0 = av0 * exp2i(S), as1 = av1 * exp2i(S);
-          sts_u64(pairs + (lane * M + m) * 8, pack2(as0, as0));
-          sts_u64(pairs + ((32 + lane) * M + m) * 8, pack2(as1, as1));
-          float t = as0 + as1;
+      for (int m = 0; m < M; ++m)
 #pragma unroll
-          for (int o = 16; o > 1; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-          t = __shfl_sync(0xffffffffu, t, lane >> 4);
-          asum[m] = pack2(t, t);
-          // 2^(149 - S - 4p) for the pairs' positions (0,1), (2,3) and (4,5)
-          pw01[m] = pack2(exp2i(149 - S), exp2i(145 - S));
-          pw23[m] = pack2(exp2i(141 - S), exp2i(137 - S));
-          pw45[m] = pack2(exp2i(133 - S), exp2i(129 - S));
+        for (int i = 0; i < kStages; ++i)
+          raw[m][i] = i < n_units ? ldg_cg_u32(a_lane + (m * p.lda + i * kRows) * 2) : 0u;
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        int S = 0;
+        if constexpr (kBf16) {
+          uint32_t emax = 0;
+#pragma unroll
+          for (int i = 0; i < kStages; ++i) emax = max(emax, bf16x2_emax(raw[m][i]));
+          S = scale_exp(__reduce_max_sync(0xffffffffu, emax));
         }
+        if (m == 2 * lm.t) pw0 = exp2i(-S);
+        if (m == 2 * lm.t + 1) pw1 = exp2i(-S);
+        const float sc = exp2i(S);
+#pragma unroll
+        for (int i = 0; i < kStages; ++i)
+          if (i < n_units)
+            sts_u32(frag + i * kUnitFragBytes + bfrag_store_off<M>(lane, m),
+                    to_f16x2<T>(raw[m][i], sc));
       }
+    }
+    __syncwarp();
+    const uint32_t bfrag = frag + ((lm.g < M ? lm.g : M - 1) * 4 + lm.t) * 8;
+    for (int i = 0; i < n_units; ++i) {
+      const uint32_t base = sbase + i * L::kSlotBytes;
       // sub-box 0 carries the unit's scales; the warp's rows are in sub-box w/2
-      if (!failed && !mbar_wait_sleep(&full[slot * kSub], round & 1, p.status, kSiteGemvConsumer))
+      if (!failed && !mbar_wait_sleep(&full[i * kSub], 0, p.status, kSiteGemvConsumer))
         failed = true;
-      if (warp >= kWarpsPerSub && !failed &&
-          !mbar_wait_sleep(&full[slot * kSub + warp / kWarpsPerSub], round & 1, p.status,
-                           kSiteGemvConsumer))
+      if (warp >= 2 && !failed &&
+          !mbar_wait_sleep(&full[i * kSub + warp / 2], 0, p.status, kSiteGemvConsumer))
         failed = true;
       if (stamp && i == 0) t_first = globaltimer();
-      uint64_t sc[4];
-      if constexpr (kGrouped) {
-        const int srow = (warp * kRowsPerWarp) / kGroup;
-        scales8<T>(lds_v4(base + kWBytes + srow * kCols * 2 + (lane & 15) * 16), sc);
-      } else {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) sc[q] = pack2(p.scalar_scale, p.scalar_scale);
-      }
-      __syncwarp();
-
-      // lane l: word l % 16 (columns 8(l%16) .. +8) of rows 64w + 2i + l / 16
-      uint64_t acc[M][4];
-#pragma unroll
-      for (int m = 0; m < M; ++m)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) acc[m][q] = 0ull;
-      const uint32_t wrow =
-          base + (warp * kRowsPerWarp + (lane >> 4)) * kRowBytes + (lane & 15) * 4;
-      const uint32_t prow = pairs + (lane >> 4) * M * 8;
-      constexpr int kBatch = M == 1 ? 8 : 4;  // rows in flight per lane
-#pragma unroll
-      for (int b = 0; b < kRowsPerWarp / 2 / kBatch; ++b) {
-        uint32_t wv[kBatch];
-        uint64_t a2[kBatch][M];
-#pragma unroll
-        for (int r = 0; r < kBatch; ++r) wv[r] = lds_u32(wrow + (b * kBatch + r) * 2 * kRowBytes);
-#pragma unroll
-        for (int r = 0; r < kBatch; ++r)
-#pragma unroll
-          for (int m = 0; m < M; ++m) a2[r][m] = lds_u64(prow + ((b * kBatch + r) * 2 * M + m) * 8);
-#pragma unroll
-        for (int r = 0; r < kBatch; ++r) {
-          const uint32_t w = wv[r] ^ dc.flip;  // every nibble q -> q + 8
-          const uint32_t hi = w >> 8;          // nibbles 6, 7 at positions 4, 5
-          uint64_t d[4];
-          d[0] = pack2(__uint_as_float(w & 0xFu), __uint_as_float(w & 0xF0u));
-          d[1] = pack2(__uint_as_float(w & 0xF00u), __uint_as_float(w & 0xF000u));
-          d[2] = pack2(__uint_as_float(w & 0xF0000u), __uint_as_float(w & 0xF00000u));
-          d[3] = pack2(__uint_as_float(hi & 0xF0000u), __uint_as_float(hi & 0xF00000u));
-#pragma unroll
-          for (int m = 0; m < M; ++m)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) acc[m][q] = fma2(d[q], a2[r][m], acc[m][q]);
-        }
-      }
-      // fold the unit: remove the +8 offset, undo 2^S * 16^p, apply the scale
-#pragma unroll
-      for (int m = 0; m < M; ++m)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint64_t off = q == 0 ? off01 : (q == 1 ? off23 : off45);
-          const uint64_t pw = q == 0 ? pw01[m] : (q == 1 ? pw23[m] : pw45[m]);
-          const uint64_t c = fma2(off, asum[m], acc[m][q]);
-          tot[m][q] = fma2(mul2(c, pw), sc[q], tot[m][q]);
-        }
-      __syncwarp();  // every lane is done with the slot and the pairs
-      if (lane == 0) mbar_arrive(&empty[slot]);
-      if (++slot == kStages) slot = 0, ++round;
+      unit<M, T, kGrouped, false>(
+          lm, base + warp * kRowsPerWarp * kRowBytes, bfrag + i * kUnitFragBytes,
+          base + kWBytes + ((warp * kRowsPerWarp) / kGroup) * kCols * 2 + lm.g * 32,
+          p.scalar_scale, 1.0f, 1.0f, dc, tot);
     }
   }
   if (stamp) t_comp = globaltimer();
 
   // ---------------- reduction: warps, then the cluster ----------------
   failed = __syncthreads_or(failed) != 0;  // every warp is done with the ring
-  if (warp < kWarps) {
-    // lanes l and l + 16 hold the two row parities of the same columns
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-      float2 v[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        v[q] = unpack2(tot[m][q]);
-        v[q].x += __shfl_xor_sync(0xffffffffu, v[q].x, 16);
-        v[q].y += __shfl_xor_sync(0xffffffffu, v[q].y, 16);
-      }
-      if (lane < 16) {
-        const uint32_t dst = sbase + L::kRedOff + ((warp * M + m) * kCols + lane * 8) * 4;
-        sts_v4f(dst, v[0].x, v[0].y, v[1].x, v[1].y);
-        sts_v4f(dst + 16, v[2].x, v[2].y, v[3].x, v[3].y);
-      }
-    }
-  }
+  constexpr int kOut = M * kCols;          // sums per CTA: [m][column]
+  if (warp < kWarps)
+    store_sums<M>(sbase + L::kRedOff + warp * kOut * 4, lane_map(lane), tot, pw0, pw1);
   __syncthreads();
-  // thread t < 128 owns column t of the strip, for every output row m
-  float colsum[M];
+  // thread x < 256 owns sums x, x + 256, ... of the CTA's [m][column]
+  constexpr int kPer = (kOut + kMmaThreads - 1) / kMmaThreads;
+  float colsum[kPer];
 #pragma unroll
-  for (int m = 0; m < M; ++m) {
-    colsum[m] = 0.0f;
-    if (threadIdx.x < kCols) {
+  for (int k = 0; k < kPer; ++k) {
+    const int o = threadIdx.x + k * kMmaThreads;
+    colsum[k] = 0.0f;
+    if (threadIdx.x < kMmaThreads && o < kOut) {
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w)
-        colsum[m] += lds_f32(sbase + L::kRedOff + ((w * M + m) * kCols + threadIdx.x) * 4);
+      for (int w = 0; w < kWarps; ++w) colsum[k] += lds_f32(sbase + L::kRedOff + (w * kOut + o) * 4);
     }
   }
   if (p.split > 1) cluster_wait_acquire();  // the leader's barrier is initialised
   bool stored = false;
-  const uint32_t in_base = sbase + L::kInOff;  // [rank][m][kCols]
+  const uint32_t in_base = sbase + L::kInOff;  // [rank][m][column]
   if (rank != 0) {
-    // push this CTA's column sums into slot `rank` of the leader's buffer
-    if (threadIdx.x < kCols) {
+    // push this CTA's sums into slot `rank` of the leader's buffer
 #pragma unroll
-      for (int m = 0; m < M; ++m)
-        st_async_f32(in_base + ((rank * M + m) * kCols + threadIdx.x) * 4, smem_u32(pushed), 0u,
-                     colsum[m]);
+    for (int k = 0; k < kPer; ++k) {
+      const int o = threadIdx.x + k * kMmaThreads;
+      if (threadIdx.x < kMmaThreads && o < kOut)
+        st_async_f32(in_base + (rank * kOut + o) * 4, smem_u32(pushed), 0u, colsum[k]);
     }
   } else {
     if (p.split > 1 &&
         !mbar_wait(pushed, 0, p.status, kSiteGemvConsumer))  // the others' sums have landed
       failed = true;
     failed = __syncthreads_or(failed) != 0;
-    if (!failed && threadIdx.x < kCols) {
+    if (!failed) {
 #pragma unroll
-      for (int m = 0; m < M; ++m) {
-        float v = colsum[m];  // in CTA order: rank 0 first, then ranks 1 .. split-1
-        for (int j = 1; j < p.split; ++j)
-          v += lds_f32(in_base + ((j * M + m) * kCols + threadIdx.x) * 4);
-        emit_out(p.out, p.peers, p.out_dtype,
-                 m * p.ldo + static_cast<int64_t>(strip) * kCols + threadIdx.x, v);
+      for (int k = 0; k < kPer; ++k) {
+        const int o = threadIdx.x + k * kMmaThreads;
+        if (threadIdx.x < kMmaThreads && o < kOut) {
+          float v = colsum[k];  // in CTA order: rank 0 first, then ranks 1 .. split-1
+          for (int j = 1; j < p.split; ++j) v += lds_f32(in_base + (j * kOut + o) * 4);
+          emit_out(p.out, p.peers, p.out_dtype,
+                   (o / kCols) * p.ldo + static_cast<int64_t>(strip) * kCols + o % kCols, v);
+          stored = true;
+        }
       }
-      stored = true;
     }
   }
   if (stamp) {
@@ -519,7 +358,7 @@ CUtensorMapDataType tmap_type16(int dt) {
 }
 
 // Whether clusters of `split` CTAs of this kernel can be resident (per
-// device and split; 0 unknown, 1 yes, 2 no).
+// device, row count and split; 0 unknown, 1 yes, 2 no).
 template <typename Kern>
 bool cluster_fits(Kern kernel, int split, int smem_bytes, int m) {
   static int cache[64][kMaxM + 1][kMaxSplit + 1] = {};
@@ -584,7 +423,8 @@ bool gemv_cluster_supported(int64_t M, int64_t N, int64_t K, int group, const vo
   if (M < 1 || M > kMaxM) return false;
   if (N % kCols != 0 || K % kRows != 0 || N <= 0 || K <= 0) return false;
   if (N > (1ll << 30) || K > (1ll << 30)) return false;
-  if (gemv_cluster_split(N, K) < 1) return false;
+  const int split = gemv_cluster_split(N, K);
+  if (split < 1 || (K / kRows + split - 1) / split > kStages) return false;  // all units resident
   if (lda % 8 != 0 || (reinterpret_cast<uintptr_t>(a) & 15) != 0) return false;
   if ((reinterpret_cast<uintptr_t>(wp) & 15) != 0) return false;
   if (scales != nullptr && (group != kGroup || (reinterpret_cast<uintptr_t>(scales) & 15) != 0))
@@ -605,13 +445,14 @@ bool gemv_cluster_preferred(int64_t M, int64_t N, int64_t K) {
 
 cudaError_t launch_w4a16_gemv_cluster(const DecodeArgs& a, cudaStream_t s, const char** why,
                                       const OutputShard* shard) {
-  CUtensorMap tmW, tmA, tmS;
+  if (!gemv_cluster_supported(a.M, a.N, a.K, a.group, a.scales, a.lda, a.a, a.wp)) {
+    *why = "cluster GEMV: unsupported shape or alignment";
+    return cudaErrorInvalidValue;
+  }
+  CUtensorMap tmW, tmS;
   const CUtensorMapDataType dt = tmap_type16(a.a_dtype);
   if (!encode_tmap_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.wp, a.N / 2, a.K, a.N / 2, kRowBytes,
-                      kSubRows, CU_TENSOR_MAP_SWIZZLE_NONE, why))
-    return cudaErrorInvalidValue;
-  if (!encode_tmap_2d(&tmA, dt, a.a, a.K, a.M, a.lda * 2, kABox, static_cast<uint32_t>(a.M),
-                      CU_TENSOR_MAP_SWIZZLE_NONE, why))
+                      kSubRows, CU_TENSOR_MAP_SWIZZLE_64B, why))
     return cudaErrorInvalidValue;
   const bool grouped = a.scales != nullptr;
   if (grouped) {
@@ -631,6 +472,8 @@ cudaError_t launch_w4a16_gemv_cluster(const DecodeArgs& a, cudaStream_t s, const
   p.out_dtype = a.out_dtype;
   p.ldo = a.ldo;
   p.out = a.out;
+  p.a = static_cast<const uint16_t*>(a.a);
+  p.lda = a.lda;
   p.status = a.status;
   const int64_t grid = (a.N / kCols) * p.split;
   p.stamps = phase_stamps(static_cast<size_t>(grid));
@@ -641,7 +484,7 @@ cudaError_t launch_w4a16_gemv_cluster(const DecodeArgs& a, cudaStream_t s, const
     }
     p.peers = *shard;
   }
-  const DecodeConsts dc{0x88888888u};
+  const Consts dc = consts();
 
   auto launch = [&](auto kernel, int smem_bytes) -> cudaError_t {
     cudaError_t e = set_max_smem(reinterpret_cast<const void*>(kernel), smem_bytes);
@@ -666,7 +509,7 @@ cudaError_t launch_w4a16_gemv_cluster(const DecodeArgs& a, cudaStream_t s, const
     attrs[2].val.clusterSchedulingPolicyPreference = cudaClusterSchedulingPolicySpread;
     cfg.attrs = attrs;
     cfg.numAttrs = 3;
-    return cudaLaunchKernelEx(&cfg, kernel, tmW, tmA, tmS, p, dc);
+    return cudaLaunchKernelEx(&cfg, kernel, tmW, tmS, p, dc);
   };
   auto by_m = [&](auto mtag) -> cudaError_t {
     constexpr int kM = decltype(mtag)::value;
@@ -680,7 +523,12 @@ cudaError_t launch_w4a16_gemv_cluster(const DecodeArgs& a, cudaStream_t s, const
   switch (a.M) {
     case 1: return by_m(std::integral_constant<int, 1>{});
     case 2: return by_m(std::integral_constant<int, 2>{});
-    default: return by_m(std::integral_constant<int, 3>{});
+    case 3: return by_m(std::integral_constant<int, 3>{});
+    case 4: return by_m(std::integral_constant<int, 4>{});
+    case 5: return by_m(std::integral_constant<int, 5>{});
+    case 6: return by_m(std::integral_constant<int, 6>{});
+    case 7: return by_m(std::integral_constant<int, 7>{});
+    default: return by_m(std::integral_constant<int, 8>{});
   }
 }
 

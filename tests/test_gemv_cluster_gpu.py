@@ -1,9 +1,10 @@
-"""GPU parity of the cluster form of the W4A16 GEMV (M = 1..3 on small layers:
-one wave of one CTA per SM).
+"""GPU parity of the cluster form of the W4A16 GEMV (M = 1..8 on small layers:
+one wave of one CTA per SM, mma.sync tiles of exactly decoded fp16 operands).
 
-Same arithmetic as the stream-K GEMV (exact integer codes times fp32-scaled
-activations, fp32 group scale on the group sum), so the same tight bounds
-against the oracle's fp32 dequantize-then-matmul: rel-Frobenius <= 1e-5 and
+Every product is exact (weights as (q + 8) * 2^-24 fp16 subnormals, bf16
+activations scaled into fp16 per output row by 2^S_m, fp32 accumulators), the
++8 offsets and group scales are folded per 512-row unit, so the bounds against
+the oracle's fp32 dequantize-then-matmul are tight: rel-Frobenius <= 1e-5 and
 max-abs <= 1e-4 * max|Y|. The K split is reduced in CTA order inside each
 cluster, so results are bitwise reproducible, with and without weight staging
 (which changes only when the weights are loaded). The phase stamps the kernel
@@ -74,7 +75,9 @@ def _staging(mode):
 
 
 CASES = [(1, 4096, 4096), (1, 8192, 2048), (1, 5120, 4096), (1, 4608, 2048), (1, 3584, 8192),
-         (2, 4096, 4096), (2, 8192, 2048), (3, 5120, 4096), (3, 4096, 4096), (3, 3584, 8192)]
+         (2, 4096, 4096), (2, 8192, 2048), (3, 5120, 4096), (3, 4096, 4096), (3, 3584, 8192),
+         (4, 4096, 4096), (5, 8192, 2048), (6, 4608, 2048), (7, 3584, 8192), (8, 4096, 4096),
+         (8, 5120, 4096)]
 
 
 @pytest.mark.parametrize("M,N,K", CASES)
@@ -95,10 +98,10 @@ def test_cluster_gemv_vs_oracle(M, N, K, dt):
     assert pk.device_status() == (0, 0)
 
 
-def test_four_rows_take_the_tensor_core_decode():
-    # M = 4 at 4096^2: the tensor-core decode kernel (8.5 us) beats this one
-    # (9.2 us), so no GEMV stamps are written; the result still matches
-    a, packed, scales, ref = make_case(4, 4096, 4096, seed=11)
+def test_nine_rows_take_the_tcgen05_decode():
+    # M = 9 is past the mma's n8 block: the tcgen05 decode kernel runs (no
+    # GEMV stamps) and the result still matches at its bf16 tolerance
+    a, packed, scales, ref = make_case(9, 4096, 4096, seed=11)
     with Stamps() as st:
         y = pk.int4_gemm(a, packed, scales)
         torch.cuda.synchronize()
@@ -106,6 +109,33 @@ def test_four_rows_take_the_tensor_core_decode():
     r = torch.from_numpy(ref).to(y.device)
     rel = (torch.norm(y.float() - r) / torch.norm(r)).item()
     assert rel <= 1e-2, rel
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_rows_far_apart_in_magnitude(dt):
+    # each output row has its own activation scale 2^S_m in the tensor-core
+    # form: rows 2^-40 / 2^40 apart (bf16; fp16: 2^-12 / 2^3, within its
+    # range), an all-zero row and subnormal activations each keep the tight
+    # bound on their own
+    M, N, K = 5, 4096, 4096
+    a, packed, scales, _ = make_case(M, N, K, dt, seed=21)
+    af = a.float()
+    lo, hi = (2.0 ** -40, 2.0 ** 40) if dt == torch.bfloat16 else (2.0 ** -12, 2.0 ** 3)
+    af[0] *= lo
+    af[1] *= hi
+    af[2] = 0.0
+    af[3] *= 2.0 ** -130 if dt == torch.bfloat16 else 2.0 ** -16
+    a = af.to(dt)
+    y = pk.int4_gemm(a, packed, scales).float().cpu()
+    w = (pk.unpack_int4_n(packed).float() * scales.float().repeat_interleave(128, 0)).cpu()
+    ref = a.float().cpu().double() @ w.double()
+    for m in range(M):
+        r = ref[m]
+        if m == 2:
+            assert torch.equal(y[m], torch.zeros_like(y[m]))
+            continue
+        rel = (torch.norm(y[m].double() - r) / torch.norm(r)).item()
+        assert rel <= 1e-5, (m, rel)
 
 
 @pytest.mark.parametrize("mode", [0, 1])
