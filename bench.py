@@ -63,6 +63,8 @@ WORKLOADS = {
     # Llama-70B MLP layers sharded along N over the ranks, output all-gathered
     # with NCCL; strong scaling: the layer is fixed, ranks split it
     "llama70b_up_m1": dict(kind="w4a16", M=1, N=28672, K=8192, sharded=True),
+    "llama70b_up_m4": dict(kind="w4a16", M=4, N=28672, K=8192, sharded=True),
+    "llama70b_up_m8": dict(kind="w4a16", M=8, N=28672, K=8192, sharded=True),
     "llama70b_up_m32": dict(kind="w4a16", M=32, N=28672, K=8192, sharded=True),
     "llama70b_up_m256": dict(kind="w4a16", M=256, N=28672, K=8192, sharded=True,
                              ncu_traffic=129.6e6),

@@ -52,7 +52,7 @@ constexpr int kMaxM = 8;                      // one n8 block of the tile
 // 2(4g + t), +1 for g < M; padded so that the four k-step blocks of a unit
 // start on different banks (8M + pad = 8 or 24 mod 32).
 template <int M>
-constexpr int blk_words() {
+__host__ __device__ constexpr int blk_words() {
   return 8 * M + (M % 2 == 0 ? 8 : 0);
 }
 

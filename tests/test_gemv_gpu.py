@@ -50,15 +50,22 @@ def test_gemv_decode(M, N, dt):
 
 
 @pytest.mark.parametrize("M,N,K,group", [
-    (1, 4128, 4096, 128),    # last 256-column slice ragged (32 columns)
-    (1, 1024, 4160, 64),     # K not a multiple of 128, group 64 (four scale rows per unit)
+    (1, 4128, 4096, 128),    # last 128-column slice ragged (32 columns)
+    (1, 1024, 4160, 64),     # K not a multiple of 128, group 64 (eight scale rows per unit)
     (2, 8192, 4160, 64),     # M = 2
-    (1, 2048, 4100, 128),    # K not a multiple of the 256-row unit
+    (1, 2048, 4100, 128),    # K not a multiple of the 512-row unit
     (1, 512, 8192, 256),     # group 256
-    (1, 1024, 4224, 192),    # groups straddle the 256-row units
-    (1, 256, 163840, 128),   # stream-K: one slice split over every CTA (fan-in ~300)
+    (1, 1024, 4224, 192),    # groups straddle the 512-row units
+    (1, 256, 163840, 128),   # stream-K: one slice split over every CTA (fan-in ~150)
     (2, 65536, 512, 128),    # stream-K, M = 2: CTA ranges span several slices
-    (1, 8192, 256, 64),      # one unit per slice: every segment a whole slice, no reduction
+    (1, 8192, 256, 64),      # one partial unit per slice: every segment a whole slice
+    (3, 4128, 4096, 128),    # M = 3..8: the n8 block of the tiles
+    (4, 28672, 2048, 128),
+    (5, 1024, 4224, 192),
+    (6, 2048, 4100, 128),
+    (7, 65536, 512, 128),
+    (8, 8192, 4160, 64),
+    (8, 256, 163840, 128),
 ])
 def test_gemv_shapes(M, N, K, group):
     a, packed, scales, ref = make_case(M, N, K, group=group, seed=N + K)
@@ -67,9 +74,9 @@ def test_gemv_shapes(M, N, K, group):
 
 
 def test_gemv_llama70b_shapes():
-    for (N, K) in ((28672, 8192), (8192, 28672)):
-        a, packed, scales, ref = make_case(1, N, K, seed=7)
-        check_tight(pk.int4_gemm(a, packed, scales), ref, f"N={N} K={K}")
+    for (M, N, K) in ((1, 28672, 8192), (1, 8192, 28672), (8, 28672, 8192)):
+        a, packed, scales, ref = make_case(M, N, K, seed=7)
+        check_tight(pk.int4_gemm(a, packed, scales), ref, f"M={M} N={N} K={K}")
 
 
 def test_gemv_deterministic_and_bf16_out():
