@@ -25,21 +25,24 @@
 //    stores, and re-arms the counter. Fixed summation order: deterministic
 //    for a given SM count.
 //  * Pipeline. Warp 8 (one thread) is the TMA producer of a ring of as many
-//    unit slots as shared memory holds (six, 210 KB): per unit the
+//    unit slots as shared memory holds (six, ~220 KB): per unit the
 //    activation tile A[0:M, k0:k0+64] and the unit's group-scale row (one
 //    mbarrier), then the eight warps' weight boxes (one mbarrier each).
+//    Warp 9 turns each unit's activations into the B fragments the eight mma
+//    warps share (one mbarrier), so their loop is the tile decode alone.
 //    Before griddepcontrol.wait it only prefetches weights and scales into
 //    L2 (a hint that cannot return stale data), so with programmatic
 //    dependent launch the DRAM fetch overlaps the previous kernel's tail;
 //    every load into shared memory and every global write comes after the
 //    wait. Rows past K and columns past N arrive as zeros (TMA bounds fill).
-//  * Arithmetic. Per unit each warp converts the 64 activation rows into its
-//    fp16 B fragments, bf16 rows scaled by 2^S_m per output row m (S from the
-//    unit's 64 rows, so the largest magnitude lies in [2^14, 2^15)), runs the
-//    tile decode and folds the tiles' fp32 sums with the group scale (the
-//    unit lies in one group: groups are multiples of 64) times 2^-S_m. The
-//    result is the reference's fp32 dequantize-then-matmul up to summation
-//    order.
+//  * Arithmetic. The B fragments hold the unit's 64 activation rows in fp16,
+//    bf16 rows scaled by 2^S_m per output row m (S from the unit's 64 rows,
+//    so the largest magnitude lies in [2^14, 2^15)); the prep warp also
+//    stores 2^-S_m and -8 * 2^-24 * sum(a') per row, the tiles' starting
+//    value that removes the +8 offsets. Each mma warp runs the tile decode
+//    and folds the tiles' fp32 sums with the group scale (the unit lies in
+//    one group: groups are multiples of 64) times 2^-S_m. The result is the
+//    reference's fp32 dequantize-then-matmul up to summation order.
 #include "pk_common.cuh"
 
 #include <cstring>
@@ -60,7 +63,8 @@ using w4mma::kRowBytes;  // 64: a warp's 128 columns of one row
 
 constexpr int kWarps = 8;
 constexpr int kProducerWarp = kWarps;
-constexpr int kThreads = (kWarps + 1) * 32;
+constexpr int kPrepWarp = kWarps + 1;
+constexpr int kThreads = (kWarps + 2) * 32;
 constexpr int kMmaThreads = kWarps * 32;
 constexpr int kUnitRows = 64;                         // K rows per unit
 constexpr int kWarpCols = 128;                        // columns per warp
@@ -70,18 +74,25 @@ constexpr int kWBytes = kWarps * kBoxBytes;           // 32768
 constexpr int kSBytes = kSliceCols * 2;               // one group-scale row
 constexpr int kSBox = 256;                            // scales per TMA box (box limit 256)
 
+// A ring slot: the unit's weights (eight warp boxes), its group-scale row
+// and activations (TMA), then what the prep warp makes of the activations:
+// the fp16 B fragments, 2^-S_m and the +8 offsets' starting value per output
+// row (8 entries each, whatever M).
 template <int M>
 struct Cfg {
   static constexpr int kABytes = kUnitRows * 2 * M;  // [m][64] activations
-  static constexpr int kSlotBytes = (kWBytes + kSBytes + kABytes + 1023) / 1024 * 1024;
-  static constexpr int kFragWarpBytes = kKSteps * blk_words<M>() * 4;  // one unit's B fragments
+  static constexpr int kActOff = kWBytes + kSBytes;
+  static constexpr int kFragOff = kActOff + (kABytes + 15) / 16 * 16;
+  static constexpr int kFragBytes = kKSteps * blk_words<M>() * 4;
+  static constexpr int kPwOff = kFragOff + kFragBytes;
+  static constexpr int kOffOff = kPwOff + 8 * 4;
+  static constexpr int kSlotBytes = (kOffOff + 8 * 4 + 1023) / 1024 * 1024;
   // as many ring slots as the shared memory holds
-  static constexpr int kStages = (227 * 1024 - 1024 - 512 - kWarps * kFragWarpBytes) / kSlotBytes;
+  static constexpr int kStages = (227 * 1024 - 1024 - 512) / kSlotBytes;
   static constexpr int kRingBytes = kStages * kSlotBytes;
-  static constexpr int kFragOff = kRingBytes;
-  static constexpr int kBarOff = kFragOff + kWarps * kFragWarpBytes;
-  // per slot: activations + scales, the eight weight boxes, the slot's release
-  static constexpr int kBarsPerSlot = 1 + kWarps + 1;
+  static constexpr int kBarOff = kRingBytes;
+  // per slot: activations + scales, B fragments ready, eight weight boxes, release
+  static constexpr int kBarsPerSlot = 2 + kWarps + 1;
   static constexpr int kSmemBytes = kBarOff + kBarsPerSlot * kStages * 8 + 16 + 1024;
   static_assert(kStages >= 4, "a ring of at least four units");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
@@ -153,7 +164,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = smem_u32(smem);
   uint64_t* afull = reinterpret_cast<uint64_t*>(smem + C::kBarOff);  // [slot]: activations, scales
-  uint64_t* wfull = afull + C::kStages;                               // [slot][warp]: weights
+  uint64_t* bready = afull + C::kStages;                              // [slot]: B fragments
+  uint64_t* wfull = bready + C::kStages;                              // [slot][warp]: weights
   uint64_t* empty = wfull + C::kStages * kWarps;                      // [slot]
   volatile int* last_flag = reinterpret_cast<volatile int*>(empty + C::kStages);
 
@@ -176,6 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&afull[s], 1);
+      mbar_init(&bready[s], 1);
       for (int w = 0; w < kWarps; ++w) mbar_init(&wfull[s * kWarps + w], 1);
       mbar_init(&empty[s], kWarps);
     }
@@ -218,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int k0 = kb * kUnitRows;
         uint8_t* base = smem + slot * C::kSlotBytes;
         mbar_arrive_expect_tx(&afull[slot], tx_a);
-        tma_load_2d(base + kWBytes + kSBytes, &tmA, &afull[slot], k0, 0);
+        tma_load_2d(base + C::kActOff, &tmA, &afull[slot], k0, 0);
         if constexpr (kGrouped)
           for (int h = 0; h < kSliceCols / kSBox; ++h)
             tma_load_2d(base + kWBytes + h * kSBox * 2, &tmS, &afull[slot],
@@ -245,6 +258,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
+  } else if (warp == kPrepWarp) {
+    // ---------------- prep warp: activations -> B fragments ----------------
+    // Lane l takes rows 2l, 2l + 1 of the unit: bf16 rows scaled by 2^S_m per
+    // output row m (S_m from the unit's 64 rows), the offsets' starting value
+    // -8 * 2^-24 * sum(a') per row. No global access: no dependency wait.
+    bool failed = false;
+    for (int i = 0, slot = 0, round = 0; i < n_units;
+         ++i, slot = (slot + 1 == C::kStages ? 0 : slot + 1), round += (slot == 0)) {
+      const uint32_t base = sbase + slot * C::kSlotBytes;
+      if (!failed && !mbar_wait_sleep(&afull[slot], round & 1, p.status, kSiteGemvConsumer))
+        failed = true;
+      uint32_t raw[M];
+#pragma unroll
+      for (int m = 0; m < M; ++m) raw[m] = lds_u32(base + C::kActOff + (m * kUnitRows + 2 * lane) * 2);
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const int S =
+            kBf16 ? w4mma::scale_exp(__reduce_max_sync(0xffffffffu, w4mma::bf16x2_emax(raw[m])))
+                  : 0;
+        const uint32_t h2 = w4mma::to_f16x2<T>(raw[m], w4mma::exp2i(S));
+        w4mma::sts_u32(base + C::kFragOff + w4mma::bfrag_store_off<M>(lane, m), h2);
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+        float s = f.x + f.y;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) {
+          sts_f32(base + C::kPwOff + m * 4, w4mma::exp2i(-S));
+          sts_f32(base + C::kOffOff + m * 4, s * -4.76837158203125e-07f);  // -8 * 2^-24
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bready[slot]);
+    }
   } else {
     // ---------------- mma warps ----------------
     griddep_wait();
@@ -255,46 +301,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < 8; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) tot[j][e] = 0.0f;
-    const uint32_t frag = sbase + C::kFragOff + warp * C::kFragWarpBytes;
-    const uint32_t bfrag = frag + ((lm.g < M ? lm.g : M - 1) * 4 + lm.t) * 8;
+    const uint32_t bfrag_lane = C::kFragOff + ((lm.g < M ? lm.g : M - 1) * 4 + lm.t) * 8;
     bool failed = false;
     int slice = static_cast<int>(u0 / KB);
     int kb = static_cast<int>(u0 % KB);
     for (int i = 0, slot = 0, round = 0; i < n_units;
          ++i, slice += (kb + 1 == KB), kb = (kb + 1 == KB ? 0 : kb + 1),
              slot = (slot + 1 == C::kStages ? 0 : slot + 1), round += (slot == 0)) {
-      const int k0 = kb * kUnitRows;
       const uint32_t base = sbase + slot * C::kSlotBytes;
-      if (!failed && !mbar_wait_sleep(&afull[slot], round & 1, p.status, kSiteGemvConsumer))
+      if (!failed && !mbar_wait_sleep(&bready[slot], round & 1, p.status, kSiteGemvConsumer))
         failed = true;
-      // activations -> B fragments, one scale 2^S_m per output row for the
-      // unit's 64 rows (every warp keeps its own copy)
-      uint32_t raw[M];
-#pragma unroll
-      for (int m = 0; m < M; ++m)
-        raw[m] = lds_u32(base + kWBytes + kSBytes + (m * kUnitRows + 2 * lane) * 2);
-      int S[M];
-#pragma unroll
-      for (int m = 0; m < M; ++m)
-        S[m] = kBf16 ? w4mma::scale_exp(__reduce_max_sync(0xffffffffu, w4mma::bf16x2_emax(raw[m])))
-                     : 0;
-      float pw0 = 1.0f, pw1 = 1.0f;
-#pragma unroll
-      for (int m = 0; m < M; ++m) {
-        if (m == 2 * lm.t) pw0 = w4mma::exp2i(-S[m]);
-        if (m == 2 * lm.t + 1) pw1 = w4mma::exp2i(-S[m]);
-        w4mma::sts_u32(frag + w4mma::bfrag_store_off<M>(lane, m),
-                       w4mma::to_f16x2<T>(raw[m], w4mma::exp2i(S[m])));
-      }
-      __syncwarp();
+      uint32_t bf[kKSteps][2];
+      w4mma::load_bfrags<M>(base + bfrag_lane, bf);
+      const uint2 pwv = w4mma::lds_v2(base + C::kPwOff + 8 * lm.t);   // rows 2t, 2t + 1
+      const uint2 ofv = w4mma::lds_v2(base + C::kOffOff + 8 * lm.t);
+      const float pw0 = __uint_as_float(pwv.x), pw1 = __uint_as_float(pwv.y);
+      const float o0 = __uint_as_float(ofv.x), o1 = __uint_as_float(ofv.y);
+      const float doff[4] = {o0, o1, 16.0f * o0, 16.0f * o1};
       if (!failed && !mbar_wait_sleep(&wfull[slot * kWarps + warp], round & 1, p.status,
                                       kSiteGemvConsumer))
         failed = true;
       if (stamp && i == 0) t_first = globaltimer();
-      w4mma::unit<M, T, kGrouped, true>(lm, base + warp * kBoxBytes, bfrag,
-                                        base + kWBytes + (warp * kWarpCols + lm.g * 16) * 2,
-                                        p.scalar_scale, pw0, pw1, dc, tot);
-      __syncwarp();  // every lane is done with the slot and the fragments
+      w4mma::tiles<M, T, kGrouped, true>(lm, base + warp * kBoxBytes, bf,
+                                         base + kWBytes + (warp * kWarpCols + lm.g * 16) * 2,
+                                         p.scalar_scale, pw0, pw1, doff, dc, tot);
+      __syncwarp();  // every lane is done with the slot
       if (lane == 0) mbar_arrive(&empty[slot]);
 
       const bool seg_end = (i + 1 == n_units) || (kb + 1 == KB);

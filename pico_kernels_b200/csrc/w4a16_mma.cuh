@@ -141,27 +141,41 @@ __device__ __forceinline__ uint32_t to_f16x2(uint32_t raw, float sc) {
   }
 }
 
-// One unit of one warp: tot[j][e] += (sum over the warp's 64 rows of
-// q * a') * scale * (e < 2 ? pwe[e] : pwe[e - 2]). wbase: the warp's first
-// row in the swizzled slot; bfrag: this lane's B-fragment entry of k-step 0
-// (k-step s at + s * blk_words * 4); scale_addr: the lane's 32 bytes of group
-// scales (columns 16g .. 16g + 15), used when kGrouped.
-template <int M, typename T, bool kGrouped, bool kPw>
-__device__ __forceinline__ void unit(const LaneMap& lm, uint32_t wbase, uint32_t bfrag,
-                                     uint32_t scale_addr, float scalar_scale, float pw0,
-                                     float pw1, const Consts& dc, float (&tot)[8][4]) {
-  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t kOffLo = 0x80088008u;  // -8 * 2^-24 in both fp16 halves
-  constexpr uint32_t kOffHi = 0x80808080u;  // -128 * 2^-24
-  uint32_t bf[kKSteps][2];
-  float doff[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+// The B fragments of a unit's four k-steps (bfrag: this lane's entry of
+// k-step 0, k-step s at + s * blk_words * 4).
+template <int M>
+__device__ __forceinline__ void load_bfrags(uint32_t bfrag, uint32_t (&bf)[kKSteps][2]) {
 #pragma unroll
   for (int s = 0; s < kKSteps; ++s) {
     const uint2 v = lds_v2(bfrag + s * blk_words<M>() * 4);
     bf[s][0] = v.x;
     bf[s][1] = v.y;
-    mma_16816(doff, kOffLo, kOffHi, kOffLo, kOffHi, v.x, v.y);
   }
+}
+
+// The +8 offsets of a unit through the tensor cores: the constant
+// -8 * 2^-24 (tile rows g) and -128 * 2^-24 (rows g + 8) times the
+// activations, the starting value of every tile's sum.
+__device__ __forceinline__ void offsets_mma(const uint32_t (&bf)[kKSteps][2], float (&doff)[4]) {
+  constexpr uint32_t kOffLo = 0x80088008u;  // -8 * 2^-24 in both fp16 halves
+  constexpr uint32_t kOffHi = 0x80808080u;  // -128 * 2^-24
+#pragma unroll
+  for (int e = 0; e < 4; ++e) doff[e] = 0.0f;
+#pragma unroll
+  for (int s = 0; s < kKSteps; ++s) mma_16816(doff, kOffLo, kOffHi, kOffLo, kOffHi, bf[s][0], bf[s][1]);
+}
+
+// The tiles of one unit of one warp, started from doff, then folded:
+// tot[j][e] += tile sum * scale * (e % 2 ? pw1 : pw0) (kPw) or * scale.
+// wbase: the warp's first row in the swizzled slot; scale_addr: the lane's
+// 32 bytes of group scales (columns 16g .. 16g + 15), used when kGrouped.
+template <int M, typename T, bool kGrouped, bool kPw>
+__device__ __forceinline__ void tiles(const LaneMap& lm, uint32_t wbase,
+                                      const uint32_t (&bf)[kKSteps][2], uint32_t scale_addr,
+                                      float scalar_scale, float pw0, float pw1,
+                                      const float (&doff)[4], const Consts& dc,
+                                      float (&tot)[8][4]) {
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   float acc[8][4];
 #pragma unroll
   for (int j = 0; j < 8; ++j)
@@ -218,6 +232,18 @@ __device__ __forceinline__ void unit(const LaneMap& lm, uint32_t wbase, uint32_t
       tot[j][3] = fmaf(acc[j][3], so, tot[j][3]);
     }
   }
+}
+
+// One unit of one warp with its offsets through the tensor cores.
+template <int M, typename T, bool kGrouped, bool kPw>
+__device__ __forceinline__ void unit(const LaneMap& lm, uint32_t wbase, uint32_t bfrag,
+                                     uint32_t scale_addr, float scalar_scale, float pw0,
+                                     float pw1, const Consts& dc, float (&tot)[8][4]) {
+  uint32_t bf[kKSteps][2];
+  load_bfrags<M>(bfrag, bf);
+  float doff[4];
+  offsets_mma(bf, doff);
+  tiles<M, T, kGrouped, kPw>(lm, wbase, bf, scale_addr, scalar_scale, pw0, pw1, doff, dc, tot);
 }
 
 // The lane's sums as [m][column] partials of its warp: 2^24 (low nibbles)
