@@ -140,15 +140,14 @@ PK_API size_t pk_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int split
  * 1 = no split, > 1 = split the K reduction over that many CTAs (decode
  * shapes), reduced deterministically in split order through `workspace`
  * (pk_w4a16_workspace_size bytes, zero-filled once before its first use; the
- * kernel leaves it ready for the next call). With split_k = 0 at M = 1 (and
- * at M = 2 for layers of 16 MB or more) a CUDA-core GEMV runs instead, and
- * at M = 1..3 on layers that fit one wave of clusters (N % 128 == 0,
- * K % 512 == 0, e.g. 4096 x 4096) its cluster form, which needs no
- * workspace; for large layers it splits K over the SMs and reduces through
- * the workspace,
- * and without one it falls back to the tensor-core decode kernel, which
- * serves the other shapes up to M = 32 (N and K multiples of 128, group 128
- * or a scalar scale). For 32 < M <= 256 (N % 128 == 0, K % 64 == 0) a
+ * kernel leaves it ready for the next call). With split_k = 0 and M <= 8 a
+ * decode GEMV on mma.sync tiles of exactly decoded fp16 operands runs
+ * instead: on layers that fit one wave of clusters (N % 128 == 0,
+ * K % 512 == 0, group 128 or a scalar scale, e.g. 4096 x 4096) its cluster
+ * form, which needs no workspace; on other layers (N % 32 == 0, groups a
+ * multiple of 64) a stream-K form that reduces through the workspace, and
+ * without one the tensor-core decode kernel, which also serves 8 < M <= 32
+ * (N and K multiples of 128, group 128 or a scalar scale). For 32 < M <= 256 (N % 128 == 0, K % 64 == 0) a
  * swap-AB tensor-core kernel that dequantizes each weight once runs where a
  * model of measured per-stage times favours it over the tcgen05 prefill
  * kernel, which serves the rest. From
@@ -209,7 +208,7 @@ PK_API int pk_w4a16_gemm_host(const void* a_host, int a_dtype, int64_t lda, cons
                               void* y_dev, void* workspace, size_t workspace_bytes,
                               void* stream);
 
-/* Weight staging of the decode GEMVs (M = 1..3; process-wide, default 0).
+/* Weight staging of the cluster decode GEMV (M <= 8; process-wide, default 0).
  * mode 0: a GEMV prefetches its weights and scales into L2 before the
  *   kernel ahead of it in the stream has finished (a hint that never returns
  *   stale data), and loads them into shared memory only after it has.
@@ -224,7 +223,7 @@ PK_API int pk_w4a16_gemm_host(const void* a_host, int a_dtype, int64_t lda, cons
 PK_API int pk_set_weight_staging(int mode);
 
 /* Profiling aid: while dev_buf is set (NULL turns it off), each CTA of the
- * decode GEMVs (M = 1..3) launched afterwards writes 8 uint64 words at
+ * decode GEMVs (M <= 8) launched afterwards writes 8 uint64 words at
  * dev_buf[slot * bytes / 16 + 8 * cta]: %globaltimer at entry, after
  * griddepcontrol.wait, when its first weights landed, when its arithmetic
  * ended and when its output was stored, then its SM id, its unit count (the
