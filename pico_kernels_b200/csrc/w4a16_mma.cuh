@@ -165,27 +165,25 @@ __device__ __forceinline__ void offsets_mma(const uint32_t (&bf)[kKSteps][2], fl
   for (int s = 0; s < kKSteps; ++s) mma_16816(doff, kOffLo, kOffHi, kOffLo, kOffHi, bf[s][0], bf[s][1]);
 }
 
-// The tiles of one unit of one warp, started from doff, then folded:
-// tot[j][e] += tile sum * scale * (e % 2 ? pw1 : pw0) (kPw) or * scale.
-// wbase: the warp's first row in the swizzled slot; scale_addr: the lane's
-// 32 bytes of group scales (columns 16g .. 16g + 15), used when kGrouped.
-template <int M, typename T, bool kGrouped, bool kPw>
-__device__ __forceinline__ void tiles(const LaneMap& lm, uint32_t wbase,
-                                      const uint32_t (&bf)[kKSteps][2], uint32_t scale_addr,
-                                      float scalar_scale, float pw0, float pw1,
-                                      const float (&doff)[4], const Consts& dc,
-                                      float (&tot)[8][4]) {
-  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-  float acc[8][4];
+// The tile loop of one unit of one warp: acc[j] = doff + the tile sums of
+// the unit's four k-steps. v holds the first k-step's rows on entry (loaded
+// with load_rows); the later k-steps' rows are loaded while a k-step's eight
+// A fragments are decoded, and its eight mma's then issue back to back.
+__device__ __forceinline__ void load_rows(const LaneMap& lm, uint32_t wbase, int s, uint2 (&v)[4]) {
+#pragma unroll
+  for (int r = 0; r < 4; ++r) v[r] = lds_v2(wbase + s * 16 * kRowBytes + lm.woff[r]);
+}
+__device__ __forceinline__ void tile_loop(const LaneMap& lm, uint32_t wbase, uint2 (&v)[4],
+                                          const uint32_t (&bf)[kKSteps][2],
+                                          const float (&doff)[4], const Consts& dc,
+                                          float (&acc)[8][4]) {
 #pragma unroll
   for (int j = 0; j < 8; ++j)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[j][e] = doff[e];
 #pragma unroll
   for (int s = 0; s < kKSteps; ++s) {
-    uint2 v[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) v[r] = lds_v2(wbase + s * 16 * kRowBytes + lm.woff[r]);
+    uint32_t a[8][4];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint32_t w0 = h ? v[0].y : v[0].x, w1 = h ? v[1].y : v[1].x;
@@ -193,18 +191,33 @@ __device__ __forceinline__ void tiles(const LaneMap& lm, uint32_t wbase,
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
         const uint32_t z01 = prmt(w0, w1, lm.sel[b]), z23 = prmt(w2, w3, lm.sel[b]);
-        mma_16816(acc[4 * h + b], lop3_and_xor(z01, dc.m_lo, dc.f_lo),
-                  lop3_and_xor(z01, dc.m_hi, dc.f_hi), lop3_and_xor(z23, dc.m_lo, dc.f_lo),
-                  lop3_and_xor(z23, dc.m_hi, dc.f_hi), bf[s][0], bf[s][1]);
+        a[4 * h + b][0] = lop3_and_xor(z01, dc.m_lo, dc.f_lo);
+        a[4 * h + b][1] = lop3_and_xor(z01, dc.m_hi, dc.f_hi);
+        a[4 * h + b][2] = lop3_and_xor(z23, dc.m_lo, dc.f_lo);
+        a[4 * h + b][3] = lop3_and_xor(z23, dc.m_hi, dc.f_hi);
       }
     }
+    if (s + 1 < kKSteps) load_rows(lm, wbase, s + 1, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      mma_16816(acc[j], a[j][0], a[j][1], a[j][2], a[j][3], bf[s][0], bf[s][1]);
   }
-  uint32_t sws[8];
-  if constexpr (kGrouped) {
-    const uint4 s0 = lds_v4(scale_addr), s1 = lds_v4(scale_addr + 16);
-    sws[0] = s0.x, sws[1] = s0.y, sws[2] = s0.z, sws[3] = s0.w;
-    sws[4] = s1.x, sws[5] = s1.y, sws[6] = s1.z, sws[7] = s1.w;
-  }
+}
+
+// The lane's 32 bytes of group scales (columns 16g .. 16g + 15).
+__device__ __forceinline__ void load_scales(uint32_t scale_addr, uint32_t (&sws)[8]) {
+  const uint4 s0 = lds_v4(scale_addr), s1 = lds_v4(scale_addr + 16);
+  sws[0] = s0.x, sws[1] = s0.y, sws[2] = s0.z, sws[3] = s0.w;
+  sws[4] = s1.x, sws[5] = s1.y, sws[6] = s1.z, sws[7] = s1.w;
+}
+
+// Fold a unit's tile sums: tot[j][e] += acc[j][e] * scale * (e % 2 ? pw1 :
+// pw0) (kPw) or * scale; scale from sws (kGrouped) or scalar_scale.
+template <typename T, bool kGrouped, bool kPw>
+__device__ __forceinline__ void fold(const float (&acc)[8][4], const uint32_t (&sws)[8],
+                                     float scalar_scale, float pw0, float pw1,
+                                     float (&tot)[8][4]) {
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     float se, so;
@@ -232,6 +245,22 @@ __device__ __forceinline__ void tiles(const LaneMap& lm, uint32_t wbase,
       tot[j][3] = fmaf(acc[j][3], so, tot[j][3]);
     }
   }
+}
+
+// The tiles of one unit of one warp, started from doff, then folded.
+template <int M, typename T, bool kGrouped, bool kPw>
+__device__ __forceinline__ void tiles(const LaneMap& lm, uint32_t wbase,
+                                      const uint32_t (&bf)[kKSteps][2], uint32_t scale_addr,
+                                      float scalar_scale, float pw0, float pw1,
+                                      const float (&doff)[4], const Consts& dc,
+                                      float (&tot)[8][4]) {
+  uint2 v[4];
+  load_rows(lm, wbase, 0, v);
+  float acc[8][4];
+  tile_loop(lm, wbase, v, bf, doff, dc, acc);
+  uint32_t sws[8];
+  if constexpr (kGrouped) load_scales(scale_addr, sws);
+  fold<T, kGrouped, kPw>(acc, sws, scalar_scale, pw0, pw1, tot);
 }
 
 // One unit of one warp with its offsets through the tensor cores.
