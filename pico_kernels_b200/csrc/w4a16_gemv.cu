@@ -6,16 +6,18 @@
 // reference's nibble order (gemm_int4.py:43-50, pack_int4_n at :65-72).
 //
 // At M <= 8 the layer is a stream over the packed weights (K*N/2 bytes) with
-// 2*M*K*N flops, far below one flop per byte. The decode is the shared tile
-// decode of w4a16_mma.cuh (2 PRMT + 4 LOP3 + 1 mma per 8 weights and lane).
+// 2*M*K*N flops, far below one flop per byte. The decode is the four-tile
+// form of the tile decode in w4a16_mma.cuh (2 PRMT + 4 LOP3 + 1 mma per 8
+// weights and lane) on 16 mma warps: with two warps per scheduler the decode's
+// dependency chains left the issue slots ~65 % idle.
 //
 //  * Units. The weights are cut into units of 64 rows x 1024 columns (64
 //    rows of 512 contiguous bytes, 32 KB): wide enough that each DRAM page a
 //    unit opens serves half a kilobyte (units one 64-byte column strip wide
 //    streamed at about half the HBM rate). A "slice" is a 1024-column strip,
-//    KB units tall. Warp w of 8 owns columns [128w, 128w + 128) of every
-//    unit: its own TMA box (64 rows x 64 bytes, 64-byte swizzled), its own
-//    accumulators, no cross-warp reduction.
+//    KB units tall. Warp w of 16 owns columns [64w, 64w + 64) of every unit
+//    (a quarter of one of the unit's four TMA boxes of 64 rows x 128 bytes,
+//    128-byte swizzled), its own accumulators: no cross-warp reduction.
 //  * Work split (stream-K): units numbered slice-major, CTA c of G (one per
 //    SM) takes [U*c/G, U*(c+1)/G). A CTA's range covers parts of a few slices
 //    ("segments"). A segment that is a whole slice is stored directly;
@@ -24,12 +26,12 @@
 //    acq_rel atomic; the last arriver sums the slice's partials in CTA order,
 //    stores, and re-arms the counter. Fixed summation order: deterministic
 //    for a given SM count.
-//  * Pipeline. Warp 8 (one thread) is the TMA producer of a ring of as many
+//  * Pipeline. Warp 16 (one thread) is the TMA producer of a ring of as many
 //    unit slots as shared memory holds (six, ~220 KB): per unit the
 //    activation tile A[0:M, k0:k0+64] and the unit's group-scale row (one
-//    mbarrier), then the eight warps' weight boxes (one mbarrier each).
-//    Warp 9 turns each unit's activations into the B fragments the eight mma
-//    warps share (one mbarrier), so their loop is the tile decode alone.
+//    mbarrier), then the four weight boxes (one mbarrier each). Warp 17
+//    turns each unit's activations into the B fragments the 16 mma warps
+//    share (one mbarrier), so their loop is the tile decode alone.
 //    Before griddepcontrol.wait it only prefetches weights and scales into
 //    L2 (a hint that cannot return stale data), so with programmatic
 //    dependent launch the DRAM fetch overlaps the previous kernel's tail;
@@ -55,26 +57,26 @@ namespace pk {
 namespace {
 
 using w4mma::Consts;
-using w4mma::LaneMap;
 using w4mma::blk_words;
 using w4mma::kKSteps;
 using w4mma::kMaxM;
-using w4mma::kRowBytes;  // 64: a warp's 128 columns of one row
+using w4mma::kBoxRowBytes4;  // 128: four warps' 256 columns of one row
 
-constexpr int kWarps = 8;
+constexpr int kWarps = 16;
 constexpr int kProducerWarp = kWarps;
 constexpr int kPrepWarp = kWarps + 1;
 constexpr int kThreads = (kWarps + 2) * 32;
 constexpr int kMmaThreads = kWarps * 32;
 constexpr int kUnitRows = 64;                         // K rows per unit
-constexpr int kWarpCols = 128;                        // columns per warp
+constexpr int kWarpCols = 64;                         // columns per warp
 constexpr int kSliceCols = kWarps * kWarpCols;        // 1024 columns per slice
-constexpr int kBoxBytes = kUnitRows * kRowBytes;      // 4096: one warp's weights
-constexpr int kWBytes = kWarps * kBoxBytes;           // 32768
+constexpr int kBoxes = kWarps / 4;                    // TMA boxes per unit, four warps each
+constexpr int kBoxBytes = kUnitRows * kBoxRowBytes4;  // 8192
+constexpr int kWBytes = kBoxes * kBoxBytes;           // 32768
 constexpr int kSBytes = kSliceCols * 2;               // one group-scale row
 constexpr int kSBox = 256;                            // scales per TMA box (box limit 256)
 
-// A ring slot: the unit's weights (eight warp boxes), its group-scale row
+// A ring slot: the unit's weights (four boxes), its group-scale row
 // and activations (TMA), then what the prep warp makes of the activations:
 // the fp16 B fragments, 2^-S_m and the +8 offsets' starting value per output
 // row (8 entries each, whatever M).
@@ -91,8 +93,8 @@ struct Cfg {
   static constexpr int kStages = (227 * 1024 - 1024 - 512) / kSlotBytes;
   static constexpr int kRingBytes = kStages * kSlotBytes;
   static constexpr int kBarOff = kRingBytes;
-  // per slot: activations + scales, B fragments ready, eight weight boxes, release
-  static constexpr int kBarsPerSlot = 2 + kWarps + 1;
+  // per slot: activations + scales, B fragments ready, four weight boxes, release
+  static constexpr int kBarsPerSlot = 2 + kBoxes + 1;
   static constexpr int kSmemBytes = kBarOff + kBarsPerSlot * kStages * 8 + 16 + 1024;
   static_assert(kStages >= 4, "a ring of at least four units");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
@@ -165,8 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sbase = smem_u32(smem);
   uint64_t* afull = reinterpret_cast<uint64_t*>(smem + C::kBarOff);  // [slot]: activations, scales
   uint64_t* bready = afull + C::kStages;                              // [slot]: B fragments
-  uint64_t* wfull = bready + C::kStages;                              // [slot][warp]: weights
-  uint64_t* empty = wfull + C::kStages * kWarps;                      // [slot]
+  uint64_t* wfull = bready + C::kStages;                              // [slot][box]: weights
+  uint64_t* empty = wfull + C::kStages * kBoxes;                      // [slot]
   volatile int* last_flag = reinterpret_cast<volatile int*>(empty + C::kStages);
 
   const int warp = threadIdx.x >> 5;
@@ -189,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&afull[s], 1);
       mbar_init(&bready[s], 1);
-      for (int w = 0; w < kWarps; ++w) mbar_init(&wfull[s * kWarps + w], 1);
+      for (int b = 0; b < kBoxes; ++b) mbar_init(&wfull[s * kBoxes + b], 1);
       mbar_init(&empty[s], kWarps);
     }
     fence_barrier_init();
@@ -208,8 +210,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int pre = n_units < C::kStages ? n_units : C::kStages;
       for (int i = 0, s = static_cast<int>(u0 / KB), kb = static_cast<int>(u0 % KB); i < pre;
            ++i) {
-        for (int w = 0; w < kWarps; ++w)
-          tma_prefetch_l2_2d(&tmW, s * (kSliceCols / 2) + w * kRowBytes, kb * kUnitRows);
+        for (int b = 0; b < kBoxes; ++b)
+          tma_prefetch_l2_2d(&tmW, s * (kSliceCols / 2) + b * kBoxRowBytes4, kb * kUnitRows);
         if constexpr (kGrouped)
           for (int h = 0; h < kSliceCols / kSBox; ++h)
             tma_prefetch_l2_2d(&tmS, s * kSliceCols + h * kSBox, group_of(kb * kUnitRows, p));
@@ -236,11 +238,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int h = 0; h < kSliceCols / kSBox; ++h)
             tma_load_2d(base + kWBytes + h * kSBox * 2, &tmS, &afull[slot],
                         slice * kSliceCols + h * kSBox, group_of(k0, p));
-        // the eight boxes of a unit are 512 contiguous bytes of each row
-        for (int w = 0; w < kWarps; ++w) {
-          mbar_arrive_expect_tx(&wfull[slot * kWarps + w], kBoxBytes);
-          tma_load_2d(base + w * kBoxBytes, &tmW, &wfull[slot * kWarps + w],
-                      slice * (kSliceCols / 2) + w * kRowBytes, k0);
+        // the four boxes of a unit are 512 contiguous bytes of each row
+        for (int b = 0; b < kBoxes; ++b) {
+          mbar_arrive_expect_tx(&wfull[slot * kBoxes + b], kBoxBytes);
+          tma_load_2d(base + b * kBoxBytes, &tmW, &wfull[slot * kBoxes + b],
+                      slice * (kSliceCols / 2) + b * kBoxRowBytes4, k0);
         }
         issued = i + 1;
         if (++kb == KB) kb = 0, ++slice;
@@ -253,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = i % C::kStages;
           const uint32_t par = (i / C::kStages) & 1;
           mbar_wait(&afull[s], par, nullptr, 0);
-          for (int w = 0; w < kWarps; ++w) mbar_wait(&wfull[s * kWarps + w], par, nullptr, 0);
+          for (int b = 0; b < kBoxes; ++b) mbar_wait(&wfull[s * kBoxes + b], par, nullptr, 0);
         }
       }
     }
@@ -295,13 +297,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- mma warps ----------------
     griddep_wait();
     if (stamp) t_wait = globaltimer();
-    const LaneMap lm = w4mma::lane_map(lane);
-    float tot[8][4];  // tile j: columns 16g + 2j ([0], [1]) and + 1 ([2], [3]); rows 2t, 2t + 1
+    const int g = lane >> 2, t = lane & 3;  // the mma fragments' group and thread-in-group
+    float tot[4][4];  // tile j: columns 8g + 2j ([0], [1]) and + 1 ([2], [3]); rows 2t, 2t + 1
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) tot[j][e] = 0.0f;
-    const uint32_t bfrag_lane = C::kFragOff + ((lm.g < M ? lm.g : M - 1) * 4 + lm.t) * 8;
+    const uint32_t bfrag_lane = C::kFragOff + ((g < M ? g : M - 1) * 4 + t) * 8;
+    uint32_t roff[4];  // the lane's rows in its box (four warps per box)
+    w4mma::lane_rows4(lane, warp & 3, roff);
+    const uint32_t box_off = (warp >> 2) * kBoxBytes;
     bool failed = false;
     int slice = static_cast<int>(u0 / KB);
     int kb = static_cast<int>(u0 % KB);
@@ -313,18 +318,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         failed = true;
       uint32_t bf[kKSteps][2];
       w4mma::load_bfrags<M>(base + bfrag_lane, bf);
-      const uint2 pwv = w4mma::lds_v2(base + C::kPwOff + 8 * lm.t);   // rows 2t, 2t + 1
-      const uint2 ofv = w4mma::lds_v2(base + C::kOffOff + 8 * lm.t);
+      const uint2 pwv = w4mma::lds_v2(base + C::kPwOff + 8 * t);   // rows 2t, 2t + 1
+      const uint2 ofv = w4mma::lds_v2(base + C::kOffOff + 8 * t);
       const float pw0 = __uint_as_float(pwv.x), pw1 = __uint_as_float(pwv.y);
       const float o0 = __uint_as_float(ofv.x), o1 = __uint_as_float(ofv.y);
       const float doff[4] = {o0, o1, 16.0f * o0, 16.0f * o1};
-      if (!failed && !mbar_wait_sleep(&wfull[slot * kWarps + warp], round & 1, p.status,
+      if (!failed && !mbar_wait_sleep(&wfull[slot * kBoxes + (warp >> 2)], round & 1, p.status,
                                       kSiteGemvConsumer))
         failed = true;
       if (stamp && i == 0) t_first = globaltimer();
-      w4mma::tiles<M, T, kGrouped, true>(lm, base + warp * kBoxBytes, bf,
-                                         base + kWBytes + (warp * kWarpCols + lm.g * 16) * 2,
-                                         p.scalar_scale, pw0, pw1, doff, dc, tot);
+      float acc[4][4];
+      w4mma::tile_loop4(base + box_off, roff, bf, doff, dc, acc);
+      w4mma::fold4<T, kGrouped>(acc, base + kWBytes + (warp * kWarpCols + 8 * g) * 2,
+                                p.scalar_scale, pw0, pw1, tot);
       __syncwarp();  // every lane is done with the slot
       if (lane == 0) mbar_arrive(&empty[slot]);
 
@@ -339,13 +345,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* mine = p.partials + (cta + slice) * kOut;
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int n = 2 * lm.t + e;
+        const int n = 2 * t + e;
         if (n < M) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
+          for (int j = 0; j < 4; ++j) {
             // undo 2^-24 (low nibbles) and 2^-20 (high nibbles)
             const float lo = tot[j][e] * 16777216.0f, hi = tot[j][2 + e] * 1048576.0f;
-            const int c = warp * kWarpCols + 16 * lm.g + 2 * j;
+            const int c = warp * kWarpCols + 8 * g + 2 * j;
             if (whole) {
               const int64_t col = static_cast<int64_t>(slice) * kSliceCols + c;
               if (col < p.N) store_col(p, n, col, lo), stored = true;
@@ -357,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
+      for (int j = 0; j < 4; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) tot[j][e] = 0.0f;
       if (whole) continue;
@@ -488,8 +494,8 @@ cudaError_t launch_w4a16_gemv(const DecodeArgs& a, cudaStream_t s, const char** 
   }
   CUtensorMap tmW, tmA, tmS;
   const CUtensorMapDataType dt = tmap_type16(a.a_dtype);
-  if (!encode_tmap_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.wp, a.N / 2, a.K, a.N / 2, kRowBytes,
-                      kUnitRows, CU_TENSOR_MAP_SWIZZLE_64B, why))
+  if (!encode_tmap_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.wp, a.N / 2, a.K, a.N / 2,
+                      kBoxRowBytes4, kUnitRows, CU_TENSOR_MAP_SWIZZLE_128B, why))
     return cudaErrorInvalidValue;
   if (!encode_tmap_2d(&tmA, dt, a.a, a.K, a.M, a.lda * 2, kUnitRows, static_cast<uint32_t>(a.M),
                       CU_TENSOR_MAP_SWIZZLE_NONE, why))

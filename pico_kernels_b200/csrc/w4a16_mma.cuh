@@ -190,11 +190,12 @@ __device__ __forceinline__ void tile_loop(const LaneMap& lm, uint32_t wbase, uin
       const uint32_t w2 = h ? v[2].y : v[2].x, w3 = h ? v[3].y : v[3].x;
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
-        const uint32_t z01 = prmt(w0, w1, lm.sel[b]), z23 = prmt(w2, w3, lm.sel[b]);
-        a[4 * h + b][0] = lop3_and_xor(z01, dc.m_lo, dc.f_lo);
-        a[4 * h + b][1] = lop3_and_xor(z01, dc.m_hi, dc.f_hi);
-        a[4 * h + b][2] = lop3_and_xor(z23, dc.m_lo, dc.f_lo);
-        a[4 * h + b][3] = lop3_and_xor(z23, dc.m_hi, dc.f_hi);
+        const uint32_t z01 = __byte_perm(w0, w1, lm.sel[b]);
+        const uint32_t z23 = __byte_perm(w2, w3, lm.sel[b]);
+        a[4 * h + b][0] = (z01 & dc.m_lo) ^ dc.f_lo;
+        a[4 * h + b][1] = (z01 & dc.m_hi) ^ dc.f_hi;
+        a[4 * h + b][2] = (z23 & dc.m_lo) ^ dc.f_lo;
+        a[4 * h + b][3] = (z23 & dc.m_hi) ^ dc.f_hi;
       }
     }
     if (s + 1 < kKSteps) load_rows(lm, wbase, s + 1, v);
@@ -273,6 +274,105 @@ __device__ __forceinline__ void unit(const LaneMap& lm, uint32_t wbase, uint32_t
   float doff[4];
   offsets_mma(bf, doff);
   tiles<M, T, kGrouped, kPw>(lm, wbase, bf, scale_addr, scalar_scale, pw0, pw1, doff, dc, tot);
+}
+
+// ---------------------------------------------------------------------------
+// Four-tile warps (64 columns, 32 packed bytes per row), for kernels with 16
+// mma warps. Four warps share a TMA box of 64 rows x 128 bytes, 128-byte
+// swizzled (the 16-byte chunk index XOR-ed with row % 8); warp q of a box
+// owns bytes [32q, 32q + 32). Lane (g, t) reads the word of columns
+// [8g, 8g + 8) of rows 2t, 2t + 1, 2t + 8, 2t + 9 of a k-step, the tile's
+// k-columns of those numbers: in every load the four lane groups touch rows
+// whose (row / 2) % 4 differ, so their chunks land on different banks
+// (conflict-free). Tile j (= byte j of the word) has columns 8g + 2j (tile
+// row g) and 8g + 2j + 1 (row g + 8). The B fragments are those of the
+// eight-tile form (rows 2l, 2l + 1 per prep lane l).
+// ---------------------------------------------------------------------------
+constexpr int kRowBytes4 = 32;     // a warp's bytes of one row
+constexpr int kBoxRowBytes4 = 128;  // four warps' bytes of one row
+
+// Byte offsets, within a box, of the lane's four rows of k-step 0 (k-step s
+// at + s * 16 * 128: 16 rows keep row % 8).
+__device__ __forceinline__ void lane_rows4(int lane, int q, uint32_t (&off)[4]) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int row = 2 * t + (r & 1) + 8 * (r >> 1);
+    const int chunk = (2 * q + (g >> 2)) ^ (row & 7);
+    off[r] = row * kBoxRowBytes4 + chunk * 16 + (g & 3) * 4;
+  }
+}
+
+__device__ __forceinline__ void load_rows4(uint32_t box, const uint32_t (&off)[4], int s,
+                                           uint32_t (&v)[4]) {
+#pragma unroll
+  for (int r = 0; r < 4; ++r) v[r] = lds_u32(box + s * 16 * kBoxRowBytes4 + off[r]);
+}
+
+// acc[j] = doff + the tile sums of the unit's four k-steps (box: the warp's
+// box in the slot, off: lane_rows4).
+__device__ __forceinline__ void tile_loop4(uint32_t box, const uint32_t (&off)[4],
+                                           const uint32_t (&bf)[kKSteps][2],
+                                           const float (&doff)[4], const Consts& dc,
+                                           float (&acc)[4][4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[j][e] = doff[e];
+  uint32_t v[4];
+  load_rows4(box, off, 0, v);
+#pragma unroll
+  for (int s = 0; s < kKSteps; ++s) {
+    uint32_t a[4][4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const uint32_t sel = b | (b << 4) | ((b + 4) << 8) | ((b + 4) << 12);
+      const uint32_t z01 = __byte_perm(v[0], v[1], sel);
+      const uint32_t z23 = __byte_perm(v[2], v[3], sel);
+      a[b][0] = (z01 & dc.m_lo) ^ dc.f_lo;
+      a[b][1] = (z01 & dc.m_hi) ^ dc.f_hi;
+      a[b][2] = (z23 & dc.m_lo) ^ dc.f_lo;
+      a[b][3] = (z23 & dc.m_hi) ^ dc.f_hi;
+    }
+    if (s + 1 < kKSteps) load_rows4(box, off, s + 1, v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      mma_16816(acc[j], a[j][0], a[j][1], a[j][2], a[j][3], bf[s][0], bf[s][1]);
+  }
+}
+
+// Fold four tiles: tot[j][e] += acc[j][e] * scale * (e % 2 ? pw1 : pw0);
+// scale from the lane's 16 bytes of group scales (columns 8g .. 8g + 7).
+template <typename T, bool kGrouped>
+__device__ __forceinline__ void fold4(const float (&acc)[4][4], uint32_t scale_addr,
+                                      float scalar_scale, float pw0, float pw1,
+                                      float (&tot)[4][4]) {
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  uint32_t sws[4] = {0u, 0u, 0u, 0u};
+  if constexpr (kGrouped) {
+    const uint4 s0 = lds_v4(scale_addr);
+    sws[0] = s0.x, sws[1] = s0.y, sws[2] = s0.z, sws[3] = s0.w;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float se, so;
+    if constexpr (kGrouped) {
+      if constexpr (kBf16) {
+        se = __uint_as_float(sws[j] << 16);
+        so = __uint_as_float(sws[j] & 0xFFFF0000u);
+      } else {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&sws[j]));
+        se = f.x;
+        so = f.y;
+      }
+    } else {
+      se = so = scalar_scale;
+    }
+    tot[j][0] = fmaf(acc[j][0], se * pw0, tot[j][0]);
+    tot[j][1] = fmaf(acc[j][1], se * pw1, tot[j][1]);
+    tot[j][2] = fmaf(acc[j][2], so * pw0, tot[j][2]);
+    tot[j][3] = fmaf(acc[j][3], so * pw1, tot[j][3]);
+  }
 }
 
 // The lane's sums as [m][column] partials of its warp: 2^24 (low nibbles)
