@@ -109,6 +109,30 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
     return _lib
 
 
+_fast = None
+
+
+def fast():
+    """The CPython fast-call module (_pkfast) over the same library, or the
+    ctypes library when that module was not built: both expose the hot calls
+    under their C names' suffix (w4a16_gemm, w4a16_gemm_host)."""
+    global _fast
+    f = _fast
+    if f is not None:
+        return f
+    lib = load()  # the library first, by path: the module then binds to it
+    try:
+        from . import _pkfast as mod  # noqa: PLC0415
+        f = mod
+    except ImportError:
+        class _Ctypes:
+            w4a16_gemm = lib.pk_w4a16_gemm
+            w4a16_gemm_host = lib.pk_w4a16_gemm_host
+        f = _Ctypes
+    _fast = f
+    return f
+
+
 def last_error() -> str:
     return load().pk_last_error_string().decode(errors="replace")
 

@@ -5,7 +5,10 @@
 Each ``csrc/*.cu`` compiles to an object under ``_build/`` (in parallel, and
 only when it or a header changed), then everything links into
 ``pico_kernels_b200/libpico_b200.so``. No fast-math: the quantizers rely on
-IEEE fp32 division for bit-exact parity.
+IEEE fp32 division for bit-exact parity. Then ``csrc/pyfast.cpp`` compiles
+with the host compiler into the CPython module ``_pkfast`` beside it, the
+fast-call entry points of the hottest calls (ctypes remains the path for
+the rest, and for all calls when Python's headers are missing).
 """
 
 from __future__ import annotations
@@ -15,6 +18,7 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
@@ -23,6 +27,7 @@ CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
 BUILD = PKG.parent / "_build"
 LIB = PKG / "libpico_b200.so"
+FAST = PKG / ("_pkfast" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -70,12 +75,34 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if force or not LIB.exists() or LIB.stat().st_mtime < max(o.stat().st_mtime for o in objs):
         tmp = LIB.with_suffix(".so.tmp")
         cmd = [cc, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcudart_static",
-               "-ldl", "-lrt", "-lpthread"]
+               "-ldl", "-lrt", "-lpthread", "-Xlinker", "-soname=libpico_b200.so"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
         os.replace(tmp, LIB)
+    build_fast(force)
     return LIB
+
+
+def build_fast(force: bool = False) -> Path | None:
+    """The CPython module _pkfast (csrc/pyfast.cpp), linked against the
+    library by its soname with an $ORIGIN run path; None without headers."""
+    src = CSRC / "pyfast.cpp"
+    inc = sysconfig.get_paths().get("include")
+    cxx = shutil.which("g++") or shutil.which("c++")
+    if not inc or not (Path(inc) / "Python.h").exists() or cxx is None:
+        return None
+    newest = max(src.stat().st_mtime, LIB.stat().st_mtime, (INCLUDE / "pico_b200.h").stat().st_mtime)
+    if not force and FAST.exists() and FAST.stat().st_mtime >= newest:
+        return FAST
+    tmp = FAST.with_suffix(".tmp")
+    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", f"-I{inc}", f"-I{INCLUDE}", str(src),
+           "-o", str(tmp), f"-L{PKG}", "-lpico_b200", "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"host compiler failed on {src.name}:\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, FAST)
+    return FAST
 
 
 def main() -> None:

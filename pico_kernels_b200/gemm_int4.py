@@ -149,7 +149,7 @@ def int4_gemm(a: torch.Tensor, w_packed: torch.Tensor, scale,
         ws_bytes = _ws_bytes[key] = lib.pk_w4a16_workspace_size(M, N, K, split_k)
     stream = _lib.stream_of(a)
     ws = _lib.workspace(a.device, ws_bytes, stream=stream) if ws_bytes else None
-    st = lib.pk_w4a16_gemm(
+    st = _lib.fast().w4a16_gemm(
         a.data_ptr(), _lib.dtype_code(a.dtype), a.stride(0), w_packed.data_ptr(),
         _lib.ptr(scales), scalar, group, M, N, K, out.data_ptr(), _lib.dtype_code(out_dtype), N,
         split_k, _lib.ptr(ws), ws_bytes, stream)
@@ -227,7 +227,7 @@ def int4_gemm_host(a: torch.Tensor, w_packed: torch.Tensor, scale, *,
     ws = _lib.workspace(dev, ws_bytes, stream=stream) if ws_bytes else None
     a_dev = _lib.workspace(dev, M * K * 2, tag="stage_a", stream=stream)
     y_dev = _lib.workspace(dev, M * N * out.element_size(), tag="stage_y", stream=stream)
-    st = lib.pk_w4a16_gemm_host(
+    st = _lib.fast().w4a16_gemm_host(
         a.data_ptr(), _lib.dtype_code(a.dtype), a.stride(0), w_packed.data_ptr(),
         _lib.ptr(scales), scalar, group, M, N, K, out.data_ptr(), _lib.dtype_code(out_dtype),
         a_dev.data_ptr(), y_dev.data_ptr(), _lib.ptr(ws), ws_bytes, stream)

@@ -110,3 +110,21 @@ def test_workspace_size_is_host_only():
     assert lib.pk_w4a16_workspace_size(1, 4096, 4096, 1) == 0
     assert lib.pk_w4a16_workspace_size(1, 4096, 4096, 8) > 0
     assert lib.pk_w4a16_workspace_size(1, 4096, 4096, 8) < lib.pk_w4a16_workspace_size(16, 4096, 4096, 8)
+
+
+def test_fast_call_module_shares_the_library():
+    # the CPython fast-call module binds to the library ctypes loaded: an
+    # error it records is the one pk_last_error_string reports
+    from pico_kernels_b200 import _lib
+    f = _lib.fast()
+    assert f.__name__.endswith("_pkfast"), "the fast-call module is built beside the library"
+    st = f.w4a16_gemm(0, _lib.PK_BF16, 256, 0, None, 1.0, 128, 1, 256, 256, 0, _lib.PK_F32, 256,
+                      0, None, 0, 0)
+    assert st == _lib.PK_ERR_SHAPE
+    assert "null pointer" in _lib.last_error()
+    st = f.w4a16_gemm_host(0, _lib.PK_BF16, 256, 0, None, 1.0, 128, 1, 256, 256, 0, _lib.PK_F32,
+                           0, 0, None, 0, 0)
+    assert st != _lib.PK_OK
+    import pytest
+    with pytest.raises(TypeError):
+        f.w4a16_gemm(0, 1)

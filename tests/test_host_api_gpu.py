@@ -1,8 +1,9 @@
 """int4_gemm_host / pk_w4a16_gemm_host: activations and outputs in host memory.
 
 One C-ABI call copies A to the device, runs the same kernels as int4_gemm
-(split_k = 0, so the same routing and split) and copies y back: the result
-must equal the device-tensor call bit for bit, for page-locked and pageable
+(split_k = 0, so the same routing and split) and copies y back (decode
+kernels store it through the page-locked output's mapping): the result must
+equal the device-tensor call bit for bit, for page-locked and pageable
 buffers, row-strided activations (the 2-D copy) and a bf16 output.
 """
 
@@ -68,3 +69,22 @@ def test_device_tensors_are_rejected():
     packed, scales = _weights(256, 256)
     with pytest.raises(pk.DtypeError):
         pk.int4_gemm_host(torch.zeros(1, 256, dtype=torch.bfloat16, device="cuda"), packed, scales)
+
+
+@pytest.mark.parametrize("M", [1, 4, 8])
+def test_cluster_gemv_from_host_buffers(M):
+    """The one-wave cluster GEMV path from page-locked host buffers: row
+    strides, several calls in flight, the result bit-equal to the
+    device-tensor call."""
+    N = K = 4096
+    packed, scales = _weights(N, K, seed=6)
+    gen = torch.Generator().manual_seed(7)
+    bigs = [torch.randn(M, K + 64, generator=gen).to(torch.bfloat16).pin_memory() for _ in range(3)]
+    acts = [b[:, :K] for b in bigs]
+    outs = [torch.empty((M, N)).pin_memory() for _ in range(3)]
+    for a, o in zip(acts, outs):
+        pk.int4_gemm_host(a, packed, scales, out=o)
+    torch.cuda.synchronize()
+    assert pk.device_status() == (0, 0)
+    for a, o in zip(acts, outs):
+        assert torch.equal(o, pk.int4_gemm(a.contiguous().cuda(), packed, scales).cpu())
