@@ -87,7 +87,8 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 1024, 2048), (1, 4096, 4096), (16, 1024, 2048),
+@pytest.mark.parametrize("M,N,K", [(1, 1024, 2048), (1, 4096, 4096), (4, 1024, 2048),
+                                   (8, 3072, 4096), (8, 4096, 4096), (16, 1024, 2048),
                                    (32, 1024, 1024), (64, 1024, 1024), (200, 20480, 512),
                                    (300, 2048, 1024), (512, 1024, 2048)])
 def test_sharded_entry_one_rank(M, N, K):
