@@ -296,8 +296,9 @@ size_t pk_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int split_k) {
     return prefill_workspace_bytes(N, K);
   const void* aligned = reinterpret_cast<const void*>(16);
   size_t bytes = 0;
-  if (split_k == 0 && gemv_preferred(M, N, K) &&
-      gemv_supported(M, N, K, 128, aligned, 8, aligned, aligned))
+  // the GEMV serves the shapes the decode kernel does not take (other group
+  // sizes) whatever its preference: size for both
+  if (split_k == 0 && gemv_supported(M, N, K, 128, aligned, 8, aligned, aligned))
     bytes = gemv_workspace_bytes(M, N, K);
   if (decode_supported(M, N, K, 128, nullptr, 8, aligned)) {
     const int split = split_k > 0 ? split_k : decode_pick_split(M, N, K);
@@ -353,8 +354,8 @@ int pk_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const uint8_t* wp, co
 
   // Other decode shapes where it is faster, with the automatic split: the
   // stream-K CUDA-core GEMV (a weight stream).
-  if (split_k == 0 && gemv_preferred(M, N, K) &&
-      gemv_supported(M, N, K, group_size, scales, lda, a, wp)) {
+  if (split_k == 0 && gemv_supported(M, N, K, group_size, scales, lda, a, wp) &&
+      (gemv_preferred(M, N, K) || !decode_supported(M, N, K, group_size, scales, lda, a))) {
     const size_t need = gemv_workspace_bytes(M, N, K);
     bool have_ws = need == 0;
     if (need > 0 && workspace != nullptr) {
@@ -679,7 +680,8 @@ int sharded_path(int64_t M, int64_t N, int64_t K, int group, bool grouped, int o
   if (gemv_cluster_preferred(M, N, K) &&
       gemv_cluster_supported(M, N, K, group, sc, K, aligned, aligned))
     return kPathCluster;
-  if (gemv_preferred(M, N, K) && gemv_supported(M, N, K, group, sc, K, aligned, aligned))
+  if (gemv_supported(M, N, K, group, sc, K, aligned, aligned) &&
+      (gemv_preferred(M, N, K) || !decode_supported(M, N, K, group, sc, K, aligned)))
     return kPathGemv;
   if (decode_supported(M, N, K, group, sc, K, aligned)) return kPathDecode;
   if (skinny_supported(M, N, K, group, sc, K, aligned) && skinny_preferred(M, N, K))

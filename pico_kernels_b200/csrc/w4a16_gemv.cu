@@ -452,12 +452,21 @@ int64_t gemv_grid(int64_t N, int64_t K) {
 }  // namespace
 
 bool gemv_preferred(int64_t M, int64_t N, int64_t K) {
-  // Measured on B200 against the tcgen05 decode kernel, Llama-70B up_proj
-  // (28672 x 8192): M = 4 43 vs 83 us, M = 8 48 vs 84 us; the tile decode
-  // costs the same instructions per weight for every M up to 8.
-  (void)N;
-  (void)K;
-  return M >= 1 && M <= kMaxM;
+  // Faster than the tcgen05 decode kernel unless a slice's partial sums come
+  // from too many CTAs: the fan-in, CTAs per 1024-column slice (~G / NS),
+  // costs the slice's last arriver one L2 round trip per batch of partials,
+  // and batches shrink as M grows. Measured on B200 (us, stream-K vs decode):
+  // M=1: fan-in 11-37 wins (14336x4096 14.3 vs 28.9, 4096x11008 13.3 vs
+  // 14.7), 48 and 74 lose (3072^2 8.2 vs 6.4, 2048x8192 11.5 vs 10.5); M=2..4:
+  // 14-25 win (6144^2 M=4 12.3 vs 17.2), 37 loses (4096x11008 M=4 21.5 vs
+  // 14.6); M=8: 14 wins (11008x4096 22.5 vs 23.3), 19 loses (8192^2 26.2 vs
+  // 23.8). Llama-70B up_proj (fan-in 6): M=1 32.4 vs 66, M=8 40.1 vs 84.
+  if (M < 1 || M > kMaxM) return false;
+  const int64_t NS = (N + kSliceCols - 1) / kSliceCols;
+  const int64_t G = gemv_grid(N, K);
+  const int64_t fan_in = (G + NS - 1) / NS;
+  const int64_t limit = M == 1 ? 40 : (M <= 4 ? 25 : 14);
+  return fan_in <= limit;
 }
 
 bool gemv_supported(int64_t M, int64_t N, int64_t K, int group, const void* scales, int64_t lda,
