@@ -655,9 +655,11 @@ __device__ __forceinline__ void emit_out(void* out, const OutputShard& x, int ou
 // leader's). The CTA's peer stores are ordered before one system-scope fence
 // by thread 0 through the barrier (the grid-synchronisation pattern), taken
 // only by CTAs that stored; the last of the `arrivals` CTAs adds 1 to each
-// peer's flag (release, system scope) and waits, bounded, until its own flag
-// reaches its next expected count, advanced in device memory so CUDA graph
-// replays stay in step.
+// peer's flag and waits, bounded, until its own flag reaches its next
+// expected count, advanced in device memory so CUDA graph replays stay in
+// step. The additions are one release pattern: a single system-scope fence,
+// then relaxed reductions issued back to back. (A release reduction per peer
+// fences before each one, so every peer cost one more NVLink round trip.)
 template <typename P>
 __device__ __forceinline__ void peer_exchange_finish(const P& p, bool stored, int* status,
                                                      int where, unsigned arrivals) {
@@ -669,9 +671,10 @@ __device__ __forceinline__ void peer_exchange_finish(const P& p, bool stored, in
   asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p.done) : "memory");
   if (prev != total - 1) return;
   *p.done = 0u;  // re-arm; the next call starts after this grid completes
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
   for (int r = 0; r < p.world; ++r) {
     if (r == p.rank) continue;
-    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.peer_flag[r]) : "memory");
+    asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(p.peer_flag[r]) : "memory");
   }
   unsigned* expected = reinterpret_cast<unsigned*>(p.peer_flag[p.rank]) + 1;
   const uint32_t target = *expected + static_cast<uint32_t>(p.world - 1);

@@ -1,6 +1,6 @@
 """N-sharded W4A16 / fp8 layers on GPUs with NCCL (one process per GPU).
 
-With at least two GPUs, two ranks each compute their column slice with the
+With at least two (four, eight) GPUs, as many ranks each compute their column slice with the
 sm_100a kernels and all-gather the output over NVLink (NCCL, or the fused
 peer-store exchange inside the GEMV, decode and skinny kernels); the result
 must equal the unsharded kernel's output (same kernels, same per-column
@@ -126,16 +126,20 @@ def test_single_rank_path():
     assert torch.equal(y, pk.int4_gemm(a, packed, scales))
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_ranks_nccl_all_gather():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ranks_exchange(world):
+    """`world` ranks, one per GPU: the NCCL paths and the fused exchange
+    (every rank's flag barrier adds to world - 1 peers' flags)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=300)
         assert p.exitcode == 0
-    for rank, ok in sorted(q.get(timeout=5) for _ in range(2)):
+    for rank, ok in sorted(q.get(timeout=5) for _ in range(world)):
         assert all(ok), (rank, ok)
