@@ -133,6 +133,27 @@ def fast():
     return f
 
 
+_tfast = None
+
+
+def torch_fast():
+    """The module _pktorch (tensor checks of int4_gemm / int4_gemm_host in
+    C++, over the same library and the same cached workspaces), or None when
+    it was not built; its calls return -1 for what they leave to Python."""
+    global _tfast
+    f = _tfast
+    if f is None:
+        load()  # the library first, by path: the module then binds to it
+        try:
+            from . import _pktorch as mod  # noqa: PLC0415
+            mod.bind(_workspaces)
+            f = mod
+        except ImportError:
+            f = False
+        _tfast = f
+    return f or None
+
+
 def last_error() -> str:
     return load().pk_last_error_string().decode(errors="replace")
 

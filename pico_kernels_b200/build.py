@@ -8,7 +8,9 @@ only when it or a header changed), then everything links into
 IEEE fp32 division for bit-exact parity. Then ``csrc/pyfast.cpp`` compiles
 with the host compiler into the CPython module ``_pkfast`` beside it, the
 fast-call entry points of the hottest calls (ctypes remains the path for
-the rest, and for all calls when Python's headers are missing).
+the rest, and for all calls when Python's headers are missing), and
+``csrc/pytorch_fast.cpp`` against torch's headers into ``_pktorch``, which
+makes the tensor checks of ``int4_gemm`` / ``int4_gemm_host`` in C++.
 """
 
 from __future__ import annotations
@@ -28,6 +30,7 @@ INCLUDE = PKG.parent / "include"
 BUILD = PKG.parent / "_build"
 LIB = PKG / "libpico_b200.so"
 FAST = PKG / ("_pkfast" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
+TFAST = PKG / ("_pktorch" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -81,6 +84,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
         os.replace(tmp, LIB)
     build_fast(force)
+    build_torch_fast(force)
     return LIB
 
 
@@ -103,6 +107,39 @@ def build_fast(force: bool = False) -> Path | None:
         raise RuntimeError(f"host compiler failed on {src.name}:\n{r.stdout}\n{r.stderr}")
     os.replace(tmp, FAST)
     return FAST
+
+
+def build_torch_fast(force: bool = False) -> Path | None:
+    """The CPython module _pktorch (csrc/pytorch_fast.cpp): the tensor checks
+    of int4_gemm / int4_gemm_host in C++ against torch's headers and
+    libraries, linked like _pkfast; None without Python's or torch's headers."""
+    import torch  # noqa: PLC0415
+
+    src = CSRC / "pytorch_fast.cpp"
+    inc = sysconfig.get_paths().get("include")
+    cxx = shutil.which("g++") or shutil.which("c++")
+    tdir = Path(torch.__file__).resolve().parent
+    cuda_inc = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "include"
+    if (not inc or not (Path(inc) / "Python.h").exists() or cxx is None
+            or not (tdir / "include" / "torch").is_dir() or not (cuda_inc / "cuda.h").exists()):
+        return None
+    newest = max(src.stat().st_mtime, LIB.stat().st_mtime, (INCLUDE / "pico_b200.h").stat().st_mtime)
+    if not force and TFAST.exists() and TFAST.stat().st_mtime >= newest:
+        return TFAST
+    tmp = TFAST.with_suffix(".tmp")
+    abi = int(bool(getattr(torch._C, "_GLIBCXX_USE_CXX11_ABI", True)))
+    tlib = tdir / "lib"
+    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           f"-I{inc}", f"-I{INCLUDE}", f"-I{tdir / 'include'}",
+           f"-I{tdir / 'include' / 'torch' / 'csrc' / 'api' / 'include'}", f"-I{cuda_inc}",
+           str(src), "-o", str(tmp), f"-L{PKG}", "-lpico_b200", f"-L{tlib}", "-ltorch_python",
+           "-ltorch", "-ltorch_cpu", "-lc10", "-lc10_cuda", "-Wl,-rpath,$ORIGIN",
+           f"-Wl,-rpath,{tlib}"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"host compiler failed on {src.name}:\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, TFAST)
+    return TFAST
 
 
 def main() -> None:

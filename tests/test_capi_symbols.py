@@ -128,3 +128,24 @@ def test_fast_call_module_shares_the_library():
     import pytest
     with pytest.raises(TypeError):
         f.w4a16_gemm(0, 1)
+
+
+def test_torch_fast_module_leaves_host_tensors_to_python():
+    # _pktorch serves CUDA tensors only: host tensors go back to the Python
+    # path (-1), which raises the documented error
+    import pytest
+    import torch
+
+    import pico_kernels_b200 as pk
+    from pico_kernels_b200 import _lib
+    tf = _lib.torch_fast()
+    assert tf is not None and tf.__name__.endswith("_pktorch")
+    a = torch.zeros(1, 256, dtype=torch.bfloat16)
+    wp = torch.zeros(256, 128, dtype=torch.uint8)
+    out = torch.zeros(1, 256)
+    assert tf.int4_gemm(a, wp, 1.0, None, out, torch.float32, 0) == -1
+    assert tf.int4_gemm_host(a, wp, 1.0, None, out, torch.float32) == -1
+    with pytest.raises(_lib.DtypeError):
+        pk.int4_gemm(a, wp, 1.0, out=out)
+    with pytest.raises(TypeError):
+        tf.int4_gemm(a)
