@@ -5,15 +5,18 @@
 // costs 0.1-0.3 us, together more than the decode GEMM's kernel. These
 // functions make the same checks on the tensors in C++ and call
 // libpico_b200.so directly (linked by its soname, so the library instance is
-// the one ctypes loaded). Each returns the C ABI's status, or -1 when the
-// call is not one it serves (no `out`, inputs that need a copy or a cast,
-// a workspace not yet allocated, anything unexpected): the caller then takes
-// the Python path, which raises the documented errors or allocates. The
+// the one ctypes loaded). Each returns the output tensor, or the C ABI's
+// status when the call failed, or -1 when the call is not one it serves
+// (inputs that need a copy or a cast, a workspace not yet allocated, a host
+// output not given, anything unexpected): the caller then takes the Python
+// path, which raises the documented errors or allocates. Calls run with the
+// GIL held (the shape cache below relies on it). The
 // workspaces are the ones pico_kernels_b200._lib keeps (its dict is bound
 // once with bind()), so reset_workspaces() covers both paths.
 #define PY_SSIZE_T_CLEAN
 #include <Python.h>
 
+#include <ATen/ops/empty.h>
 #include <c10/cuda/CUDAStream.h>
 #include <torch/csrc/Dtype.h>
 #include <torch/csrc/autograd/python_variable.h>
@@ -155,7 +158,8 @@ bool output(PyObject* out_obj, PyObject* dtype_obj, int64_t M, int64_t N, int de
   return true;
 }
 
-// int4_gemm(a, w_packed, scale, group_size, out, out_dtype, split_k) -> status or -1
+// int4_gemm(a, w_packed, scale, group_size, out, out_dtype, split_k)
+//   -> out (allocated here when None), or the status, or -1
 PyObject* int4_gemm(PyObject*, PyObject* const* args, Py_ssize_t n) {
   if (n != 7) {
     PyErr_Format(PyExc_TypeError, "int4_gemm takes 7 arguments (%zd given)", n);
@@ -173,11 +177,18 @@ PyObject* int4_gemm(PyObject*, PyObject* const* args, Py_ssize_t n) {
     Weights w;
     if (!weights(args[1], args[2], args[3], K, a.scalar_type(), device, &w))
       return PyLong_FromLong(kNotServed);
-    void* out;
-    int out_code;
-    int64_t elt;
-    if (!output(args[4], args[5], M, w.N, device, &out, &out_code, &elt))
+    void* out = nullptr;
+    int out_code = 0;
+    int64_t elt = 0;
+    const bool alloc = args[4] == Py_None;
+    if (alloc) {
+      if (!THPDtype_Check(args[5])) return PyLong_FromLong(kNotServed);
+      const at::ScalarType want = reinterpret_cast<THPDtype*>(args[5])->scalar_type;
+      if (want != at::kFloat && want != at::kBFloat16) return PyLong_FromLong(kNotServed);
+      out_code = code_of(want);
+    } else if (!output(args[4], args[5], M, w.N, device, &out, &out_code, &elt)) {
       return PyLong_FromLong(kNotServed);
+    }
     const long split = PyLong_AsLong(args[6]);
     if (split == -1 && PyErr_Occurred()) {
       PyErr_Clear();
@@ -191,18 +202,28 @@ PyObject* int4_gemm(PyObject*, PyObject* const* args, Py_ssize_t n) {
       ws = workspace(device, stream, g_tag_splitk, ws_bytes);
       if (ws == nullptr) return PyLong_FromLong(kNotServed);
     }
+    at::Tensor y;
+    if (alloc) {
+      y = at::empty({M, w.N}, at::TensorOptions()
+                                  .dtype(out_code == PK_F32 ? at::kFloat : at::kBFloat16)
+                                  .device(at::Device(at::kCUDA, static_cast<int8_t>(device))));
+      out = y.data_ptr();
+    }
     const int st = pk_w4a16_gemm(a.data_ptr(), a_code, a.stride(0),
                                  static_cast<const uint8_t*>(w.wp), w.scales, w.scalar, w.group,
                                  M, w.N, K, out, out_code, w.N, static_cast<int>(split), ws,
                                  ws_bytes, reinterpret_cast<void*>(stream));
-    return PyLong_FromLong(st);
+    if (st != PK_OK) return PyLong_FromLong(st);
+    if (alloc) return THPVariable_Wrap(std::move(y));
+    Py_INCREF(args[4]);
+    return args[4];
   } catch (...) {
     PyErr_Clear();
     return PyLong_FromLong(kNotServed);
   }
 }
 
-// int4_gemm_host(a, w_packed, scale, group_size, out, out_dtype) -> status or -1
+// int4_gemm_host(a, w_packed, scale, group_size, out, out_dtype) -> out, or the status, or -1
 // (a and out: host tensors; the staging buffers "stage_a" / "stage_y" and the
 // workspace are the cached ones of the weights' device and current stream)
 PyObject* int4_gemm_host(PyObject*, PyObject* const* args, Py_ssize_t n) {
@@ -245,7 +266,9 @@ PyObject* int4_gemm_host(PyObject*, PyObject* const* args, Py_ssize_t n) {
                                       static_cast<const uint8_t*>(w.wp), w.scales, w.scalar,
                                       w.group, M, w.N, K, out, out_code, a_dev, y_dev, ws,
                                       ws_bytes, reinterpret_cast<void*>(stream));
-    return PyLong_FromLong(st);
+    if (st != PK_OK) return PyLong_FromLong(st);
+    Py_INCREF(args[4]);
+    return args[4];
   } catch (...) {
     PyErr_Clear();
     return PyLong_FromLong(kNotServed);
@@ -267,12 +290,12 @@ PyObject* bind(PyObject*, PyObject* const* args, Py_ssize_t n) {
 PyMethodDef kMethods[] = {
     {"int4_gemm", reinterpret_cast<PyCFunction>(reinterpret_cast<void (*)()>(int4_gemm)),
      METH_FASTCALL,
-     "int4_gemm(a, w_packed, scale, group_size, out, out_dtype, split_k): the C ABI's status, "
-     "or -1 when the Python path must take the call."},
+     "int4_gemm(a, w_packed, scale, group_size, out, out_dtype, split_k): the output tensor, "
+     "the C ABI's status on failure, or -1 when the Python path must take the call."},
     {"int4_gemm_host",
      reinterpret_cast<PyCFunction>(reinterpret_cast<void (*)()>(int4_gemm_host)), METH_FASTCALL,
-     "int4_gemm_host(a, w_packed, scale, group_size, out, out_dtype): the C ABI's status, or -1 "
-     "when the Python path must take the call."},
+     "int4_gemm_host(a, w_packed, scale, group_size, out, out_dtype): out, the C ABI's status "
+     "on failure, or -1 when the Python path must take the call."},
     {"bind", reinterpret_cast<PyCFunction>(reinterpret_cast<void (*)()>(bind)), METH_FASTCALL,
      "bind(workspaces): the workspace dict of pico_kernels_b200._lib."},
     {nullptr, nullptr, 0, nullptr}};

@@ -118,14 +118,13 @@ def int4_gemm(a: torch.Tensor, w_packed: torch.Tensor, scale,
     ``a``'s device; a decode loop reuses it instead of allocating per call).
     """
     del BLOCK_M, BLOCK_N, BLOCK_K
-    if out is not None:  # the same checks and call in C++ (_pktorch), when it serves them
-        tf = _lib.torch_fast()
-        if tf is not None:
-            st = tf.int4_gemm(a, w_packed, scale, group_size, out, out_dtype, split_k)
-            if st == 0:
-                return out
-            if st > 0:
-                _lib.check(st, "int4_gemm")
+    tf = _lib.torch_fast()  # the same checks and call in C++, when it serves them
+    if tf is not None:
+        res = tf.int4_gemm(a, w_packed, scale, group_size, out, out_dtype, split_k)
+        if type(res) is not int:
+            return res
+        if res > 0:
+            _lib.check(res, "int4_gemm")
     _lib.require_cuda(a, w_packed)
     if a.dtype not in (torch.float16, torch.bfloat16):
         raise _lib.DtypeError(f"a must be fp16 or bf16 (got {a.dtype})")
@@ -202,14 +201,14 @@ def int4_gemm_host(a: torch.Tensor, w_packed: torch.Tensor, scale, *,
     current stream of the weights' device: synchronise it before reading
     ``out``. Page-locked ``a`` and ``out`` make the copies asynchronous.
     """
-    if out is not None:  # the same checks and call in C++ (_pktorch), when it serves them
+    if out is not None:  # the same checks and call in C++, when it serves them
         tf = _lib.torch_fast()
         if tf is not None:
-            st = tf.int4_gemm_host(a, w_packed, scale, group_size, out, out_dtype)
-            if st == 0:
-                return out
-            if st > 0:
-                _lib.check(st, "int4_gemm_host")
+            res = tf.int4_gemm_host(a, w_packed, scale, group_size, out, out_dtype)
+            if type(res) is not int:
+                return res
+            if res > 0:
+                _lib.check(res, "int4_gemm_host")
     if a.is_cuda or (out is not None and out.is_cuda):
         raise _lib.DtypeError("int4_gemm_host takes host tensors for a and out")
     _lib.require_cuda(w_packed)

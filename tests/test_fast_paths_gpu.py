@@ -1,10 +1,11 @@
 """The C++ tensor-check path of int4_gemm / int4_gemm_host (module _pktorch).
 
-With `out` given, the wrappers hand the call to _pktorch, which checks the
-tensors in C++ and calls the same C ABI; what it does not serve it returns
-to the Python path. Results must equal the Python path's bit for bit (same
-kernel routing, same workspaces), the C++ path must actually serve the
-common calls, and misuse must raise the Python path's errors.
+The wrappers hand each call to _pktorch first, which checks the tensors in
+C++, allocates a device output when none is given, and calls the same C ABI;
+what it does not serve it returns to the Python path (-1). Results must
+equal the Python path's bit for bit (same kernel routing, same workspaces),
+the C++ path must actually serve the common calls, and misuse must raise the
+Python path's errors.
 """
 
 import pytest
@@ -48,13 +49,18 @@ def test_device_call_equals_python_path(M, N, K, dtype, out_dtype):
                                             out=torch.empty(M, N, device="cuda",
                                                             dtype=out_dtype)))
     out = torch.full((M, N), float("nan"), device="cuda", dtype=out_dtype)
-    st = _lib.torch_fast().int4_gemm(a, packed, scales, None, out, out_dtype, 0)
-    assert st == 0, "the C++ path serves a call whose workspace exists"
+    res = _lib.torch_fast().int4_gemm(a, packed, scales, None, out, out_dtype, 0)
+    assert res is out, "the C++ path serves a call whose workspace exists"
     torch.cuda.synchronize()
     assert pk.device_status() == (0, 0)
     assert torch.equal(out, ref)
     y = pk.int4_gemm(a, packed, scales, out_dtype=out_dtype, out=out)
     assert y is out and torch.equal(y, ref)
+    # no out: allocated by the C++ path on a's device
+    y = _lib.torch_fast().int4_gemm(a, packed, scales, None, None, out_dtype, 0)
+    assert isinstance(y, torch.Tensor) and y.dtype == out_dtype and y.device == a.device
+    assert y.shape == (M, N) and torch.equal(y, ref)
+    assert torch.equal(pk.int4_gemm(a, packed, scales, out_dtype=out_dtype), ref)
 
 
 def test_scalar_scale_and_split_k():
@@ -66,7 +72,7 @@ def test_scalar_scale_and_split_k():
         ref = _python_path(lambda: pk.int4_gemm(a, q, 0.03, split_k=split,
                                                 out=torch.empty(M, N, device="cuda")))
         out = torch.empty(M, N, device="cuda")
-        assert _lib.torch_fast().int4_gemm(a, q, 0.03, None, out, torch.float32, split) == 0
+        assert _lib.torch_fast().int4_gemm(a, q, 0.03, None, out, torch.float32, split) is out
         torch.cuda.synchronize()
         assert torch.equal(out, ref)
 
@@ -102,8 +108,8 @@ def test_host_call_equals_python_path(M, N, K):
                                                  out=torch.empty(M, N).pin_memory()))
     torch.cuda.synchronize()
     out = torch.full((M, N), float("nan")).pin_memory()
-    st = _lib.torch_fast().int4_gemm_host(a, packed, scales, None, out, torch.float32)
-    assert st == 0, "the C++ path serves a call whose staging buffers exist"
+    res = _lib.torch_fast().int4_gemm_host(a, packed, scales, None, out, torch.float32)
+    assert res is out, "the C++ path serves a call whose staging buffers exist"
     torch.cuda.synchronize()
     assert pk.device_status() == (0, 0)
     assert torch.equal(out, ref)
