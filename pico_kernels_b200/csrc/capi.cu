@@ -569,7 +569,9 @@ int pk_w4a16_gemm_host(const void* a_host, int a_dtype, int64_t lda, const uint8
   }
   // (Reading A through its mapping inside the GEMM instead was measured
   // slower: every CTA of the grid then reads its rows across the host link,
-  // 17.1 vs 12.5 us per call at M = 1 4096^2; the copy kernel reads them once.)
+  // 32 times the bytes at M = 1 4096^2 for the cluster GEMV; 13.9 vs 12.8 us
+  // per call back to back on one box, although it saves a launch; the copy
+  // kernel reads them once.)
   const size_t row = static_cast<size_t>(K) * 2;
   cudaError_t e;
   if (a_map != nullptr)
